@@ -1,0 +1,157 @@
+// TEST INFRASTRUCTURE ONLY -- C entry points of the CPU oracle (see zeno_oracle.h).
+// reset_to_state / set_gravity / set_timestep follow src/main.zig:290-385, 633-663.
+#include <cstring>
+#include <string>
+
+#include "oracle_model.h"
+#include "zeno_oracle.h"
+
+using namespace zo;
+
+extern "C" {
+
+void* zo_create(const char* xml, const ZoConfig* c) {
+  if (!xml || !c) return nullptr;
+  Scene sc;
+  if (!parse_mjcf(std::string(xml), &sc)) return nullptr;
+  Config cfg;
+  cfg.num_envs = c->num_envs;
+  cfg.timestep = c->timestep;
+  cfg.contact_iterations = c->contact_iterations;
+  cfg.max_contacts_per_env = c->max_contacts_per_env;
+  cfg.seed = c->seed;
+  cfg.substeps = c->substeps;
+  cfg.enable_profiling = c->enable_profiling;
+  World* w = new World();
+  if (!world_init(w, sc, cfg)) {
+    delete w;
+    return nullptr;
+  }
+  return w;
+}
+
+void zo_destroy(void* h) { delete static_cast<World*>(h); }
+
+int zo_step(void* h, const float* actions, uint32_t substeps) {
+  if (!h) return -1;
+  world_step(static_cast<World*>(h), actions, substeps);
+  return 0;
+}
+
+int zo_run(void* h, const float* actions, uint32_t nsteps, uint32_t substeps) {
+  if (!h) return -1;
+  World* w = static_cast<World*>(h);
+  for (uint32_t s = 0; s < nsteps; s++) world_step(w, actions + size_t(s) * w->E * w->A, substeps);
+  return 0;
+}
+
+int zo_step_subset(void* h, const float* actions, const uint8_t* mask, uint32_t substeps) {
+  if (!h) return -1;
+  return world_step_subset(static_cast<World*>(h), actions, mask, substeps);
+}
+
+int zo_reset(void* h, const uint8_t* mask) {
+  if (!h) return -1;
+  world_reset(static_cast<World*>(h), mask);
+  return 0;
+}
+
+int zo_reset_to_state(void* h, const float* pos, const float* quat, const float* vel, const float* angvel,
+                      const uint8_t* mask) {
+  if (!h) return -1;
+  World* w = static_cast<World*>(h);
+  const size_t per = size_t(w->B) * 4;
+  auto copy_in = [&](std::vector<float>& dst, const float* src) {
+    for (uint32_t e = 0; e < w->E; e++) {
+      if (mask && !mask[e]) continue;
+      std::memcpy(&dst[e * per], &src[e * per], per * sizeof(float));
+    }
+  };
+  copy_in(w->pos, pos);
+  copy_in(w->quat, quat);
+  if (vel) copy_in(w->vel, vel);
+  if (angvel) copy_in(w->angvel, angvel);
+  std::fill(w->counts.begin(), w->counts.end(), 0u);
+  return 0;
+}
+
+int zo_set_gravity(void* h, float gx, float gy, float gz) {
+  if (!h) return -1;
+  World* w = static_cast<World*>(h);
+  w->params.gravity[0] = gx;
+  w->params.gravity[1] = gy;
+  w->params.gravity[2] = gz;
+  return 0;
+}
+
+int zo_set_timestep(void* h, float ts) {
+  if (!h) return -1;
+  if (ts <= 0) return -6;
+  World* w = static_cast<World*>(h);
+  w->timestep = ts;
+  uint32_t s = w->cfg.substeps > 1 ? w->cfg.substeps : 1;
+  w->params.dt = ts / float(s);
+  return 0;
+}
+
+int zo_set_task(void* h, const ZoTask* t) {
+  if (!h || !t) return -1;
+  World* w = static_cast<World*>(h);
+  if (t->enabled && t->body >= w->B) return -6;
+  w->task.enabled = t->enabled != 0;
+  w->task.body = t->body;
+  w->task.auto_reset = t->auto_reset != 0;
+  w->task.z_min = t->z_min;
+  w->task.z_max = t->z_max;
+  w->task.noise = t->noise;
+  w->task.forward_weight = t->forward_weight;
+  w->task.alive_bonus = t->alive_bonus;
+  w->task.ctrl_cost = t->ctrl_cost;
+  w->task.seed = t->seed;
+  w->task_env_offset = t->env_offset;
+  return 0;
+}
+
+void zo_dims(void* h, uint32_t out[10]) {
+  World* w = static_cast<World*>(h);
+  uint32_t d[10] = {w->E, w->B, w->J, w->A, w->G, w->S, w->M, w->K, w->obs, w->num_colors};
+  std::memcpy(out, d, sizeof(d));
+}
+
+void* zo_buffer(void* h, const char* name, size_t* nbytes) {
+  World* w = static_cast<World*>(h);
+  std::string n(name);
+  auto ret = [&](auto& v) -> void* {
+    *nbytes = v.size() * sizeof(v[0]);
+    return v.empty() ? nullptr : (void*)v.data();
+  };
+  if (n == "positions") return ret(w->pos);
+  if (n == "quaternions") return ret(w->quat);
+  if (n == "velocities") return ret(w->vel);
+  if (n == "angular_velocities") return ret(w->angvel);
+  if (n == "accelerations") return ret(w->acc);
+  if (n == "joint_positions") return ret(w->jpos);
+  if (n == "joint_velocities") return ret(w->jvel);
+  if (n == "joint_torques") return ret(w->jtorque);
+  if (n == "observations") return ret(w->obs_buf);
+  if (n == "rewards") return ret(w->rewards);
+  if (n == "dones") return ret(w->dones);
+  if (n == "contacts") return ret(w->contacts);
+  if (n == "contact_counts") return ret(w->counts);
+  if (n == "prev_contacts") return ret(w->prev_contacts);
+  if (n == "prev_contact_counts") return ret(w->prev_counts);
+  if (n == "actions") return ret(w->actions);
+  if (n == "bodies") return ret(w->bodies);
+  if (n == "joints") return ret(w->joints);
+  if (n == "geoms") return ret(w->geoms);
+  if (n == "actuators") return ret(w->actuators);
+  if (n == "sensors") return ret(w->sensors);
+  if (n == "constraints") return ret(w->constraints);
+  if (n == "constraint_template") return ret(w->templ);
+  if (n == "color_ranges") return ret(w->color_ranges);
+  if (n == "inv_mass_inertia") return ret(w->inv_mi);
+  *nbytes = 0;
+  return nullptr;
+}
+
+}  // extern "C"
