@@ -1,0 +1,79 @@
+"""Build libzeno.so in-tree (zeno_b200/lib/libzeno.so) with nvcc for sm_100a.
+
+The kernel is compiled with -fmad=false and IEEE division / square root so that every
+floating-point operation is the one written in the source (explicit __fmaf_rn calls
+are the only fused operations); host model-building code is compiled with
+-ffp-contract=off for the same reason.
+
+Usage: python -m zeno_b200.build [--force]
+"""
+from __future__ import annotations
+
+import os
+import shutil
+import subprocess
+import sys
+from pathlib import Path
+
+PKG = Path(__file__).resolve().parent
+CSRC = PKG / "csrc"
+INCLUDE = PKG.parent / "include"
+OUT_DIR = PKG / "lib"
+LIB = OUT_DIR / "libzeno.so"
+OBJ_DIR = PKG / "_build"
+
+CUDA_HOME = Path(os.environ.get("CUDA_HOME", "/usr/local/cuda"))
+NVCC = str(CUDA_HOME / "bin" / "nvcc") if (CUDA_HOME / "bin" / "nvcc").exists() else "nvcc"
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+NVCC_FLAGS = ARCH + ["-lineinfo", "-O3", "-std=c++17", "-fmad=false", "-prec-div=true", "-prec-sqrt=true",
+                     "-ftz=false", "-Xcompiler", "-fPIC", "-Xptxas", "-warn-spills"]
+CXX_FLAGS = ["-O2", "-std=c++17", "-fPIC", "-ffp-contract=off", "-fno-fast-math", "-Wall",
+             f"-I{CUDA_HOME / 'include'}", f"-I{INCLUDE}"]
+CU_SOURCES = ["step_kernel.cu"]
+CXX_SOURCES = ["mjcf.cpp", "model.cpp", "world.cpp", "capi.cpp"]
+HEADERS = ["zeno_types.h", "devmath.cuh", "step_kernel.h", "scene.h", "model.h", "world.h"]
+
+
+def _newer(target: Path, deps) -> bool:
+    if not target.exists():
+        return False
+    t = target.stat().st_mtime
+    return all(Path(d).stat().st_mtime <= t for d in deps)
+
+
+def build(force: bool = False, verbose: bool = False) -> Path:
+    """Compile every CUDA/C++ source and link libzeno.so; returns the library path."""
+    deps = [CSRC / s for s in CU_SOURCES + CXX_SOURCES + HEADERS] + [INCLUDE / "zeno.h", Path(__file__)]
+    if not force and _newer(LIB, deps):
+        return LIB
+    OBJ_DIR.mkdir(exist_ok=True)
+    OUT_DIR.mkdir(exist_ok=True)
+    objs = []
+    cxx = shutil.which("g++") or "g++"
+
+    def run(cmd):
+        if verbose:
+            print(" ".join(cmd), flush=True)
+        r = subprocess.run(cmd, capture_output=True, text=True)
+        if r.returncode != 0:
+            raise RuntimeError(f"build failed: {' '.join(cmd)}\n{r.stdout}\n{r.stderr}")
+        if verbose and (r.stdout or r.stderr):
+            print(r.stdout, r.stderr)
+
+    for src in CU_SOURCES:
+        obj = OBJ_DIR / (src + ".o")
+        run([NVCC, *NVCC_FLAGS, f"-I{INCLUDE}", "-c", str(CSRC / src), "-o", str(obj)])
+        objs.append(str(obj))
+    for src in CXX_SOURCES:
+        obj = OBJ_DIR / (src + ".o")
+        run([cxx, *CXX_FLAGS, "-c", str(CSRC / src), "-o", str(obj)])
+        objs.append(str(obj))
+    tmp = LIB.with_suffix(".so.tmp")
+    run([NVCC, *ARCH, "-shared", "-o", str(tmp), *objs, "-Xlinker", "--no-undefined"])
+    os.replace(tmp, LIB)
+    return LIB
+
+
+if __name__ == "__main__":
+    p = build(force="--force" in sys.argv, verbose=True)
+    print(p)

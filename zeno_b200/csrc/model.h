@@ -1,0 +1,37 @@
+// Model building: Scene -> the read-only tables the step kernel uses, plus the
+// reference-layout records (BodyDataGPU, JointDataGPU, GeomGPU, ActuatorDataGPU,
+// SensorGPU, XPBDConstraint) exported for parity checks of the model itself.
+#pragma once
+#include <cstdint>
+#include <string>
+#include <vector>
+
+#include "scene.h"
+#include "zeno_types.h"
+
+namespace zb {
+
+struct HostModel {
+  uint32_t B = 0, J = 0, A = 0, G = 0, S = 0, K = 0, obs_dim = 0, num_colors = 0;
+  std::vector<DBody> bodies;
+  std::vector<uint32_t> jf_list;
+  std::vector<DJoint> joints;
+  std::vector<DGeom> geoms;
+  std::vector<DPair> pairs;
+  std::vector<DActuator> actuators;
+  std::vector<DSensor> sensors;
+  std::vector<DConstraint> constraints;  // colour-sorted
+  std::vector<uint32_t> color_ranges;    // (start, count) per colour
+  std::vector<uint32_t> subtree;
+  std::vector<float> init_state;         // B*4 pos, B*4 quat, B*4 vel, B*4 angvel, J jpos, J jvel
+  bool actuators_unique = true;
+  // reference-layout records (byte blobs) for model parity checks
+  std::vector<uint8_t> ref_bodies, ref_joints, ref_geoms, ref_actuators, ref_sensors, ref_constraints;
+};
+
+// Builds every table.  Fails (returns false, fills *err) for models the kernel cannot
+// hold: more than 255 bodies or geoms per environment (contact slots pack the body and
+// geom indices into one byte each).
+bool build_model(const Scene& sc, HostModel* m, std::string* err);
+
+}  // namespace zb

@@ -1,0 +1,985 @@
+// Fused batched physics step for sm_100a.
+//
+// One launch runs every substep of one World.step (src/world/world.zig:694-792) for all
+// environments.  The reference encodes 16 + iterations*(colours+1) separate Metal
+// dispatches per substep (world.zig:934-1293); here each environment is owned by a
+// group of L lanes inside one warp, its bodies and contact slots live in shared memory
+// for the whole step, and the stages are separated by __syncwarp on the group mask.
+// HBM is read once at the start and written once at the end of the step.
+//
+// Order of work inside a substep (reference kernel in brackets, all_shaders.metal):
+//   prev-contact snapshot            [cache_contacts 1454-1478, from the previous substep]
+//   actions -> joint torques         [apply_actions 196-229]
+//   gravity force/torque, kinematic  [compute_forces 345-388, update_kinematic 304-339]
+//   joint torques -> body wrenches   [apply_joint_forces 122-190; ordered per-body sums]
+//   save prev pose, integrate        [save_prev_state 1900-1913, integrate 394-462]
+//   broad phase                      [broad_phase 468-533; ballot compaction in order]
+//   stable sort of new slots         [sort_contacts 711-745; rank sort on append only]
+//   narrow phase                     [narrow_phase 751-894]
+//   warm start from prev contacts    [match_cached_contacts 1483-1544; key-run search]
+//   XPBD joints, colour by colour    [solve_joints 909-1399, world.zig:1163-1195]
+//   contacts in slot order           [solve_contacts 1644-1793; level schedule]
+//   velocities from positions        [xpbd_update_velocities 1922-1961]
+//   joint state + sensors (last substep only: both are overwritten every substep)
+//                                    [update_joint_states 1550-1638, read_sensors 1799-1893]
+// then accelerations (world.zig:736-746) and the optional episode task extension.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+
+#include "devmath.cuh"
+#include "step_kernel.h"
+#include "zeno_types.h"
+
+namespace zb {
+
+// ------------------------------------------------------------------------------------
+// Shared-memory plan for one environment (bytes, 16-byte aligned sections)
+// ------------------------------------------------------------------------------------
+__host__ __device__ inline uint32_t align16(uint32_t x) { return (x + 15u) & ~15u; }
+
+struct Plan {
+  uint32_t pos, quat, vel, ang, ppos, pquat, frc, trq;  // float4[B]
+  uint32_t jt, jp, jv;                                  // float[J]
+  uint32_t cpp, cnf, cim;                               // float4[M] current slots (by storage index)
+  uint32_t cpk;                                         // u32[M] packed body/geom indices
+  uint32_t ppp, pim, ppk;                               // prev snapshot (slot order)
+  uint32_t ord, sched, sidx, slev;                      // u16[M] each
+  uint32_t lvl, lcur;                                   // u16[M+1] each
+  uint32_t blev;                                        // u16[B]
+  uint32_t flags;                                       // u32
+  uint32_t bytes;
+};
+
+__host__ __device__ inline Plan make_plan(uint32_t B, uint32_t J, uint32_t M) {
+  Plan p;
+  uint32_t o = 0;
+  const uint32_t b4 = align16(16u * B), j1 = align16(4u * (J > 0 ? J : 1)), m4 = align16(16u * M);
+  const uint32_t m1 = align16(4u * M), h1 = align16(2u * M), h2 = align16(2u * (M + 1)), bb = align16(2u * B);
+  p.pos = o; o += b4;
+  p.quat = o; o += b4;
+  p.vel = o; o += b4;
+  p.ang = o; o += b4;
+  p.ppos = o; o += b4;
+  p.pquat = o; o += b4;
+  p.frc = o; o += b4;
+  p.trq = o; o += b4;
+  p.jt = o; o += j1;
+  p.jp = o; o += j1;
+  p.jv = o; o += j1;
+  p.cpp = o; o += m4;
+  p.cnf = o; o += m4;
+  p.cim = o; o += m4;
+  p.cpk = o; o += m1;
+  p.ppp = o; o += m4;
+  p.pim = o; o += m4;
+  p.ppk = o; o += m1;
+  p.ord = o; o += h1;
+  p.sched = o; o += h1;
+  p.sidx = o; o += h1;
+  p.slev = o; o += h1;
+  p.lvl = o; o += h2;
+  p.lcur = o; o += h2;
+  p.blev = o; o += bb;
+  p.flags = o; o += 16;
+  p.bytes = o;
+  return p;
+}
+
+uint32_t env_smem_bytes(uint32_t B, uint32_t J, uint32_t M) { return make_plan(B, J, M).bytes; }
+
+__device__ __forceinline__ uint32_t pack4(uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  return a | (b << 8) | (c << 16) | (d << 24);
+}
+// Slot indices read back from HBM are trusted only within the model's bounds (the
+// contacts buffer is host-writable through the ABI); out-of-range values become 0.
+__device__ __forceinline__ uint32_t pack_checked(uint4 ix, uint32_t B, uint32_t G) {
+  return pack4(ix.x < B ? ix.x : 0u, ix.y < B ? ix.y : 0u, ix.z < G ? ix.z : 0u, ix.w < G ? ix.w : 0u);
+}
+__device__ __forceinline__ uint32_t pk_a(uint32_t k) { return k & 0xFFu; }
+__device__ __forceinline__ uint32_t pk_b(uint32_t k) { return (k >> 8) & 0xFFu; }
+__device__ __forceinline__ uint32_t pk_ga(uint32_t k) { return (k >> 16) & 0xFFu; }
+__device__ __forceinline__ uint32_t pk_gb(uint32_t k) { return k >> 24; }
+// sort_contacts key: min(body) << 16 | max(body)
+__device__ __forceinline__ uint32_t pk_key(uint32_t k) {
+  uint32_t a = pk_a(k), b = pk_b(k);
+  return ((a < b ? a : b) << 16) | (a < b ? b : a);
+}
+
+template <class T>
+__device__ __forceinline__ T* sm(unsigned char* base, uint32_t off) {
+  return reinterpret_cast<T*>(base + off);
+}
+
+// ------------------------------------------------------------------------------------
+// XPBD joint constraint (solve_joints, all_shaders.metal:909-1399).  The multiplier is
+// not tracked: with compliance 0, alpha~ = 0 and dlambda = -C / w exactly.
+// ------------------------------------------------------------------------------------
+__device__ __forceinline__ void solve_constraint(const DConstraint& c, const DBody* bodies, float4* pos,
+                                                 float4* quat) {
+  const uint32_t type = c.type & 0xFFu;
+  if (type > 10) return;
+  const uint32_t ia = c.body_a, ib = c.body_b;
+  const float4 mia = __ldg(reinterpret_cast<const float4*>(bodies[ia].inv_mass_inertia));
+  const float4 mib = __ldg(reinterpret_cast<const float4*>(bodies[ib].inv_mass_inertia));
+  const V3 Ia{mia.y, mia.z, mia.w}, Ib{mib.y, mib.z, mib.w};
+  const float ima = mia.x, imb = mib.x;
+  if (ima + imb < 1e-8f) return;
+  const V3 pa = v3(pos[ia]), pb = v3(pos[ib]);
+  const float4 qa = quat[ia], qb = quat[ib];
+  const V3 aa = v3(c.anchor_a[0], c.anchor_a[1], c.anchor_a[2]);
+  const V3 ab = v3(c.anchor_b[0], c.anchor_b[1], c.anchor_b[2]);
+
+  if (type == 2) {  // positional
+    const V3 ra = rotate(aa, qa), rb = rotate(ab, qb);
+    const V3 diff = (pa + ra) - (pb + rb);
+    const float C = len(diff);
+    if (C > 1e-6f) {
+      const V3 n = diff * __frcp_rn(C);
+      const V3 rna = cross(ra, n), rnb = cross(rb, n);
+      const float wa = ima + dot(hadamard(rna, Ia), rna);
+      const float wb = imb + dot(hadamard(rnb, Ib), rnb);
+      const float dl = __fdiv_rn(-C, wa + wb);
+      const V3 imp = n * dl;
+      const float4 ca = __ldg(reinterpret_cast<const float4*>(bodies[ia].com));
+      const float4 cb = __ldg(reinterpret_cast<const float4*>(bodies[ib].com));
+      const V3 rca = ra - rotate(v3(ca), qa), rcb = rb - rotate(v3(cb), qb);
+      if (ima > 0.0f) {
+        pos[ia] = with_w(madd(imp, ima, pa), pos[ia].w);
+        quat[ia] = qnormalize(qmadd(qmul_v(hadamard(cross(rca, imp), Ia), qa), 0.5f, qa));
+      }
+      if (imb > 0.0f) {
+        pos[ib] = with_w(msub(imp, imb, pb), pos[ib].w);
+        quat[ib] = qnormalize(qmsub(qmul_v(hadamard(cross(rcb, imp), Ib), qb), 0.5f, qb));
+      }
+    }
+  } else if (type == 7) {  // weld: corrections on body b only
+    const V3 ra = rotate(aa, qa), rb = rotate(ab, qb);
+    const V3 diff = (pa + ra) - (pb + rb);
+    const float C = len(diff);
+    if (C > 1e-6f) {
+      const V3 n = diff * __frcp_rn(C);
+      const V3 rnb = cross(rb, n);
+      const float wb = imb + dot(hadamard(rnb, Ib), rnb);
+      if (wb > 1e-8f) {
+        const V3 imp = n * __fdiv_rn(-C, wb);
+        pos[ib] = with_w(msub(imp, imb, pb), pos[ib].w);
+        quat[ib] = qnormalize(qmsub(qmul_v(hadamard(cross(rb, imp), Ib), qb), 0.5f, qb));
+      }
+    }
+    const float4 qau = quat[ia], qbu = quat[ib];
+    const float4 tgt = make_float4(c.axis_target[0], c.axis_target[1], c.axis_target[2], c.axis_target[3]);
+    float4 qerr = qmul(qmul(qconj(qau), qbu), qconj(tgt));
+    if (qerr.w < 0.0f) qerr = qneg(qerr);
+    const V3 ev = xyz(qerr);
+    const float sh = len(ev);
+    if (sh > 1e-6f) {
+      const V3 axr = ev * __frcp_rn(sh);
+      const float ang = 2.0f * atan2r(sh, qerr.w);
+      const V3 aw = rotate(axr, qau);
+      const float wb = dot(hadamard(aw, Ib), aw);
+      if (wb > 1e-8f) {
+        const V3 ai = aw * __fdiv_rn(ang, wb);
+        if (imb > 0.0f) quat[ib] = qnormalize(qmsub(qmul_v(hadamard(ai, Ib), qbu), 0.5f, qbu));
+      }
+    }
+  } else if (type == 3) {  // angular: keep hinge axes parallel
+    const V3 aaw = rotate(aa, qa), abw = rotate(ab, qb);
+    const V3 cr = cross(aaw, abw);
+    const float sa = len(cr);
+    if (sa > 1e-6f) {
+      const V3 n = cr * __frcp_rn(sa);
+      const float angC = asinr(clampf(sa, -1.0f, 1.0f));
+      const float w = dot(hadamard(n, Ia), n) + dot(hadamard(n, Ib), n);
+      if (w > 1e-8f) {
+        const float dl = __fdiv_rn(-angC, w);
+        if (ima > 0.0f) quat[ia] = qnormalize(qmadd(qmul_v(hadamard(n * dl, Ia), qa), 0.5f, qa));
+        if (imb > 0.0f) quat[ib] = qnormalize(qmadd(qmul_v(hadamard(n * (-dl), Ib), qb), 0.5f, qb));
+      }
+    }
+  } else if (type == 4) {  // angular limit
+    const float lo = c.limits[0], hi = c.limits[1];
+    const float4 qrel = qmul(qconj(qa), qb);
+    const float angle = 2.0f * atan2r(dot(xyz(qrel), aa), qrel.w);
+    float viol = 0.0f;
+    if (angle < lo) viol = lo - angle;
+    else if (angle > hi) viol = hi - angle;
+    if (fabsf(viol) > 1e-6f) {
+      const V3 aw = rotate(aa, qa);
+      const float w = dot(hadamard(aw, Ia), aw) + dot(hadamard(aw, Ib), aw);
+      if (w > 1e-8f) {
+        const V3 ai = aw * __fdiv_rn(viol, w);
+        if (ima > 0.0f) quat[ia] = qnormalize(qmadd(qmul_v(hadamard(ai, Ia), qa), 0.5f, qa));
+        if (imb > 0.0f) quat[ib] = qnormalize(qmsub(qmul_v(hadamard(ai, Ib), qb), 0.5f, qb));
+      }
+    }
+  } else if (type == 5) {  // linear limit
+    const float lo = c.limits[0], hi = c.limits[1];
+    const V3 ra = rotate(v3(0.0f, 0.0f, 0.0f), qa), rb = rotate(ab, qb);
+    const V3 aw = rotate(aa, qa);
+    const float dist = dot((pb + rb) - (pa + ra), aw);
+    float viol = 0.0f;
+    if (dist < lo) viol = lo - dist;
+    else if (dist > hi) viol = hi - dist;
+    if (fabsf(viol) > 1e-6f) {
+      const V3 n = viol > 0.0f ? aw : -aw;
+      const V3 rna = cross(ra, n), rnb = cross(rb, n);
+      const float wa = ima + dot(hadamard(rna, Ia), rna);
+      const float wb = imb + dot(hadamard(rnb, Ib), rnb);
+      const float w = wa + wb;
+      if (w > 1e-8f) {
+        const V3 imp = n * __fdiv_rn(fabsf(viol), w);
+        if (ima > 0.0f) pos[ia] = with_w(msub(imp, ima, pa), pos[ia].w);
+        if (imb > 0.0f) pos[ib] = with_w(madd(imp, imb, pb), pos[ib].w);
+      }
+    }
+  } else if (type == 10) {  // slider: perpendicular lock + relative-orientation weld
+    const V3 ra = rotate(aa, qa), rb = rotate(ab, qb);
+    const V3 diff = (pa + ra) - (pb + rb);
+    const V3 aw = rotate(v3(c.axis_target[0], c.axis_target[1], c.axis_target[2]), qa);
+    const V3 perp = msub(aw, dot(diff, aw), diff);
+    const float pl = len(perp);
+    if (pl > 1e-6f) {
+      const V3 n = perp * __frcp_rn(pl);
+      const V3 rna = cross(ra, n), rnb = cross(rb, n);
+      const float wa = ima + dot(hadamard(rna, Ia), rna);
+      const float wb = imb + dot(hadamard(rnb, Ib), rnb);
+      const V3 imp = n * __fdiv_rn(-pl, wa + wb);
+      if (ima > 0.0f) {
+        pos[ia] = with_w(madd(imp, ima, pa), pos[ia].w);
+        quat[ia] = qnormalize(qmadd(qmul_v(hadamard(cross(ra, imp), Ia), qa), 0.5f, qa));
+      }
+      if (imb > 0.0f) {
+        pos[ib] = with_w(msub(imp, imb, pb), pos[ib].w);
+        quat[ib] = qnormalize(qmsub(qmul_v(hadamard(cross(rb, imp), Ib), qb), 0.5f, qb));
+      }
+    }
+    const float4 qau = quat[ia], qbu = quat[ib];
+    const float4 tgt = make_float4(c.limits[0], c.limits[1], c.limits[2], c.limits[3]);
+    float4 qerr = qmul(qmul(qconj(qau), qbu), qconj(tgt));
+    if (qerr.w < 0.0f) qerr = qneg(qerr);
+    const V3 ev = xyz(qerr);
+    const float sh = len(ev);
+    if (sh > 1e-6f) {
+      const V3 axe = ev * __frcp_rn(sh);
+      const float ae = 2.0f * atan2r(sh, qerr.w);
+      const V3 aw2 = rotate(axe, qau);
+      const float w = dot(hadamard(aw2, Ia), aw2) + dot(hadamard(aw2, Ib), aw2);
+      if (w > 1e-8f) {
+        const V3 ai = aw2 * __fdiv_rn(ae, w);
+        if (ima > 0.0f) quat[ia] = qnormalize(qmadd(qmul_v(hadamard(ai, Ia), qau), 0.5f, qau));
+        if (imb > 0.0f) quat[ib] = qnormalize(qmsub(qmul_v(hadamard(ai, Ib), qbu), 0.5f, qbu));
+      }
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------------
+// Contact solve for one slot (solve_contacts, all_shaders.metal:1644-1793)
+// ------------------------------------------------------------------------------------
+__device__ __forceinline__ void solve_contact(float4& cpp, float4& cnf, float4& cim, uint32_t pk,
+                                              const DBody* bodies, float4* pos, float4* vel, float4* ang,
+                                              float dt, float baumgarte, float slop) {
+  const uint32_t ia = pk_a(pk), ib = pk_b(pk);
+  const float4 mia = __ldg(reinterpret_cast<const float4*>(bodies[ia].inv_mass_inertia));
+  const float4 mib = __ldg(reinterpret_cast<const float4*>(bodies[ib].inv_mass_inertia));
+  const V3 Ia{mia.y, mia.z, mia.w}, Ib{mib.y, mib.z, mib.w};
+  const float ima = mia.x, imb = mib.x;
+  const float isum = ima + imb;
+  if (isum < 1e-8f) return;
+  const V3 n = xyz(cnf);
+  const float pen = cpp.w, fr = cnf.w;
+  const V3 cp = xyz(cpp);
+  const V3 ra = cp - v3(pos[ia]), rb = cp - v3(pos[ib]);
+  const V3 va = v3(vel[ia]) + cross(v3(ang[ia]), ra);
+  const V3 vb = v3(vel[ib]) + cross(v3(ang[ib]), rb);
+  const V3 rv = va - vb;
+  const float vn = dot(rv, n);
+  const V3 vt = msub(n, vn, rv);
+  const float ts = len(vt);
+  const V3 rna = cross(ra, n), rnb = cross(rb, n);
+  const float wn = (ima + dot(hadamard(rna, Ia), rna)) + (imb + dot(hadamard(rnb, Ib), rnb));
+  if (wn < 1e-8f) return;
+  const float excess = fmaxf(pen - slop, 0.0f);
+  const float bias = __fdiv_rn(baumgarte * excess, dt);
+  const float vrest = vn < -0.5f ? cim.w * vn : 0.0f;
+  const float jn = fmaxf(__fdiv_rn(-(vn + vrest) + bias, wn), 0.0f);
+  const V3 in_ = n * jn;
+  const float pcorr = baumgarte * excess;
+  if (ima > 1e-8f) {
+    vel[ia] = with_w(madd(in_, ima, v3(vel[ia])), vel[ia].w);
+    ang[ia] = with_w(v3(ang[ia]) + hadamard(cross(ra, in_), Ia), ang[ia].w);
+    pos[ia] = with_w(madd(n, pcorr * __fdiv_rn(ima, isum), v3(pos[ia])), pos[ia].w);
+  }
+  if (imb > 1e-8f) {
+    vel[ib] = with_w(msub(in_, imb, v3(vel[ib])), vel[ib].w);
+    ang[ib] = with_w(v3(ang[ib]) - hadamard(cross(rb, in_), Ib), ang[ib].w);
+    pos[ib] = with_w(msub(n, pcorr * __fdiv_rn(imb, isum), v3(pos[ib])), pos[ib].w);
+  }
+  const float jacc = cim.x + jn;
+  if (ts > 1e-6f && jacc > 1e-6f) {
+    const V3 t = vt * __frcp_rn(ts);
+    const V3 rta = cross(ra, t), rtb = cross(rb, t);
+    const float wt = (ima + dot(hadamard(rta, Ia), rta)) + (imb + dot(hadamard(rtb, Ib), rtb));
+    if (wt > 1e-8f) {
+      const float jt = fminf(__fdiv_rn(ts, wt), fr * jacc);
+      const V3 it = t * jt;
+      if (ima > 1e-8f) {
+        vel[ia] = with_w(msub(it, ima, v3(vel[ia])), vel[ia].w);
+        ang[ia] = with_w(v3(ang[ia]) - hadamard(cross(ra, it), Ia), ang[ia].w);
+      }
+      if (imb > 1e-8f) {
+        vel[ib] = with_w(madd(it, imb, v3(vel[ib])), vel[ib].w);
+        ang[ib] = with_w(v3(ang[ib]) + hadamard(cross(rb, it), Ib), ang[ib].w);
+      }
+    }
+  }
+  cim.x = jn;
+}
+
+// ------------------------------------------------------------------------------------
+// Narrow phase for one slot (narrow_phase, all_shaders.metal:751-894)
+// ------------------------------------------------------------------------------------
+__device__ __forceinline__ void narrow(uint32_t pk, const DGeom* geoms, const float4* pos, float restitution,
+                                       float4& cpp, float4& cnf, float4& cim) {
+  const DGeom& gA = geoms[pk_ga(pk)];
+  const DGeom& gB = geoms[pk_gb(pk)];
+  const float4 ga0 = __ldg(reinterpret_cast<const float4*>(gA.pos_size0));
+  const float4 gb0 = __ldg(reinterpret_cast<const float4*>(gB.pos_size0));
+  const V3 pa = v3(pos[pk_a(pk)]) + v3(ga0), pb = v3(pos[pk_b(pk)]) + v3(gb0);
+  const uint32_t ta = __ldg(&gA.type), tb = __ldg(&gB.type);
+  V3 normal{0, 0, 0}, point{0, 0, 0};
+  float pen = 0.0f;
+  bool hit = false;
+  if (ta == 0 && tb == 0) {
+    const V3 d = pb - pa;
+    const float dist = len(d);
+    const float md = ga0.w + gb0.w;
+    if (dist < md && dist > 1e-6f) {
+      normal = d * __frcp_rn(dist);
+      pen = md - dist;
+      point = madd(normal, ga0.w - pen * 0.5f, pa);
+      hit = true;
+    }
+  } else if ((ta == 0 && tb == 3) || (ta == 3 && tb == 0)) {
+    const V3 sp = ta == 0 ? pa : pb, pp = ta == 0 ? pb : pa;
+    const float sr = ta == 0 ? ga0.w : gb0.w;
+    const V3 pn{0.0f, 0.0f, 1.0f};
+    const float sd = dot(sp - pp, pn);
+    if (sd < sr) {
+      normal = ta == 3 ? -pn : pn;
+      pen = sr - sd;
+      point = msub(pn, sd + pen * 0.5f, sp);
+      hit = true;
+    }
+  } else if ((ta == 1 && tb == 3) || (ta == 3 && tb == 1)) {
+    const DGeom& cg = ta == 1 ? gA : gB;
+    const V3 cpos = ta == 1 ? pa : pb;
+    const float cr = ta == 1 ? ga0.w : gb0.w;
+    const float hl = __ldg(&cg.size12_fr_rest[0]);
+    const float4 cq = __ldg(reinterpret_cast<const float4*>(cg.quat));
+    const V3 axis = rotate(v3(0.0f, 0.0f, 1.0f), cq);
+    const V3 p1 = msub(axis, hl, cpos), p2 = madd(axis, hl, cpos);
+    const float d1 = p1.z - cr, d2 = p2.z - cr;
+    if (d1 < 0.0f || d2 < 0.0f) {
+      point = d1 < d2 ? p1 : p2;
+      point.z = 0.0f;
+      pen = -fminf(d1, d2);
+      normal = ta == 1 ? v3(0.0f, 0.0f, 1.0f) : v3(0.0f, 0.0f, -1.0f);
+      hit = true;
+    }
+  }
+  if (hit) {
+    const float fr = __fsqrt_rn(__ldg(&gA.size12_fr_rest[2]) * __ldg(&gB.size12_fr_rest[2]));
+    cpp = with_w(point, pen);
+    cnf = with_w(normal, fr);
+    cim = make_float4(0.0f, 0.0f, 0.0f, restitution);
+  } else {
+    cpp.w = -1.0f;
+  }
+}
+
+// ------------------------------------------------------------------------------------
+// Episode task extension: FK-consistent noisy reset (lane 0 of the group)
+// ------------------------------------------------------------------------------------
+__device__ void reset_env_noise(const StepArgs& a, uint32_t e, float4* pos, float4* quat, float4* vel, float4* ang,
+                                float* jp, float* jv, uint32_t episode) {
+  const uint32_t B = a.B, J = a.J;
+  const float* t = a.init_state;
+  for (uint32_t b = 0; b < B; ++b) {
+    pos[b] = reinterpret_cast<const float4*>(t)[b];
+    quat[b] = reinterpret_cast<const float4*>(t)[B + b];
+    vel[b] = reinterpret_cast<const float4*>(t)[2 * B + b];
+    ang[b] = reinterpret_cast<const float4*>(t)[3 * B + b];
+  }
+  for (uint32_t j = 0; j < J; ++j) {
+    jp[j] = t[16 * B + j];
+    jv[j] = t[16 * B + J + j];
+  }
+  const DTask& tk = a.task;
+  if (tk.noise != 0.0f) {
+    const uint64_t genv = uint64_t(e) + tk.env_offset;
+    const uint32_t rb = tk.body;
+    pos[rb].x = pos[rb].x + tk.noise * uniform_pm1(tk.seed, genv, episode, 0u);
+    pos[rb].y = pos[rb].y + tk.noise * uniform_pm1(tk.seed, genv, episode, 1u);
+    pos[rb].z = pos[rb].z + tk.noise * uniform_pm1(tk.seed, genv, episode, 2u);
+    for (uint32_t j = 0; j < J; ++j) {
+      const DJoint& jd = a.joints[j];
+      if (jd.type != 1) continue;
+      const float th = tk.noise * uniform_pm1(tk.seed, genv, episode, 3u + j);
+      const uint32_t pa = jd.parent, ch = jd.child;
+      const float4 qp = quat[pa];
+      const V3 anchor = v3(pos[pa]) + rotate(v3(jd.anchor_parent[0], jd.anchor_parent[1], jd.anchor_parent[2]), qp);
+      const V3 ax = rotate(v3(jd.axis[0], jd.axis[1], jd.axis[2]), qp);
+      const float al = len(ax);
+      if (!(al > 1e-8f)) continue;
+      const V3 h = ax * __fdiv_rn(0.5f * th, al);
+      const float4 qr = qnormalize(make_float4(h.x, h.y, h.z, 1.0f));
+      const uint32_t end = ch + a.subtree[ch];
+      for (uint32_t d = ch; d < end; ++d) {
+        const V3 rel = v3(pos[d]) - anchor;
+        pos[d] = with_w(anchor + rotate(rel, qr), pos[d].w);
+        quat[d] = qnormalize(qmul(qr, quat[d]));
+      }
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------------
+// The kernel.  L lanes per environment, blockDim.x / L environments per block.
+// ------------------------------------------------------------------------------------
+template <int L>
+__global__ void __launch_bounds__(256) step_kernel(StepArgs a) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  const uint32_t NE = blockDim.x / L;
+  const uint32_t g = threadIdx.x / L;
+  const uint32_t l = threadIdx.x % L;
+  const uint32_t e = blockIdx.x * NE + g;
+  if (e >= a.num_envs) return;  // whole groups retire together; syncs are group-local
+  const unsigned gmask = L == 32 ? 0xFFFFFFFFu : (((1u << L) - 1u) << ((threadIdx.x & 31u) & ~(L - 1u)));
+  const uint32_t gshift = (threadIdx.x & 31u) & ~(L - 1u);
+
+  const uint32_t B = a.B, J = a.J, A = a.A, M = a.M;
+  const Plan P = make_plan(B, J, M);
+  unsigned char* base = smem_raw + size_t(g) * P.bytes;
+  float4* pos = sm<float4>(base, P.pos);
+  float4* quat = sm<float4>(base, P.quat);
+  float4* vel = sm<float4>(base, P.vel);
+  float4* ang = sm<float4>(base, P.ang);
+  float4* ppos = sm<float4>(base, P.ppos);
+  float4* pquat = sm<float4>(base, P.pquat);
+  float4* frc = sm<float4>(base, P.frc);
+  float4* trq = sm<float4>(base, P.trq);
+  float* jt = sm<float>(base, P.jt);
+  float* jp = sm<float>(base, P.jp);
+  float* jv = sm<float>(base, P.jv);
+  float4* cpp = sm<float4>(base, P.cpp);
+  float4* cnf = sm<float4>(base, P.cnf);
+  float4* cim = sm<float4>(base, P.cim);
+  uint32_t* cpk = sm<uint32_t>(base, P.cpk);
+  float4* ppp = sm<float4>(base, P.ppp);
+  float4* pim = sm<float4>(base, P.pim);
+  uint32_t* ppk = sm<uint32_t>(base, P.ppk);
+  uint16_t* ord = sm<uint16_t>(base, P.ord);
+  uint16_t* sched = sm<uint16_t>(base, P.sched);
+  uint16_t* sidx = sm<uint16_t>(base, P.sidx);
+  uint16_t* slev = sm<uint16_t>(base, P.slev);
+  uint16_t* lvl = sm<uint16_t>(base, P.lvl);
+  uint16_t* lcur = sm<uint16_t>(base, P.lcur);
+  uint16_t* blev = sm<uint16_t>(base, P.blev);
+  uint32_t* flags = sm<uint32_t>(base, P.flags);
+
+  // ---------------- load the environment ----------------
+  const size_t eb = size_t(e) * B;
+  const float4* gpos = reinterpret_cast<const float4*>(a.pos) + eb;
+  const float4* gquat = reinterpret_cast<const float4*>(a.quat) + eb;
+  const float4* gvel = reinterpret_cast<const float4*>(a.vel) + eb;
+  const float4* gang = reinterpret_cast<const float4*>(a.angvel) + eb;
+  for (uint32_t b = l; b < B; b += L) {
+    pos[b] = gpos[b];
+    quat[b] = gquat[b];
+    vel[b] = gvel[b];
+    ang[b] = gang[b];
+  }
+  const uint32_t J1 = J > 0 ? J : 1;
+  for (uint32_t j = l; j < J; j += L) jt[j] = a.jtorque[size_t(e) * J1 + j];
+  const Contact* gc = a.contacts + size_t(e) * M;
+  for (uint32_t i = l; i < M; i += L) {
+    const float4* src = reinterpret_cast<const float4*>(gc + i);
+    cpp[i] = src[0];
+    cnf[i] = src[1];
+    const uint4 ix = reinterpret_cast<const uint4*>(src)[2];
+    cpk[i] = pack_checked(ix, B, a.G);
+    cim[i] = src[3];
+    ord[i] = uint16_t(i);
+  }
+  uint32_t count = a.counts[e];
+  uint32_t prev_count = a.prev_counts[e];
+  const bool sep = a.prev_sep[e] != 0;
+  if (sep) {  // prev contacts diverged from the contacts buffer (after a step_subset)
+    const Contact* pc = a.prev_contacts + size_t(e) * M;
+    const uint32_t np = prev_count < M ? prev_count : M;
+    for (uint32_t i = l; i < np; i += L) {
+      const float4* src = reinterpret_cast<const float4*>(pc + i);
+      ppp[i] = src[0];
+      const uint4 ix = reinterpret_cast<const uint4*>(src)[2];
+      ppk[i] = pack_checked(ix, B, a.G);
+      pim[i] = src[3];
+    }
+  }
+  __syncwarp(gmask);
+
+  const float dt = a.dt, inv_dt = a.inv_dt;
+  const V3 grav{a.gravity[0], a.gravity[1], a.gravity[2]};
+  const float* act = a.actions + size_t(e) * A;
+
+  for (uint32_t s = 0; s < a.substeps; ++s) {
+    // ---- prev snapshot = final slot list of the previous substep ----
+    const uint32_t n_prev = prev_count < M ? prev_count : M;
+    if (!(s == 0 && sep)) {
+      for (uint32_t i = l; i < n_prev; i += L) {
+        const uint32_t st = ord[i];
+        ppk[i] = cpk[st];
+        ppp[i] = cpp[st];
+        pim[i] = cim[st];
+      }
+    }
+    // ---- actions -> joint torques; actuators sharing a joint run in index order ----
+    const uint32_t k_first = a.actuators_unique ? l : (l == 0 ? 0u : A);
+    const uint32_t k_step = a.actuators_unique ? L : 1u;
+    for (uint32_t k = k_first; k < A; k += k_step) {
+      const DActuator& ad = a.actuators[k];
+      float tq = clampf(act[k], __ldg(&ad.ctrl_min), __ldg(&ad.ctrl_max)) * __ldg(&ad.gear);
+      jt[__ldg(&ad.joint)] = clampf(tq, __ldg(&ad.force_min), __ldg(&ad.force_max));
+    }
+    // ---- gravity wrench, kinematic bodies ----
+    for (uint32_t b = l; b < B; b += L) {
+      const DBody& bd = a.bodies[b];
+      const float im = __ldg(&bd.inv_mass_inertia[0]);
+      if (im < 1e-8f) {
+        frc[b] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        trq[b] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      } else {
+        const V3 f = grav * __frcp_rn(im);
+        const float4 com = __ldg(reinterpret_cast<const float4*>(bd.com));
+        frc[b] = with_w(f, 0.0f);
+        trq[b] = with_w(cross(rotate(v3(com), quat[b]), f), 0.0f);
+      }
+      if (__ldg(&bd.type) == 1u) {
+        pos[b] = with_w(madd(v3(vel[b]), dt, v3(pos[b])), 0.0f);
+        const float4 q = quat[b];
+        quat[b] = qnormalize(qmadd(qmul_v((v3(ang[b]) * dt) * 0.5f, q), 1.0f, q));
+      }
+    }
+    __syncwarp(gmask);
+    // ---- joint torques -> body wrenches, per body in joint order ----
+    for (uint32_t b = l; b < B; b += L) {
+      const uint32_t k0 = __ldg(&a.bodies[b].jf_begin), k1 = __ldg(&a.bodies[b].jf_end);
+      if (k0 == k1) continue;
+      V3 F = v3(frc[b]), T = v3(trq[b]);
+      for (uint32_t k = k0; k < k1; ++k) {
+        const uint32_t ent = __ldg(&a.jf_list[k]);
+        const uint32_t j = ent & 0x7FFFFFFFu;
+        const float tau = jt[j];
+        if (fabsf(tau) < 1e-6f) continue;
+        const DJoint& jd = a.joints[j];
+        const V3 f = rotate(v3(__ldg(&jd.axis[0]), __ldg(&jd.axis[1]), __ldg(&jd.axis[2])), quat[__ldg(&jd.parent)]) * tau;
+        if (__ldg(&jd.type) == 2u) F = (ent >> 31) ? F - f : F + f;
+        else T = (ent >> 31) ? T - f : T + f;
+      }
+      frc[b] = with_w(F, 0.0f);
+      trq[b] = with_w(T, 0.0f);
+    }
+    __syncwarp(gmask);
+    // ---- save prev pose, semi-implicit Euler ----
+    for (uint32_t b = l; b < B; b += L) {
+      ppos[b] = pos[b];
+      pquat[b] = quat[b];
+      const float4 mi = __ldg(reinterpret_cast<const float4*>(a.bodies[b].inv_mass_inertia));
+      if (mi.x < 1e-8f) continue;
+      V3 v = madd(v3(frc[b]) * mi.x, dt, v3(vel[b])) * 0.999f;
+      vel[b] = with_w(v, 0.0f);
+      pos[b] = with_w(madd(v, dt, v3(pos[b])), 0.0f);
+      V3 w = madd(hadamard(v3(mi.y, mi.z, mi.w), v3(trq[b])), dt, v3(ang[b])) * 0.999f;
+      ang[b] = with_w(w, 0.0f);
+      const float4 q = quat[b];
+      quat[b] = qnormalize(qmadd(qmul_v((w * dt) * 0.5f, q), 1.0f, q));
+    }
+    __syncwarp(gmask);
+    // ---- broad phase: candidate pairs in emission order, compacted by ballot ----
+    const uint32_t count0 = count;
+    for (uint32_t r = 0; r < a.num_pairs; r += L) {
+      const uint32_t p = r + l;
+      bool pass = false;
+      uint32_t ga = 0, gb = 0, ba = 0, bb = 0;
+      if (p < a.num_pairs) {
+        const DPair pr = a.pairs[p];
+        ga = pr.ga;
+        gb = pr.gb;
+        ba = __ldg(&a.geoms[ga].body);
+        bb = __ldg(&a.geoms[gb].body);
+        if (pr.plane) {
+          pass = true;
+        } else {
+          const V3 pa = v3(pos[ba]) + v3(__ldg(reinterpret_cast<const float4*>(a.geoms[ga].pos_size0)));
+          const V3 pb = v3(pos[bb]) + v3(__ldg(reinterpret_cast<const float4*>(a.geoms[gb].pos_size0)));
+          const V3 d = pb - pa;
+          pass = !(dot(d, d) >= pr.min_dist_sq);
+        }
+      }
+      const uint32_t bal = (__ballot_sync(gmask, pass) >> gshift) & (L == 32 ? 0xFFFFFFFFu : ((1u << L) - 1u));
+      if (pass) {
+        const uint32_t slot = count + __popc(bal & ((1u << l) - 1u));
+        if (slot < M) cpk[ord[slot]] = pack4(ba, bb, ga, gb);
+      }
+      count += __popc(bal);
+    }
+    const uint32_t n = count < M ? count : M;
+    const uint32_t n_old = count0 < M ? count0 : M;
+    __syncwarp(gmask);
+    // ---- stable sort by body-pair key (only when slots were appended) ----
+    if (n > n_old) {
+      for (uint32_t i = l; i < n; i += L) {
+        const uint32_t ki = pk_key(cpk[ord[i]]);
+        uint32_t rank = 0;
+        for (uint32_t j = 0; j < n; ++j) {
+          const uint32_t kj = pk_key(cpk[ord[j]]);
+          rank += (kj < ki) || (kj == ki && j < i);
+        }
+        sched[rank] = ord[i];
+      }
+      __syncwarp(gmask);
+      for (uint32_t i = l; i < n; i += L) ord[i] = sched[i];
+      __syncwarp(gmask);
+    }
+    // ---- narrow phase ----
+    for (uint32_t i = l; i < n; i += L) {
+      const uint32_t st = ord[i];
+      narrow(cpk[st], a.geoms, pos, a.restitution, cpp[st], cnf[st], cim[st]);
+    }
+    __syncwarp(gmask);
+    // ---- warm start: best previous contact of the same pair within 0.2 ----
+    for (uint32_t i = l; i < n; i += L) {
+      const uint32_t st = ord[i];
+      if (cpp[st].w < 0.0f) continue;
+      const uint32_t key = pk_key(cpk[st]);
+      uint32_t lo = 0, hi = n_prev;  // first prev slot with key >= key
+      while (lo < hi) {
+        const uint32_t mid = (lo + hi) >> 1;
+        if (pk_key(ppk[mid]) < key) lo = mid + 1;
+        else hi = mid;
+      }
+      const V3 p = xyz(cpp[st]);
+      float best = 0.04f;
+      int match = -1;
+      for (uint32_t j = lo; j < n_prev && pk_key(ppk[j]) == key; ++j) {
+        const float4 q = ppp[j];
+        if (q.w < 0.0f) continue;
+        const V3 d = xyz(q) - p;
+        const float dsq = dot(d, d);
+        if (dsq < best) {
+          best = dsq;
+          match = int(j);
+        }
+      }
+      if (match >= 0) {
+        const float4 pi = pim[match];
+        cim[st].x = pi.x * 0.8f;
+        cim[st].y = pi.y * 0.8f;
+        cim[st].z = pi.z * 0.8f;
+      }
+    }
+    __syncwarp(gmask);
+    // ---- XPBD joints: colours in order, constraints of a colour in parallel ----
+    for (uint32_t it = 0; it < a.iterations; ++it) {
+      for (uint32_t col = 0; col < a.num_colors; ++col) {
+        const uint32_t off = __ldg(&a.color_ranges[2 * col]), cnt = __ldg(&a.color_ranges[2 * col + 1]);
+        for (uint32_t k = l; k < cnt; k += L) {
+          const DConstraint c = a.constraints[off + k];
+          solve_constraint(c, a.bodies, pos, quat);
+        }
+        __syncwarp(gmask);
+      }
+    }
+    // ---- contacts: level schedule equivalent to solving slots in slot order ----
+    // level(i) = 1 + max level of earlier valid slots sharing a dynamic body; slots of
+    // one level touch disjoint dynamic bodies, and every conflicting pair keeps its slot
+    // order, so solving level by level equals solving the slots one after another.
+    uint32_t nlev = 0;
+    if (l == 0) {
+      for (uint32_t b = 0; b < B; ++b) blev[b] = 0;  // stored as level + 1 (0: none)
+      uint32_t nv = 0;
+      for (uint32_t i = 0; i < n; ++i) {
+        const uint32_t st = ord[i];
+        if (cpp[st].w < 0.0f) continue;
+        const uint32_t ba = pk_a(cpk[st]), bb = pk_b(cpk[st]);
+        const bool da = __ldg(&a.bodies[ba].inv_mass_inertia[0]) > 1e-8f;
+        const bool db = __ldg(&a.bodies[bb].inv_mass_inertia[0]) > 1e-8f;
+        uint32_t lv = 0;
+        if (da && blev[ba] > lv) lv = blev[ba];
+        if (db && blev[bb] > lv) lv = blev[bb];
+        if (da) blev[ba] = uint16_t(lv + 1);
+        if (db) blev[bb] = uint16_t(lv + 1);
+        sidx[nv] = uint16_t(i);
+        slev[nv] = uint16_t(lv);
+        ++nv;
+        if (lv + 1 > nlev) nlev = lv + 1;
+      }
+      for (uint32_t v = 0; v <= nlev; ++v) lcur[v] = 0;  // counting sort, stable
+      for (uint32_t v = 0; v < nv; ++v) lcur[slev[v] + 1]++;
+      for (uint32_t v = 1; v <= nlev; ++v) lcur[v] = uint16_t(lcur[v] + lcur[v - 1]);
+      for (uint32_t v = 0; v <= nlev; ++v) lvl[v] = lcur[v];
+      for (uint32_t v = 0; v < nv; ++v) sched[lcur[slev[v]]++] = sidx[v];
+    }
+    nlev = __shfl_sync(gmask, nlev, gshift);
+    __syncwarp(gmask);
+    for (uint32_t it = 0; it < a.iterations; ++it) {
+      for (uint32_t lv = 0; lv < nlev; ++lv) {
+        const uint32_t k0 = lvl[lv], k1 = lvl[lv + 1];
+        for (uint32_t k = k0 + l; k < k1; k += L) {
+          const uint32_t st = ord[sched[k]];
+          solve_contact(cpp[st], cnf[st], cim[st], cpk[st], a.bodies, pos, vel, ang, dt, a.baumgarte, a.slop);
+        }
+        __syncwarp(gmask);
+      }
+    }
+    // ---- velocities from the position change ----
+    for (uint32_t b = l; b < B; b += L) {
+      if (__ldg(&a.bodies[b].inv_mass_inertia[0]) < 1e-8f) continue;
+      vel[b] = with_w((v3(pos[b]) - v3(ppos[b])) * inv_dt, 0.0f);
+      float4 dq = qmul(quat[b], qconj(pquat[b]));
+      if (dq.w < 0.0f) dq = qneg(dq);
+      ang[b] = with_w((xyz(dq) * 2.0f) * inv_dt, 0.0f);
+    }
+    prev_count = count;
+    __syncwarp(gmask);
+  }
+
+  // ---- joint states and sensors from the final substep ----
+  const bool stepped = a.substeps > 0;
+  const bool publish = a.step_mask == nullptr || a.step_mask[e] != 0;
+  if (stepped) {
+    for (uint32_t j = l; j < J; j += L) {
+      const DJoint& jd = a.joints[j];
+      const uint32_t ty = __ldg(&jd.type), ia = __ldg(&jd.parent), ib = __ldg(&jd.child);
+      float p = 0.0f, v = 0.0f;
+      const float4 qa = quat[ia], qb = quat[ib];
+      const V3 axl = v3(__ldg(&jd.axis[0]), __ldg(&jd.axis[1]), __ldg(&jd.axis[2]));
+      if (ty == 1) {
+        const V3 aw = rotate(axl, qa);
+        const float4 qrel = qmul(qconj(qa), qb);
+        p = 2.0f * atan2r(dot(xyz(qrel), axl), qrel.w);
+        v = dot(v3(ang[ib]) - v3(ang[ia]), aw);
+      } else if (ty == 2) {
+        const V3 aw = rotate(axl, qa);
+        const V3 ra = rotate(v3(jd.anchor_parent[0], jd.anchor_parent[1], jd.anchor_parent[2]), qa);
+        const V3 rb = rotate(v3(jd.anchor_child[0], jd.anchor_child[1], jd.anchor_child[2]), qb);
+        p = dot((v3(pos[ib]) + rb) - (v3(pos[ia]) + ra), aw);
+        const V3 vpa = v3(vel[ia]) + cross(v3(ang[ia]), ra), vpb = v3(vel[ib]) + cross(v3(ang[ib]), rb);
+        v = dot(vpb - vpa, aw);
+      }
+      jp[j] = p;
+      jv[j] = v;
+    }
+    __syncwarp(gmask);
+    if (publish) {
+      float* gobs = a.obs + size_t(e) * a.obs_dim;
+      for (uint32_t si = l; si < a.S; si += L) {
+        const DSensor sd = a.sensors[si];
+        const uint32_t o = sd.object;
+        float* out = gobs + sd.offset;
+        switch (sd.type) {
+          case 0: out[0] = jp[o]; break;
+          case 1: out[0] = jv[o]; break;
+          case 2: {
+            const V3 lg = rotate(grav, qconj(quat[o]));
+            out[0] = lg.x, out[1] = lg.y, out[2] = lg.z;
+            break;
+          }
+          case 3:
+          case 10: out[0] = ang[o].x, out[1] = ang[o].y, out[2] = ang[o].z; break;
+          case 7: out[0] = pos[o].x, out[1] = pos[o].y, out[2] = pos[o].z; break;
+          case 8: out[0] = quat[o].x, out[1] = quat[o].y, out[2] = quat[o].z, out[3] = quat[o].w; break;
+          case 9: out[0] = vel[o].x, out[1] = vel[o].y, out[2] = vel[o].z; break;
+          default: break;
+        }
+      }
+    }
+  }
+
+  const uint32_t n_fin = count < M ? count : M;
+  Contact* gcw = a.contacts + size_t(e) * M;
+  if (!publish) {
+    // step_subset: an env outside the mask keeps its public state, but the reference
+    // still advanced its contact cache (world.zig:833-929 restores only public buffers).
+    if (stepped) {
+      Contact* pc = a.prev_contacts + size_t(e) * M;
+      for (uint32_t i = l; i < n_fin; i += L) {
+        const uint32_t st = ord[i], k = cpk[st];
+        float4* dst = reinterpret_cast<float4*>(pc + i);
+        dst[0] = cpp[st];
+        dst[1] = cnf[st];
+        reinterpret_cast<uint4*>(dst)[2] = make_uint4(pk_a(k), pk_b(k), pk_ga(k), pk_gb(k));
+        dst[3] = cim[st];
+      }
+      if (l == 0) {
+        a.prev_counts[e] = prev_count;
+        a.prev_sep[e] = 1;
+      }
+    }
+    return;
+  }
+
+  // ---- accelerations from the whole-step velocity change (world.zig:736-746) ----
+  float4* gacc = reinterpret_cast<float4*>(a.acc) + eb;
+  for (uint32_t b = l; b < B; b += L) {
+    const float4 v0 = gvel[b], v1 = vel[b];
+    gacc[b] = make_float4((v1.x - v0.x) * a.inv_step, (v1.y - v0.y) * a.inv_step, (v1.z - v0.z) * a.inv_step, 0.0f);
+  }
+  // ---- contacts back to HBM (slot order) ----
+  for (uint32_t i = l; i < n_fin; i += L) {
+    const uint32_t st = ord[i], k = cpk[st];
+    float4* dst = reinterpret_cast<float4*>(gcw + i);
+    dst[0] = cpp[st];
+    dst[1] = cnf[st];
+    reinterpret_cast<uint4*>(dst)[2] = make_uint4(pk_a(k), pk_b(k), pk_ga(k), pk_gb(k));
+    dst[3] = cim[st];
+  }
+  // ---- episode task extension ----
+  uint32_t count_out = count;
+  if (a.task.enabled) {
+    __syncwarp(gmask);
+    if (l == 0) {
+      const uint32_t tb = a.task.body;
+      const float z = pos[tb].z;
+      const bool done = !(z >= a.task.z_min && z <= a.task.z_max);
+      float ctrl = 0.0f;
+      for (uint32_t k = 0; k < A; ++k) ctrl = fma_(act[k], act[k], ctrl);
+      float r = fma_(a.task.forward_weight, vel[tb].x, a.task.alive_bonus);
+      r = fma_(-a.task.ctrl_cost, ctrl, r);
+      a.rewards[e] = r;
+      a.dones[e] = done ? 1 : 0;
+      if (done && a.task.auto_reset) {
+        const uint32_t ep = a.episode[e];
+        reset_env_noise(a, e, pos, quat, vel, ang, jp, jv, ep);
+        a.episode[e] = ep + 1;
+        count_out = 0;
+        flags[0] = 1;  // the other lanes must republish the reset joint state
+      } else {
+        flags[0] = 0;
+      }
+    }
+    __syncwarp(gmask);
+    count_out = __shfl_sync(gmask, count_out, gshift);
+  }
+  // ---- body and joint state back to HBM ----
+  float4* wpos = reinterpret_cast<float4*>(a.pos) + eb;
+  float4* wquat = reinterpret_cast<float4*>(a.quat) + eb;
+  float4* wvel = reinterpret_cast<float4*>(a.vel) + eb;
+  float4* wang = reinterpret_cast<float4*>(a.angvel) + eb;
+  for (uint32_t b = l; b < B; b += L) {
+    wpos[b] = pos[b];
+    wquat[b] = quat[b];
+    wvel[b] = vel[b];
+    wang[b] = ang[b];
+  }
+  const bool reset_now = a.task.enabled && flags[0] != 0;
+  for (uint32_t j = l; j < J; j += L) {
+    a.jtorque[size_t(e) * J1 + j] = jt[j];
+    if (stepped || reset_now) {
+      a.jpos[size_t(e) * J1 + j] = jp[j];
+      a.jvel[size_t(e) * J1 + j] = jv[j];
+    }
+  }
+  if (l == 0) {
+    a.counts[e] = count_out;
+    a.prev_counts[e] = prev_count;
+    a.prev_sep[e] = 0;
+  }
+}
+
+// ------------------------------------------------------------------------------------
+// Host launcher
+// ------------------------------------------------------------------------------------
+cudaError_t launch_step(const StepArgs& args, int lanes, int envs_per_block, cudaStream_t stream) {
+  if (args.num_envs == 0) return cudaSuccess;
+  const uint32_t env_bytes = env_smem_bytes(args.B, args.J, args.M);
+  const uint32_t threads = uint32_t(lanes * envs_per_block);
+  const uint32_t blocks = (args.num_envs + envs_per_block - 1) / envs_per_block;
+  const size_t smem = size_t(env_bytes) * envs_per_block;
+  cudaError_t err = cudaSuccess;
+  switch (lanes) {
+#define ZB_LAUNCH(LN)                                                                               \
+  case LN:                                                                                          \
+    err = cudaFuncSetAttribute(step_kernel<LN>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)); \
+    if (err != cudaSuccess) return err;                                                             \
+    step_kernel<LN><<<blocks, threads, smem, stream>>>(args);                                       \
+    break;
+    ZB_LAUNCH(4)
+    ZB_LAUNCH(8)
+    ZB_LAUNCH(16)
+    ZB_LAUNCH(32)
+#undef ZB_LAUNCH
+    default: return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace zb
+
+// ------------------------------------------------------------------------------------
+// Small state kernels: masked reset to the initial template (World.reset, world.zig:1296-1314)
+// and masked per-env copies (reset_to_state / set_body_*, main.zig:290-385, world.zig:1413-1478)
+// ------------------------------------------------------------------------------------
+namespace zb {
+
+__global__ void reset_envs_kernel(float4* pos, float4* quat, float4* vel, float4* ang, float* jpos, float* jvel,
+                                  const float* init, uint32_t E, uint32_t B, uint32_t J, const uint8_t* mask) {
+  const uint32_t J1 = J > 0 ? J : 1;
+  const uint32_t per = 4 * B + J;
+  for (size_t t = size_t(blockIdx.x) * blockDim.x + threadIdx.x; t < size_t(E) * per; t += size_t(gridDim.x) * blockDim.x) {
+    const uint32_t e = uint32_t(t / per), k = uint32_t(t % per);
+    if (mask && !mask[e]) continue;
+    const float4* ti = reinterpret_cast<const float4*>(init);
+    if (k < B) pos[size_t(e) * B + k] = ti[k];
+    else if (k < 2 * B) quat[size_t(e) * B + (k - B)] = ti[B + (k - B)];
+    else if (k < 3 * B) vel[size_t(e) * B + (k - 2 * B)] = ti[2 * B + (k - 2 * B)];
+    else if (k < 4 * B) ang[size_t(e) * B + (k - 3 * B)] = ti[3 * B + (k - 3 * B)];
+    else {
+      const uint32_t j = k - 4 * B;
+      jpos[size_t(e) * J1 + j] = init[16 * B + j];
+      jvel[size_t(e) * J1 + j] = init[16 * B + J + j];
+    }
+  }
+}
+
+__global__ void masked_copy_kernel(float4* dst, const float4* src, uint32_t E, uint32_t per_env, const uint8_t* mask) {
+  for (size_t t = size_t(blockIdx.x) * blockDim.x + threadIdx.x; t < size_t(E) * per_env; t += size_t(gridDim.x) * blockDim.x) {
+    const uint32_t e = uint32_t(t / per_env);
+    if (mask && !mask[e]) continue;
+    dst[t] = src[t];
+  }
+}
+
+cudaError_t launch_reset(float* pos, float* quat, float* vel, float* ang, float* jpos, float* jvel, const float* init,
+                         uint32_t E, uint32_t B, uint32_t J, const uint8_t* mask, cudaStream_t stream) {
+  const size_t total = size_t(E) * (4 * B + J);
+  if (total == 0) return cudaSuccess;
+  const uint32_t blocks = uint32_t(std::min<size_t>((total + 255) / 256, 148 * 16));
+  reset_envs_kernel<<<blocks, 256, 0, stream>>>(reinterpret_cast<float4*>(pos), reinterpret_cast<float4*>(quat),
+                                                 reinterpret_cast<float4*>(vel), reinterpret_cast<float4*>(ang), jpos,
+                                                 jvel, init, E, B, J, mask);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_masked_copy(float* dst, const float* src, uint32_t E, uint32_t B, const uint8_t* mask,
+                               cudaStream_t stream) {
+  const size_t total = size_t(E) * B;
+  if (total == 0) return cudaSuccess;
+  const uint32_t blocks = uint32_t(std::min<size_t>((total + 255) / 256, 148 * 16));
+  masked_copy_kernel<<<blocks, 256, 0, stream>>>(reinterpret_cast<float4*>(dst), reinterpret_cast<const float4*>(src),
+                                                  E, B, mask);
+  return cudaGetLastError();
+}
+
+}  // namespace zb

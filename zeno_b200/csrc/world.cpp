@@ -1,0 +1,324 @@
+// World runtime (src/world/world.zig equivalents on CUDA).
+//
+// Memory: ABI-visible state is CUDA managed memory with the device as preferred
+// location, so a pointer handed out by a zeno_world_get_* call is valid on the host (the
+// reference's numpy views read and write it, src/python/zeno/_ffi.py:600-620) and on
+// the GPU (torch / DLPack consumers), and host writes between steps are seen by the
+// next step.  Model tables and internal caches are plain device memory.
+#include "world.h"
+
+#include <chrono>
+#include <cstring>
+#include <vector>
+
+#include "step_kernel.h"
+
+namespace zb {
+
+namespace {
+int opt_in_smem(int dev) {
+  int v = 0;
+  cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+  return v;
+}
+}  // namespace
+
+template <class T>
+cudaError_t World::managed(T** p, size_t n) {
+  n = n ? n : 1;
+  void* q = nullptr;
+  cudaError_t e = cudaMallocManaged(&q, n * sizeof(T));
+  if (e != cudaSuccess) return e;
+  allocations_.push_back(q);
+  cudaMemset(q, 0, n * sizeof(T));
+  cudaMemAdvise(q, n * sizeof(T), cudaMemAdviseSetPreferredLocation, device_);
+  bytes_ += n * sizeof(T);
+  *p = static_cast<T*>(q);
+  return cudaSuccess;
+}
+
+template <class T>
+cudaError_t World::device_buf(T** p, size_t n) {
+  n = n ? n : 1;
+  void* q = nullptr;
+  cudaError_t e = cudaMalloc(&q, n * sizeof(T));
+  if (e != cudaSuccess) return e;
+  allocations_.push_back(q);
+  cudaMemset(q, 0, n * sizeof(T));
+  bytes_ += n * sizeof(T);
+  *p = static_cast<T*>(q);
+  return cudaSuccess;
+}
+
+World* World::create(const Scene& sc, const WorldConfig& cfg, std::string* err) {
+  auto fail = [&](const std::string& m, World* w) -> World* {
+    if (err) *err = m;
+    delete w;
+    return nullptr;
+  };
+  int ndev = 0;
+  if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) return fail("no CUDA device", nullptr);
+  if (cfg.num_envs == 0) return fail("num_envs must be at least 1", nullptr);  // state.zig buffers of size 0 fail
+  World* w = new World();
+  cudaGetDevice(&w->device_);
+  w->scene_ = sc;
+  w->cfg_ = cfg;
+  w->timestep_ = cfg.timestep > 0 ? cfg.timestep : sc.timestep;
+  std::memcpy(w->gravity_, sc.gravity, 12);
+  std::string merr;
+  if (!build_model(sc, &w->model_, &merr)) return fail(merr, w);
+  const HostModel& m = w->model_;
+  const uint32_t E = cfg.num_envs, B = m.B, J1 = m.J ? m.J : 1, M = cfg.max_contacts_per_env;
+  if (M > 65535) return fail("max_contacts_per_env above 65535", w);
+
+  // launch shape: 8 lanes per env, as many envs per block as shared memory allows (<= 16)
+  const uint32_t env_bytes = env_smem_bytes(B, m.J, M);
+  const int smem_cap = opt_in_smem(w->device_);
+  if (env_bytes > uint32_t(smem_cap)) return fail("model does not fit in shared memory (reduce max_contacts_per_env)", w);
+  w->lanes_ = 8;
+  w->envs_per_block_ = int(std::min<uint32_t>(16u, uint32_t(smem_cap) / env_bytes));
+
+  if (cudaStreamCreateWithFlags(&w->own_stream_, cudaStreamNonBlocking) != cudaSuccess) return fail("stream", w);
+  w->stream_ = w->own_stream_;
+
+  cudaError_t e = cudaSuccess;
+  const size_t nb4 = size_t(E) * B * 4;
+  e = e ? e : w->managed(&w->pos, nb4);
+  e = e ? e : w->managed(&w->quat, nb4);
+  e = e ? e : w->managed(&w->vel, nb4);
+  e = e ? e : w->managed(&w->angvel, nb4);
+  e = e ? e : w->managed(&w->acc, nb4);
+  e = e ? e : w->managed(&w->jpos, size_t(E) * J1);
+  e = e ? e : w->managed(&w->jvel, size_t(E) * J1);
+  e = e ? e : w->managed(&w->jtorque, size_t(E) * J1);
+  e = e ? e : w->managed(&w->obs, size_t(E) * (m.obs_dim ? m.obs_dim : 1));
+  e = e ? e : w->managed(&w->rewards, E);
+  e = e ? e : w->managed(&w->dones, E);
+  e = e ? e : w->managed(&w->contacts, size_t(E) * M);
+  e = e ? e : w->managed(&w->counts, E);
+  e = e ? e : w->device_buf(&w->prev_counts_, E);
+  e = e ? e : w->device_buf(&w->prev_sep_, E);
+  e = e ? e : w->device_buf(&w->episode_, E);
+  e = e ? e : w->device_buf(&w->d_actions_, size_t(E) * (m.A ? m.A : 1));
+  e = e ? e : w->device_buf(&w->d_mask_, E);
+  e = e ? e : w->device_buf(&w->d_status_, 4);
+  auto upload = [&](auto** dst, const auto& v) {
+    if (e != cudaSuccess) return;
+    e = w->device_buf(dst, v.size());
+    if (e == cudaSuccess && !v.empty()) e = cudaMemcpy(*dst, v.data(), v.size() * sizeof(v[0]), cudaMemcpyHostToDevice);
+  };
+  upload(&w->d_bodies_, m.bodies);
+  upload(&w->d_jf_, m.jf_list);
+  upload(&w->d_joints_, m.joints);
+  upload(&w->d_geoms_, m.geoms);
+  upload(&w->d_pairs_, m.pairs);
+  upload(&w->d_act_, m.actuators);
+  upload(&w->d_sensors_, m.sensors);
+  upload(&w->d_cons_, m.constraints);
+  upload(&w->d_colors_, m.color_ranges);
+  upload(&w->d_subtree_, m.subtree);
+  upload(&w->d_init_, m.init_state);
+  if (e != cudaSuccess) return fail(std::string("CUDA allocation failed: ") + cudaGetErrorString(e), w);
+
+  // initializeState (world.zig:663-691): every env starts from the body definitions
+  e = launch_reset(w->pos, w->quat, w->vel, w->angvel, w->jpos, w->jvel, w->d_init_, E, B, m.J, nullptr, w->stream_);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(w->stream_);
+  if (e != cudaSuccess) return fail(std::string("CUDA init failed: ") + cudaGetErrorString(e), w);
+  return w;
+}
+
+World::~World() {
+  if (own_stream_) cudaStreamSynchronize(own_stream_);
+  for (void* p : allocations_) cudaFree(p);
+  if (own_stream_) cudaStreamDestroy(own_stream_);
+}
+
+StepArgs World::args(uint32_t substeps, const float* actions, const uint8_t* mask) const {
+  const HostModel& m = model_;
+  StepArgs a;
+  std::memset(&a, 0, sizeof(a));
+  a.num_envs = cfg_.num_envs;
+  a.B = m.B, a.J = m.J, a.A = m.A, a.G = m.G, a.S = m.S, a.M = cfg_.max_contacts_per_env, a.K = m.K;
+  a.obs_dim = m.obs_dim, a.num_colors = m.num_colors, a.num_pairs = uint32_t(m.pairs.size());
+  a.iterations = cfg_.contact_iterations;
+  a.substeps = substeps;
+  a.actuators_unique = m.actuators_unique ? 1u : 0u;
+  a.dt = timestep_ / float(substeps > 1 ? substeps : 1u);  // world.zig:699-702
+  a.inv_dt = 1.0f / a.dt;
+  a.inv_step = timestep_ > 0 ? 1.0f / timestep_ : 0.0f;  // world.zig:736
+  std::memcpy(a.gravity, gravity_, 12);
+  a.baumgarte = scene_.baumgarte, a.slop = scene_.slop, a.restitution = scene_.restitution;
+  a.bodies = d_bodies_, a.jf_list = d_jf_, a.joints = d_joints_, a.geoms = d_geoms_, a.pairs = d_pairs_;
+  a.actuators = d_act_, a.sensors = d_sensors_, a.constraints = d_cons_, a.color_ranges = d_colors_;
+  a.subtree = d_subtree_, a.init_state = d_init_;
+  a.pos = pos, a.quat = quat, a.vel = vel, a.angvel = angvel, a.acc = acc;
+  a.jpos = jpos, a.jvel = jvel, a.jtorque = jtorque, a.obs = obs, a.rewards = rewards, a.dones = dones;
+  a.contacts = contacts, a.counts = counts, a.prev_counts = prev_counts_, a.prev_contacts = prev_contacts_;
+  a.prev_sep = prev_sep_, a.episode = episode_, a.actions = actions, a.step_mask = mask;
+  a.task = task_;
+  a.status = d_status_;
+  return a;
+}
+
+cudaError_t World::launch(uint32_t substeps, const float* actions, const uint8_t* mask) {
+  return launch_step(args(substeps, actions, mask), lanes_, envs_per_block_, stream_);
+}
+
+cudaError_t World::step(const float* actions, uint32_t substeps, bool async) {
+  const auto t0 = std::chrono::steady_clock::now();
+  // substeps == 0 selects the adaptive count, which stays at the configured value
+  // (its violation probe reads a constraint field no kernel writes, world.zig:767-791)
+  const uint32_t ns = substeps == 0 ? cfg_.substeps : substeps;
+  const size_t na = size_t(cfg_.num_envs) * model_.A;
+  const float* dev_actions = d_actions_;
+  if (na > 0 && actions) {
+    cudaPointerAttributes pa;
+    if (cudaPointerGetAttributes(&pa, actions) == cudaSuccess &&
+        (pa.type == cudaMemoryTypeDevice || pa.type == cudaMemoryTypeManaged)) {
+      dev_actions = actions;  // already device-addressable: no copy
+    } else {
+      cudaGetLastError();
+      cudaError_t e = cudaMemcpyAsync(d_actions_, actions, na * sizeof(float), cudaMemcpyHostToDevice, stream_);
+      if (e != cudaSuccess) return e;
+    }
+  }
+  cudaError_t e = launch(ns, dev_actions, nullptr);
+  if (e != cudaSuccess) return e;
+  if (async) return cudaSuccess;
+  e = cudaStreamSynchronize(stream_);
+  if (e != cudaSuccess) return e;
+  if (cfg_.enable_profiling) {
+    prof_.total_step_ns =
+        float(std::chrono::duration_cast<std::chrono::nanoseconds>(std::chrono::steady_clock::now() - t0).count());
+    uint64_t total = 0;
+    std::vector<uint32_t> c(cfg_.num_envs);
+    cudaMemcpy(c.data(), counts, c.size() * 4, cudaMemcpyDefault);
+    for (uint32_t v : c) total += v;
+    prof_.num_contacts = uint32_t(total > 0xFFFFFFFFull ? 0xFFFFFFFFull : total);
+    prof_.num_active_constraints = model_.K * cfg_.num_envs;
+  } else {
+    prof_ = Profiling{};
+  }
+  return cudaSuccess;
+}
+
+cudaError_t World::step_subset(const float* actions, const uint8_t* mask, uint32_t substeps) {
+  const uint32_t E = cfg_.num_envs;
+  uint32_t active = 0;
+  for (uint32_t i = 0; i < E; ++i) active += mask[i] != 0;
+  if (active == 0) return cudaSuccess;
+  if (active == E) return step(actions, substeps);
+  cudaError_t e = cudaSuccess;
+  if (!prev_contacts_) {
+    e = device_buf(&prev_contacts_, size_t(E) * cfg_.max_contacts_per_env);
+    if (e != cudaSuccess) return e;
+  }
+  const uint32_t ns = substeps == 0 ? cfg_.substeps : substeps;
+  const size_t na = size_t(E) * model_.A;
+  if (na > 0) {
+    e = cudaMemcpyAsync(d_actions_, actions, na * sizeof(float), cudaMemcpyDefault, stream_);
+    if (e != cudaSuccess) return e;
+  }
+  e = cudaMemcpyAsync(d_mask_, mask, E, cudaMemcpyDefault, stream_);
+  if (e != cudaSuccess) return e;
+  e = launch(ns, d_actions_, d_mask_);
+  if (e != cudaSuccess) return e;
+  return cudaStreamSynchronize(stream_);
+}
+
+void World::reset(const uint8_t* mask) {
+  const uint32_t E = cfg_.num_envs;
+  const uint8_t* dm = nullptr;
+  if (mask) {
+    cudaMemcpyAsync(d_mask_, mask, E, cudaMemcpyDefault, stream_);
+    dm = d_mask_;
+  }
+  launch_reset(pos, quat, vel, angvel, jpos, jvel, d_init_, E, model_.B, model_.J, dm, stream_);
+  cudaMemsetAsync(counts, 0, size_t(E) * 4, stream_);  // all envs, world.zig:1313
+  cudaStreamSynchronize(stream_);
+}
+
+int World::set_positions(const float* p, const uint8_t* mask) {
+  const uint32_t E = cfg_.num_envs;
+  const uint8_t* dm = nullptr;
+  if (mask) {
+    cudaMemcpyAsync(d_mask_, mask, E, cudaMemcpyDefault, stream_);
+    dm = d_mask_;
+  }
+  float* staging = nullptr;
+  const size_t n = size_t(E) * model_.B * 4;
+  if (cudaMallocAsync(reinterpret_cast<void**>(&staging), n * 4, stream_) != cudaSuccess) return -5;
+  cudaMemcpyAsync(staging, p, n * 4, cudaMemcpyDefault, stream_);
+  launch_masked_copy(pos, staging, E, model_.B, dm, stream_);
+  cudaFreeAsync(staging, stream_);
+  return cudaStreamSynchronize(stream_) == cudaSuccess ? 0 : -4;
+}
+
+int World::set_velocities(const float* v, const uint8_t* mask) {
+  const uint32_t E = cfg_.num_envs;
+  const uint8_t* dm = nullptr;
+  if (mask) {
+    cudaMemcpyAsync(d_mask_, mask, E, cudaMemcpyDefault, stream_);
+    dm = d_mask_;
+  }
+  float* staging = nullptr;
+  const size_t n = size_t(E) * model_.B * 4;
+  if (cudaMallocAsync(reinterpret_cast<void**>(&staging), n * 4, stream_) != cudaSuccess) return -5;
+  cudaMemcpyAsync(staging, v, n * 4, cudaMemcpyDefault, stream_);
+  launch_masked_copy(vel, staging, E, model_.B, dm, stream_);
+  cudaFreeAsync(staging, stream_);
+  return cudaStreamSynchronize(stream_) == cudaSuccess ? 0 : -4;
+}
+
+int World::reset_to_state(const float* p, const float* q, const float* v, const float* w, const uint8_t* mask) {
+  const uint32_t E = cfg_.num_envs;
+  const uint8_t* dm = nullptr;
+  if (mask) {
+    cudaMemcpyAsync(d_mask_, mask, E, cudaMemcpyDefault, stream_);
+    dm = d_mask_;
+  }
+  const size_t n = size_t(E) * model_.B * 4;
+  float* staging = nullptr;
+  if (cudaMallocAsync(reinterpret_cast<void**>(&staging), n * 4, stream_) != cudaSuccess) return -5;
+  const float* srcs[4] = {p, q, v, w};
+  float* dsts[4] = {pos, quat, vel, angvel};
+  for (int k = 0; k < 4; ++k) {
+    if (!srcs[k]) continue;
+    cudaMemcpyAsync(staging, srcs[k], n * 4, cudaMemcpyDefault, stream_);
+    launch_masked_copy(dsts[k], staging, E, model_.B, dm, stream_);
+  }
+  cudaFreeAsync(staging, stream_);
+  cudaMemsetAsync(counts, 0, size_t(E) * 4, stream_);  // main.zig:383
+  return cudaStreamSynchronize(stream_) == cudaSuccess ? 0 : -4;
+}
+
+void World::set_gravity(float gx, float gy, float gz) {
+  gravity_[0] = gx, gravity_[1] = gy, gravity_[2] = gz;
+}
+
+int World::set_timestep(float ts) {
+  if (!(ts > 0)) return -6;
+  timestep_ = ts;
+  return 0;
+}
+
+int World::set_task(const DTask& t) {
+  if (t.enabled && t.body >= model_.B) return -6;
+  task_ = t;
+  return 0;
+}
+
+int World::set_launch(int lanes, int envs_per_block) {
+  if (lanes != 4 && lanes != 8 && lanes != 16 && lanes != 32) return -6;
+  const uint32_t env_bytes = env_smem_bytes(model_.B, model_.J, cfg_.max_contacts_per_env);
+  if (envs_per_block < 1 || lanes * envs_per_block > 256 ||
+      uint64_t(env_bytes) * envs_per_block > uint64_t(opt_in_smem(device_)))
+    return -6;
+  lanes_ = lanes;
+  envs_per_block_ = envs_per_block;
+  return 0;
+}
+
+cudaError_t World::synchronize() { return cudaStreamSynchronize(stream_); }
+
+}  // namespace zb

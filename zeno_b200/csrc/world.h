@@ -1,0 +1,124 @@
+// World runtime: owns the device model tables and the batched state of one world on
+// one GPU (the CUDA device current when the world is created), and drives the fused
+// step kernel.  Mirrors src/world/world.zig (World.init/step/stepSubset/reset/setters).
+#pragma once
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <string>
+
+#include "model.h"
+#include "zeno_types.h"
+
+namespace zb {
+
+struct WorldConfig {  // ZenoConfig fields the world uses (src/main.zig:75-86)
+  uint32_t num_envs = 1;
+  float timestep = 0.0f;  // 0: MJCF timestep
+  uint32_t contact_iterations = 4;
+  uint32_t max_contacts_per_env = 64;
+  uint64_t seed = 42;
+  uint32_t substeps = 1;
+  bool enable_profiling = false;
+};
+
+struct Profiling {  // ZenoProfilingData (src/main.zig:105-113)
+  float integrate_ns = 0, collision_broad_ns = 0, collision_narrow_ns = 0, constraint_solve_ns = 0,
+        total_step_ns = 0;
+  uint32_t num_contacts = 0, num_active_constraints = 0;
+};
+
+class World {
+ public:
+  // Returns nullptr and sets *err on failure.
+  static World* create(const Scene& sc, const WorldConfig& cfg, std::string* err);
+  ~World();
+
+  // World.step: actions may be host or device memory (E*A floats).  Synchronous unless
+  // async is set, in which case the caller synchronizes the world stream.
+  cudaError_t step(const float* actions, uint32_t substeps, bool async = false);
+  cudaError_t step_subset(const float* actions, const uint8_t* mask, uint32_t substeps);
+  void reset(const uint8_t* mask);
+  int reset_to_state(const float* pos, const float* quat, const float* vel, const float* angvel,
+                     const uint8_t* mask);
+  int set_positions(const float* pos, const uint8_t* mask);
+  int set_velocities(const float* vel, const uint8_t* mask);
+  void set_gravity(float gx, float gy, float gz);
+  int set_timestep(float ts);
+  int set_task(const DTask& t);
+  int set_launch(int lanes, int envs_per_block);
+  cudaError_t synchronize();
+  void set_stream(cudaStream_t s) { stream_ = s ? s : own_stream_; }
+  cudaStream_t stream() const { return stream_; }
+
+  const HostModel& model() const { return model_; }
+  const WorldConfig& config() const { return cfg_; }
+  float timestep() const { return timestep_; }
+  uint64_t memory_usage() const { return bytes_; }
+  int device() const { return device_; }
+  Profiling profiling() const { return prof_; }
+  void reset_profiling() { prof_ = Profiling{}; }
+  int lanes() const { return lanes_; }
+  int envs_per_block() const { return envs_per_block_; }
+
+  // ABI-visible state (managed memory: host and device addressable)
+  float* pos = nullptr;
+  float* quat = nullptr;
+  float* vel = nullptr;
+  float* angvel = nullptr;
+  float* acc = nullptr;
+  float* jpos = nullptr;
+  float* jvel = nullptr;
+  float* jtorque = nullptr;
+  float* obs = nullptr;
+  float* rewards = nullptr;
+  uint8_t* dones = nullptr;
+  Contact* contacts = nullptr;
+  uint32_t* counts = nullptr;
+
+ private:
+  World() = default;
+  StepArgs args(uint32_t substeps, const float* actions, const uint8_t* mask) const;
+  cudaError_t launch(uint32_t substeps, const float* actions, const uint8_t* mask);
+  template <class T>
+  cudaError_t managed(T** p, size_t n);
+  template <class T>
+  cudaError_t device_buf(T** p, size_t n);
+
+  Scene scene_;
+  HostModel model_;
+  WorldConfig cfg_;
+  float timestep_ = 0.0f;
+  float gravity_[3] = {0, 0, -9.81f};
+  int device_ = 0;
+  int lanes_ = 8;
+  int envs_per_block_ = 16;
+  uint64_t bytes_ = 0;
+  cudaStream_t own_stream_ = nullptr;
+  cudaStream_t stream_ = nullptr;
+  Profiling prof_;
+  DTask task_{};
+  // device model
+  DBody* d_bodies_ = nullptr;
+  uint32_t* d_jf_ = nullptr;
+  DJoint* d_joints_ = nullptr;
+  DGeom* d_geoms_ = nullptr;
+  DPair* d_pairs_ = nullptr;
+  DActuator* d_act_ = nullptr;
+  DSensor* d_sensors_ = nullptr;
+  DConstraint* d_cons_ = nullptr;
+  uint32_t* d_colors_ = nullptr;
+  uint32_t* d_subtree_ = nullptr;
+  float* d_init_ = nullptr;
+  // internal state
+  uint32_t* prev_counts_ = nullptr;
+  Contact* prev_contacts_ = nullptr;
+  uint8_t* prev_sep_ = nullptr;
+  uint32_t* episode_ = nullptr;
+  float* d_actions_ = nullptr;
+  uint8_t* d_mask_ = nullptr;
+  uint32_t* d_status_ = nullptr;
+  std::vector<void*> allocations_;
+};
+
+}  // namespace zb
