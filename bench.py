@@ -1,0 +1,322 @@
+"""Benchmark: Ant env-steps/s (16384 envs per GPU) and the step's HBM-roofline fraction.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload (BASELINE Ant config): the reference Ant model, dt 0.01 s, 4 substeps, 4 solver
+iterations, 64 contact slots per env, 16384 envs per GPU, actions U(-1, 1) drawn from a
+seeded generator, done = torso z outside [0.2, 1.0] with device-side masked reset and
+U(-0.1, 0.1) pose noise.  Synthetic inputs only; no datasets.
+
+One "step" is one World.step over all envs of a GPU (one fused kernel launch).  `value`
+is the whole-job throughput with actions already resident in HBM, timed with CUDA
+events on the launching stream around each step; L2 is flushed (a 256 MiB write)
+between timed steps, outside the events.  `e2e` is the same metric through the
+reference-facing API with host buffers: per step, actions are copied from pinned host
+memory by zeno_world_step and observations, rewards and dones are read back into host
+arrays.  Multi-GPU runs are one process per GPU (torchrun); environments are sharded with
+no collective on the step path (weak scaling); timings are the max over ranks.
+
+--impl reference times the reference algorithm on the host CPU cores: the reference
+implementation cannot run here (its step exists only as Metal shaders), so the CPU
+restatement in oracle/ is timed with all host threads on a bounded sample of envs.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+ENVS_PER_GPU = 16384
+SUBSTEPS = 4
+ITERATIONS = 4
+MAX_CONTACTS = 64
+METRIC = "env-steps/sec (whole box, Ant 16384 envs/GPU)"
+UNIT = "env-steps/s"
+
+
+def algorithmic_bytes_per_env_step(B, J, A, obs, K, S):
+    """Bytes one env-step must move to and from HBM (per-unit figure of the roofline):
+    actions R, pos/quat/vel/angvel R+W, accel W, joint pos/vel/torque W, observations W,
+    reward+done W, contact count and previous count R+W, S contact slots R+W, and the
+    constraint multipliers (lambda, lambda_prev) R+W."""
+    return 4 * A + 128 * B + 16 * B + 12 * J + 4 * obs + 5 + 16 + 128 * S + 16 * K
+
+
+class ClockSampler:
+    """Samples SM clocks and throttle reasons with nvidia-smi during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.device}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self._t = threading.Thread(target=self._read, daemon=True)
+            self._t.start()
+        except FileNotFoundError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def cpu_baseline(xml, steps, sample_envs, threads):
+    """The CPU oracle (reference algorithm restated) on a bounded sample of envs."""
+    from oracle.zeno_oracle import OracleWorld
+    o = OracleWorld(xml, num_envs=sample_envs, substeps=SUBSTEPS, contact_iterations=ITERATIONS,
+                    max_contacts_per_env=MAX_CONTACTS)
+    o.set_task(body=1, z_min=0.2, z_max=1.0, auto_reset=True, noise=0.1, seed=1)
+    rng = np.random.default_rng(0)
+    acts = rng.uniform(-1, 1, size=(steps, sample_envs, 8)).astype(np.float32)
+    o.run(acts[:1], threads=threads)  # warm-up
+    t0 = time.perf_counter()
+    o.run(acts, threads=threads)
+    dt = time.perf_counter() - t0
+    return steps * sample_envs / dt, dt
+
+
+def run_reference(args, rank):
+    if rank != 0:
+        return 0
+    from zeno_b200 import scenes
+    threads = os.cpu_count() or 1
+    sample = 2048
+    xml = scenes.ant()
+    val, dt = cpu_baseline(xml, args.warmup + args.steps, sample, threads)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": val, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": 1000.0 * sample / val, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "ant", "envs_per_gpu": ENVS_PER_GPU, "substeps": SUBSTEPS,
+                   "contact_iterations": ITERATIONS, "max_contacts_per_env": MAX_CONTACTS,
+                   "sample_envs_per_step": sample},
+        "cpu_baseline": {"value": val, "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": f"{sample} Ant envs x {args.warmup + args.steps} steps on {threads} threads "
+                                   f"({dt:.1f} s); the reference step exists only as Metal shaders, so the CPU "
+                                   "restatement in oracle/ stands in for it"},
+        "e2e": {"value": val, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_e2e(w, pinned, acts, args, E, A, dist, barrier, world_size, torch):
+    """Same metric through the reference-facing API: zeno_world_step with host actions
+    (pinned), then observations, rewards and dones read into host arrays."""
+    pinned.copy_(acts[args.warmup:].cpu())
+    host_acts = pinned.numpy()
+    w.set_stream(0)  # the public API runs on the world's own stream
+    for s in range(2):
+        w.step(host_acts[s])
+        w.get_observations(), w.get_rewards(), w.get_dones()
+    barrier()
+    e0 = time.perf_counter()
+    for s in range(args.steps):
+        w.step(host_acts[s])
+        obs = w.get_observations()
+        rew = w.get_rewards()
+        don = w.get_dones()
+    e_local = time.perf_counter() - e0
+    te = torch.tensor([e_local], dtype=torch.float64, device="cuda")
+    if dist:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_value = world_size * E * args.steps / float(te.item())
+    h2d = E * A * 4
+    d2h = obs.nbytes + rew.nbytes + don.nbytes
+    return e2e_value, h2d, int(d2h)
+
+
+def run_ours(args, rank, world_size, local_rank):
+    import torch
+
+    import zeno_b200
+    from zeno_b200 import scenes
+
+    torch.cuda.set_device(local_rank)
+    dist = None
+    if world_size > 1:
+        import torch.distributed as dist_
+        from datetime import timedelta
+        dist_.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local_rank))
+        dist = dist_
+
+    E = args.envs
+    xml = scenes.ant()
+    w = zeno_b200.ZenoWorld(mjcf_string=xml, num_envs=E, substeps=SUBSTEPS, contact_iterations=ITERATIONS,
+                            max_contacts_per_env=MAX_CONTACTS)
+    w.set_task(body=1, z_min=0.2, z_max=1.0, auto_reset=True, noise=0.1, seed=1, env_offset=rank * E)
+    # a dedicated stream: the world launches on it and the timing events record on it
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    w.set_stream(stream.cuda_stream)
+    A = w.action_dim
+
+    # inputs resident in HBM before timing: one action batch per step
+    gen = torch.Generator(device="cuda").manual_seed(1234 + rank)
+    total = args.warmup + args.steps
+    acts = torch.rand((total, E, A), device="cuda", generator=gen, dtype=torch.float32) * 2 - 1
+    flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device="cuda")  # 256 MiB > 126 MB L2
+
+    def barrier():
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for s in range(args.warmup):
+        w.step_async(acts[s])
+    barrier()
+
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    with ClockSampler(local_rank) as clk:
+        barrier()
+        wall0 = time.perf_counter()
+        for s in range(args.steps):
+            flush.zero_()
+            starts[s].record(stream)
+            w.step_async(acts[args.warmup + s])
+            ends[s].record(stream)
+        barrier()
+        wall = time.perf_counter() - wall0
+    step_ms = [starts[s].elapsed_time(ends[s]) for s in range(args.steps)]
+    t_local = sum(step_ms) / 1000.0
+    t = torch.tensor([t_local], dtype=torch.float64, device="cuda")
+    if dist:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    t_max = float(t.item())
+    value = world_size * E * args.steps / t_max
+    dones_seen = int(w.get_dones().sum())
+
+    # ---- end to end through the reference-facing API, host buffers ----
+    e2e_value, h2d, d2h = None, E * A * 4, 0
+    if args.no_e2e:
+        pinned = None
+    else:
+        pinned = torch.empty((args.steps, E, A), dtype=torch.float32, pin_memory=True)
+    if pinned is not None:
+        e2e_value, h2d, d2h = run_e2e(w, pinned, acts, args, E, A, dist, barrier, world_size, torch)
+
+    if rank == 0:
+        st = w.get_info()
+        counts = w.get_contact_counts()
+        obs_dim, B, J = w.obs_dim, w.num_bodies, w.num_joints
+        K = 24
+        bpe = algorithmic_bytes_per_env_step(B, J, A, obs_dim, K, MAX_CONTACTS)
+        mean_ms = statistics.mean(step_ms)
+        achieved = bpe * E / (mean_ms / 1000.0) / 1e9
+        peak, peak_kind = measured_peaks()
+        traffic = None
+        tf = ROOT / "profiles" / "ant_step_traffic.json"
+        if tf.exists():
+            traffic = json.loads(tf.read_text()).get("dram_bytes_per_launch")
+        cpu_val, cpu_dt = cpu_baseline(xml, 10, 1024, os.cpu_count() or 1) if not args.no_cpu else (None, 0)
+        clocks = clk.summary()
+        lanes, epb = w.get_launch()
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world_size, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": t_max * 1000.0 / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "ant", "envs_per_gpu": E, "substeps": SUBSTEPS, "contact_iterations": ITERATIONS,
+                       "max_contacts_per_env": MAX_CONTACTS, "timestep": st["timestep"],
+                       "task": "done: torso z not in [0.2, 1.0], device auto-reset, U(-0.1,0.1) noise",
+                       "actions": "U(-1,1), resident in HBM", "l2": "flushed (256 MiB write) between timed steps",
+                       "launch": {"lanes_per_env": lanes, "envs_per_block": epb},
+                       "parallelism": f"env-sharded x{world_size}, no collective on the step path"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": traffic, "peak_kind": peak_kind,
+                         "bytes_per_env_step": bpe, "kernel": "zb::step_kernel<8>",
+                         "mean_launch_ms": mean_ms},
+            "cpu_baseline": {"value": cpu_val, "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
+                             "sample": f"1024 Ant envs x 10 steps, oracle on {os.cpu_count()} threads ({cpu_dt:.1f} s)"},
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": int(d2h)},
+            "gpu_launches": args.steps,
+            "clocks": clocks,
+            "wall_s_timed_region": wall,
+            "dones_in_last_step": dones_seen,
+            "mean_contact_count": float(counts.mean()),
+        }
+        print(json.dumps(line), flush=True)
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline sample")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end (host buffer) leg")
+    ap.add_argument("--envs", type=int, default=ENVS_PER_GPU, help="environments per GPU")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    rank = int(os.environ.get("RANK", "0"))
+    world_size = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        return run_reference(args, rank)
+    return run_ours(args, rank, world_size, local_rank)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

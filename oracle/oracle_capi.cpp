@@ -39,9 +39,13 @@ int zo_step(void* h, const float* actions, uint32_t substeps) {
 }
 
 int zo_run(void* h, const float* actions, uint32_t nsteps, uint32_t substeps) {
+  return zo_run_threads(h, actions, nsteps, substeps, 1);
+}
+
+int zo_run_threads(void* h, const float* actions, uint32_t nsteps, uint32_t substeps, uint32_t threads) {
   if (!h) return -1;
   World* w = static_cast<World*>(h);
-  for (uint32_t s = 0; s < nsteps; s++) world_step(w, actions + size_t(s) * w->E * w->A, substeps);
+  for (uint32_t s = 0; s < nsteps; s++) world_step(w, actions + size_t(s) * w->E * w->A, substeps, threads);
   return 0;
 }
 

@@ -184,7 +184,7 @@ struct World {
 };
 
 bool world_init(World* w, const Scene& scene, const Config& cfg);
-void world_step(World* w, const float* actions, uint32_t substeps);
+void world_step(World* w, const float* actions, uint32_t substeps, uint32_t threads = 1);
 int world_step_subset(World* w, const float* actions, const uint8_t* mask, uint32_t substeps);
 void world_reset(World* w, const uint8_t* mask);
 void world_apply_task(World* w, const uint8_t* mask);

@@ -15,6 +15,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstring>
+#include <thread>
 
 #include "oracle_math.h"
 #include "oracle_model.h"
@@ -1087,15 +1088,27 @@ bool world_init(World* w, const Scene& scene, const Config& cfg) {
   return true;
 }
 
-// World.step (world.zig:694-792) for all environments
-void world_step(World* w, const float* actions, uint32_t substeps) {
+// World.step (world.zig:694-792) for all environments.  Environments never share
+// mutable state, so `threads` > 1 splits them across host threads (same results).
+void world_step(World* w, const float* actions, uint32_t substeps, uint32_t threads) {
   const uint32_t E = w->E, B = w->B;
   if (actions) std::memcpy(w->actions.data(), actions, sizeof(float) * size_t(E) * w->A);
   uint32_t ns = substeps == 0 ? w->adaptive_substeps : substeps;
   w->params.dt = w->timestep / float(std::max(ns, 1u));
   w->prev_vel = w->vel;
-  for (uint32_t s = 0; s < ns; s++)
-    for (uint32_t e = 0; e < E; e++) substep_env(w, e);
+  if (threads <= 1) {
+    for (uint32_t s = 0; s < ns; s++)
+      for (uint32_t e = 0; e < E; e++) substep_env(w, e);
+  } else {
+    std::vector<std::thread> pool;
+    for (uint32_t t = 0; t < threads; t++)
+      pool.emplace_back([w, t, threads, E, ns]() {
+        const uint32_t e0 = uint32_t(uint64_t(E) * t / threads), e1 = uint32_t(uint64_t(E) * (t + 1) / threads);
+        for (uint32_t e = e0; e < e1; e++)
+          for (uint32_t s = 0; s < ns; s++) substep_env(w, e);
+      });
+    for (auto& th : pool) th.join();
+  }
   float inv_step = w->timestep > 0 ? 1.0f / w->timestep : 0.0f;
   for (size_t i = 0; i < size_t(E) * B; i++) {
     w->acc[i * 4 + 0] = (w->vel[i * 4 + 0] - w->prev_vel[i * 4 + 0]) * inv_step;

@@ -49,6 +49,8 @@ void zo_dims(void* h, uint32_t out[10]);
 void* zo_buffer(void* h, const char* name, size_t* nbytes);
 // Run n steps with per-step actions drawn by the caller (actions: n*E*A floats).
 int zo_run(void* h, const float* actions, uint32_t nsteps, uint32_t substeps);
+// Same, with environments split across `threads` host threads (identical results).
+int zo_run_threads(void* h, const float* actions, uint32_t nsteps, uint32_t substeps, uint32_t threads);
 
 #ifdef __cplusplus
 }

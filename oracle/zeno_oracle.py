@@ -72,6 +72,7 @@ def lib() -> ctypes.CDLL:
         L.zo_destroy.argtypes = [vp]
         L.zo_step.argtypes = [vp, f32p, ctypes.c_uint32]
         L.zo_run.argtypes = [vp, f32p, ctypes.c_uint32, ctypes.c_uint32]
+        L.zo_run_threads.argtypes = [vp, f32p, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32]
         L.zo_step_subset.argtypes = [vp, f32p, u8p, ctypes.c_uint32]
         L.zo_reset.argtypes = [vp, u8p]
         L.zo_reset_to_state.argtypes = [vp, f32p, f32p, f32p, f32p, u8p]
@@ -150,10 +151,10 @@ class OracleWorld:
         a = np.ascontiguousarray(actions, dtype=np.float32).ravel()
         lib().zo_step(self._h, _fptr(a), substeps)
 
-    def run(self, actions: np.ndarray, substeps: int = 0) -> None:
-        """actions: (nsteps, E, A)"""
+    def run(self, actions: np.ndarray, substeps: int = 0, threads: int = 1) -> None:
+        """actions: (nsteps, E, A); environments split across `threads` host threads."""
         a = np.ascontiguousarray(actions, dtype=np.float32)
-        lib().zo_run(self._h, _fptr(a), a.shape[0], substeps)
+        lib().zo_run_threads(self._h, _fptr(a), a.shape[0], substeps, threads)
 
     def step_subset(self, actions, mask, substeps=0):
         a = np.ascontiguousarray(actions, dtype=np.float32).ravel()
