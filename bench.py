@@ -53,6 +53,22 @@ def algorithmic_bytes_per_env_step(B, J, A, obs, K, S):
     return 4 * A + 128 * B + 16 * B + 12 * J + 4 * obs + 5 + 16 + 128 * S + 16 * K
 
 
+def shard_env_offset(rank: int, envs_per_gpu: int) -> int:
+    """Global index of a rank's first env.  Envs are sharded in contiguous blocks; the
+    offset keys the reset-noise generator, so an env's trajectory does not depend on how
+    many GPUs share the job."""
+    return rank * envs_per_gpu
+
+
+def reduce_max(value: float, dist, device) -> float:
+    """Max over ranks (the timing rule for multi-GPU runs)."""
+    import torch
+    t = torch.tensor([value], dtype=torch.float64, device=device)
+    if dist is not None:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
 class ClockSampler:
     """Samples SM clocks and throttle reasons with nvidia-smi during the timed region."""
 
@@ -172,10 +188,7 @@ def run_e2e(w, pinned, acts, args, E, A, dist, barrier, world_size, torch):
         rew = w.get_rewards()
         don = w.get_dones()
     e_local = time.perf_counter() - e0
-    te = torch.tensor([e_local], dtype=torch.float64, device="cuda")
-    if dist:
-        dist.all_reduce(te, op=dist.ReduceOp.MAX)
-    e2e_value = world_size * E * args.steps / float(te.item())
+    e2e_value = world_size * E * args.steps / reduce_max(e_local, dist, "cuda")
     h2d = E * A * 4
     d2h = obs.nbytes + rew.nbytes + don.nbytes
     return e2e_value, h2d, int(d2h)
@@ -199,7 +212,8 @@ def run_ours(args, rank, world_size, local_rank):
     xml = scenes.ant()
     w = zeno_b200.ZenoWorld(mjcf_string=xml, num_envs=E, substeps=SUBSTEPS, contact_iterations=ITERATIONS,
                             max_contacts_per_env=MAX_CONTACTS)
-    w.set_task(body=1, z_min=0.2, z_max=1.0, auto_reset=True, noise=0.1, seed=1, env_offset=rank * E)
+    w.set_task(body=1, z_min=0.2, z_max=1.0, auto_reset=True, noise=0.1, seed=1,
+               env_offset=shard_env_offset(rank, E))
     # a dedicated stream: the world launches on it and the timing events record on it
     stream = torch.cuda.Stream()
     torch.cuda.set_stream(stream)
@@ -236,10 +250,7 @@ def run_ours(args, rank, world_size, local_rank):
         wall = time.perf_counter() - wall0
     step_ms = [starts[s].elapsed_time(ends[s]) for s in range(args.steps)]
     t_local = sum(step_ms) / 1000.0
-    t = torch.tensor([t_local], dtype=torch.float64, device="cuda")
-    if dist:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    t_max = float(t.item())
+    t_max = reduce_max(t_local, dist, "cuda")
     value = world_size * E * args.steps / t_max
     dones_seen = int(w.get_dones().sum())
 

@@ -159,3 +159,21 @@ void* zo_buffer(void* h, const char* name, size_t* nbytes) {
 }
 
 }  // extern "C"
+
+// ---- helpers for the known-answer tests ----
+#include "oracle_math.h"
+extern "C" {
+float zo_atan2(float y, float x) { return zo::atan2_r(y, x); }
+float zo_asin(float x) { return zo::asin_r(x); }
+// Generalised inverse mass of a contact or positional constraint, the expression the
+// solvers use (all_shaders.metal:1683-1687; xpbd.zig:495-529 computeEffectiveMass):
+// w = 1/m_a + (r_a x n)^T I_a^-1 (r_a x n) + 1/m_b + (r_b x n)^T I_b^-1 (r_b x n)
+float zo_effective_mass(float ima, float imb, const float* Ia, const float* Ib, const float* ra, const float* rb,
+                        const float* n) {
+  using namespace zo;
+  F3 N{n[0], n[1], n[2]}, RA{ra[0], ra[1], ra[2]}, RB{rb[0], rb[1], rb[2]};
+  F3 IA{Ia[0], Ia[1], Ia[2]}, IB{Ib[0], Ib[1], Ib[2]};
+  F3 rna = cross(RA, N), rnb = cross(RB, N);
+  return (ima + dot(mulv(rna, IA), rna)) + (imb + dot(mulv(rnb, IB), rnb));
+}
+}

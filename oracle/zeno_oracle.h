@@ -55,3 +55,14 @@ int zo_run_threads(void* h, const float* actions, uint32_t nsteps, uint32_t subs
 #ifdef __cplusplus
 }
 #endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+float zo_atan2(float y, float x);
+float zo_asin(float x);
+float zo_effective_mass(float ima, float imb, const float* Ia, const float* Ib, const float* ra, const float* rb,
+                        const float* n);
+#ifdef __cplusplus
+}
+#endif
