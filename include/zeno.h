@@ -215,6 +215,20 @@ const void* zeno_world_model_table(ZenoWorldHandle world, const char* name, uint
 /* Message of the last failed zeno_world_create* on this thread ("" if none). */
 const char* zeno_last_error(void);
 
+/* No counterpart in the reference.  zeno_world_reset_to_state without any device
+ * allocation, for callers that cannot allocate device memory at that point (their HBM is
+ * already reserved by another allocator, or they cannot risk an allocation blocking or
+ * failing mid-episode).  The host arrays are staged through a fixed 16 MiB array in the
+ * library's static device memory, so num_envs * num_bodies must be <= 1,048,576; larger
+ * worlds get ZENO_INVALID_ARGUMENT and a message in zeno_last_error().  The array is
+ * shared by all calls and worlds on a device (overlapping calls on the GPU race; serialize
+ * them) and is held by every GPU that loads the library until exit.  The first call on a
+ * device resolves the array's address; make it before any stream capture.  Results are
+ * identical to zeno_world_reset_to_state. */
+int zeno_world_reset_to_state_noalloc(ZenoWorldHandle world, const float* positions, const float* quaternions,
+                                      const float* velocities, const float* angular_velocities,
+                                      const uint8_t* env_mask);
+
 /* Host-only model build (no GPU needed): parse MJCF text and build the model tables;
  * zeno_model_table takes the same names as zeno_world_model_table. */
 void* zeno_model_create_from_string(const char* mjcf_string);

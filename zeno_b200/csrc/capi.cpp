@@ -37,6 +37,10 @@ ZenoWorldHandle create_world(const zb::Scene& sc, const ZenoConfig* c) {
 int cuda_status(cudaError_t e) { return e == cudaSuccess ? ZENO_SUCCESS : ZENO_METAL_ERROR; }
 }  // namespace
 
+namespace zb {
+void set_last_error(const std::string& msg) { g_last_error = msg; }
+}  // namespace zb
+
 extern "C" {
 
 ZenoWorldHandle zeno_world_create(const char* mjcf_path, const ZenoConfig* config) {

@@ -292,6 +292,26 @@ int World::reset_to_state(const float* p, const float* q, const float* v, const 
   return cudaStreamSynchronize(stream_) == cudaSuccess ? 0 : -4;
 }
 
+int World::reset_to_state_staged(const float* p, const float* q, const float* v, const float* w, const uint8_t* mask,
+                                 float* staging) {
+  const uint32_t E = cfg_.num_envs;
+  const uint8_t* dm = nullptr;
+  if (mask) {
+    if (cudaMemcpyAsync(d_mask_, mask, E, cudaMemcpyDefault, stream_) != cudaSuccess) return -4;
+    dm = d_mask_;
+  }
+  const size_t n = size_t(E) * model_.B * 4;
+  const float* srcs[4] = {p, q, v, w};
+  float* dsts[4] = {pos, quat, vel, angvel};
+  for (int k = 0; k < 4; ++k) {
+    if (!srcs[k]) continue;
+    if (cudaMemcpyAsync(staging, srcs[k], n * 4, cudaMemcpyDefault, stream_) != cudaSuccess) return -4;
+    if (launch_masked_copy(dsts[k], staging, E, model_.B, dm, stream_) != cudaSuccess) return -4;
+  }
+  if (cudaMemsetAsync(counts, 0, size_t(E) * 4, stream_) != cudaSuccess) return -4;  // main.zig:383
+  return cudaStreamSynchronize(stream_) == cudaSuccess ? 0 : -4;
+}
+
 void World::set_gravity(float gx, float gy, float gz) {
   gravity_[0] = gx, gravity_[1] = gy, gravity_[2] = gz;
 }

@@ -41,6 +41,10 @@ class World {
   void reset(const uint8_t* mask);
   int reset_to_state(const float* pos, const float* quat, const float* vel, const float* angvel,
                      const uint8_t* mask);
+  // reset_to_state staged through caller-provided device memory of at least
+  // num_envs * num_bodies float4 (no allocation; used by the no-allocation entry point).
+  int reset_to_state_staged(const float* pos, const float* quat, const float* vel, const float* angvel,
+                            const uint8_t* mask, float* staging);
   int set_positions(const float* pos, const uint8_t* mask);
   int set_velocities(const float* vel, const uint8_t* mask);
   void set_gravity(float gx, float gy, float gz);
