@@ -7,7 +7,8 @@ iterations, 64 contact slots per env, 16384 envs per GPU, actions U(-1, 1) drawn
 seeded generator, done = torso z outside [0.2, 1.0] with device-side masked reset and
 U(-0.1, 0.1) pose noise.  Synthetic inputs only; no datasets.
 
-One "step" is one World.step over all envs of a GPU (one fused kernel launch).  `value`
+One "step" is one World.step over all envs of a GPU (one fused kernel launch, plus the
+hand-over launch that steps environments the fast kernel could not represent).  `value`
 is the whole-job throughput with actions already resident in HBM, timed with CUDA
 events on the launching stream around each step; L2 is flushed (a 256 MiB write)
 between timed steps, outside the events.  `e2e` is the same metric through the
@@ -38,6 +39,8 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 ENVS_PER_GPU = 16384
+ACTION_RING = 64   # distinct pre-generated action batches, resident in HBM, cycled over the steps
+E2E_STEPS = 200    # steps of the end-to-end leg
 SUBSTEPS = 4
 ITERATIONS = 4
 MAX_CONTACTS = 64
@@ -85,7 +88,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.device}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                 "-lms", "50"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self._t = threading.Thread(target=self._read, daemon=True)
             self._t.start()
         except FileNotFoundError:
@@ -121,6 +124,19 @@ class ClockSampler:
                     reasons.add(n)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
                 "samples": len(sm)}
+
+
+def dram_bytes_per_launch(kernel: str, envs: int):
+    """DRAM bytes (read + write) per launch of `kernel` from the committed ncu summary
+    (profiles/step_traffic.md: a row `| kernel | envs | dram_bytes_per_launch |`), scaled to
+    `envs` environments (traffic is per environment), or None."""
+    import re
+    for f in sorted((ROOT / "profiles").glob("*_traffic.md")):
+        for line in f.read_text().splitlines():
+            m = re.match(r"\|\s*(\S+)\s*\|\s*(\d+)\s*\|\s*([\d.]+)\s*\|", line)
+            if m and m.group(1) == kernel:
+                return float(m.group(3)) * envs / int(m.group(2))
+    return None
 
 
 def measured_peaks():
@@ -174,21 +190,23 @@ def run_reference(args, rank):
 def run_e2e(w, pinned, acts, args, E, A, dist, barrier, world_size, torch):
     """Same metric through the reference-facing API: zeno_world_step with host actions
     (pinned), then observations, rewards and dones read into host arrays."""
-    pinned.copy_(acts[args.warmup:].cpu())
+    pinned.copy_(acts.cpu())
     host_acts = pinned.numpy()
+    ring = host_acts.shape[0]
+    steps = min(args.steps, E2E_STEPS)
     w.set_stream(0)  # the public API runs on the world's own stream
     for s in range(2):
         w.step(host_acts[s])
         w.get_observations(), w.get_rewards(), w.get_dones()
     barrier()
     e0 = time.perf_counter()
-    for s in range(args.steps):
-        w.step(host_acts[s])
+    for s in range(steps):
+        w.step(host_acts[s % ring])
         obs = w.get_observations()
         rew = w.get_rewards()
         don = w.get_dones()
     e_local = time.perf_counter() - e0
-    e2e_value = world_size * E * args.steps / reduce_max(e_local, dist, "cuda")
+    e2e_value = world_size * E * steps / reduce_max(e_local, dist, "cuda")
     h2d = E * A * 4
     d2h = obs.nbytes + rew.nbytes + don.nbytes
     return e2e_value, h2d, int(d2h)
@@ -223,7 +241,8 @@ def run_ours(args, rank, world_size, local_rank):
     # inputs resident in HBM before timing: one action batch per step
     gen = torch.Generator(device="cuda").manual_seed(1234 + rank)
     total = args.warmup + args.steps
-    acts = torch.rand((total, E, A), device="cuda", generator=gen, dtype=torch.float32) * 2 - 1
+    ring = min(total, ACTION_RING)  # distinct action batches, cycled
+    acts = torch.rand((ring, E, A), device="cuda", generator=gen, dtype=torch.float32) * 2 - 1
     flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device="cuda")  # 256 MiB > 126 MB L2
 
     def barrier():
@@ -233,7 +252,7 @@ def run_ours(args, rank, world_size, local_rank):
         torch.cuda.synchronize()
 
     for s in range(args.warmup):
-        w.step_async(acts[s])
+        w.step_async(acts[s % ring])
     barrier()
 
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
@@ -244,7 +263,7 @@ def run_ours(args, rank, world_size, local_rank):
         for s in range(args.steps):
             flush.zero_()
             starts[s].record(stream)
-            w.step_async(acts[args.warmup + s])
+            w.step_async(acts[(args.warmup + s) % ring])
             ends[s].record(stream)
         barrier()
         wall = time.perf_counter() - wall0
@@ -259,7 +278,7 @@ def run_ours(args, rank, world_size, local_rank):
     if args.no_e2e:
         pinned = None
     else:
-        pinned = torch.empty((args.steps, E, A), dtype=torch.float32, pin_memory=True)
+        pinned = torch.empty((ring, E, A), dtype=torch.float32, pin_memory=True)
     if pinned is not None:
         e2e_value, h2d, d2h = run_e2e(w, pinned, acts, args, E, A, dist, barrier, world_size, torch)
 
@@ -272,13 +291,11 @@ def run_ours(args, rank, world_size, local_rank):
         mean_ms = statistics.mean(step_ms)
         achieved = bpe * E / (mean_ms / 1000.0) / 1e9
         peak, peak_kind = measured_peaks()
-        traffic = None
-        tf = ROOT / "profiles" / "ant_step_traffic.json"
-        if tf.exists():
-            traffic = json.loads(tf.read_text()).get("dram_bytes_per_launch")
+        lanes, epb = w.get_launch()
+        kernel = "zb::fast_step_kernel" if lanes == 1 else f"zb::step_kernel<{lanes}>"
+        traffic = dram_bytes_per_launch(kernel, E)
         cpu_val, cpu_dt = cpu_baseline(xml, 10, 1024, os.cpu_count() or 1) if not args.no_cpu else (None, 0)
         clocks = clk.summary()
-        lanes, epb = w.get_launch()
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world_size, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": t_max * 1000.0 / args.steps, "higher_is_better": True,
@@ -291,12 +308,14 @@ def run_ours(args, rank, world_size, local_rank):
                        "parallelism": f"env-sharded x{world_size}, no collective on the step path"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic, "peak_kind": peak_kind,
-                         "bytes_per_env_step": bpe, "kernel": "zb::step_kernel<8>",
+                         "bytes_per_env_step": bpe, "kernel": kernel,
                          "mean_launch_ms": mean_ms},
             "cpu_baseline": {"value": cpu_val, "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
                              "sample": f"1024 Ant envs x 10 steps, oracle on {os.cpu_count()} threads ({cpu_dt:.1f} s)"},
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": int(d2h)},
-            "gpu_launches": args.steps,
+            # per step: the step kernel, plus (environment-per-lane kernel) the hand-over
+            # launch of the general kernel, which exits at once when nothing was handed over
+            "gpu_launches": args.steps * (2 if lanes == 1 else 1),
             "clocks": clocks,
             "wall_s_timed_region": wall,
             "dones_in_last_step": dones_seen,
@@ -312,7 +331,7 @@ def run_ours(args, rank, world_size, local_rank):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--steps", type=int, default=1000)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline sample")

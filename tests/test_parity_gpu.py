@@ -11,7 +11,9 @@ statistical 1000-step comparison is checked as well."""
 import numpy as np
 import pytest
 
+from oracle.zeno_oracle import OracleWorld
 from parity import CONFIGS, actions, diff_report, make_pair, product_state
+from zeno_b200 import ZenoWorld, scenes
 
 pytestmark = pytest.mark.gpu
 
@@ -157,12 +159,14 @@ def test_task_extension_bit_exact(auto_reset):
     assert saw_done
 
 
-@pytest.mark.parametrize("lanes,epb", [(4, 8), (8, 4), (16, 2), (32, 1)])
+@pytest.mark.parametrize("lanes,epb", [(1, 32), (1, 7), (1, 1), (4, 8), (8, 4), (16, 2), (32, 1)])
 def test_launch_shapes_agree(lanes, epb):
-    """Every launch shape computes the same bits (the schedule is deterministic)."""
+    """Every launch shape of both kernels computes the same bits: lanes 1 is the
+    environment-per-lane kernel, 4..32 the general kernel."""
     E = 13
     w, o, c = make_pair("ant", E)
     w.set_launch(lanes, epb)
+    assert w.get_launch() == (lanes, epb)
     rng = np.random.default_rng(2)
     acts = actions(rng, 5, E, w.action_dim, 1.0)
     for s in range(5):
@@ -196,3 +200,47 @@ def test_full_size_ant_sampled_envs_and_determinism():
     ref = o.state()
     got = {k: v[sample] for k, v in runs[0].items()}
     assert not diff_report(got, ref)
+
+
+@pytest.mark.parametrize("name", ["ant", "humanoid", "cartpole", "pendulum", "pendulum_asset"])
+def test_default_kernel_is_environment_per_lane(name):
+    """Every scene of the parity suite runs on the environment-per-lane kernel by default."""
+    w, _, _ = make_pair(name, 4)
+    assert w.get_launch()[0] == 1
+
+
+def test_large_scene_uses_general_kernel():
+    """A model beyond the constant-bank capacities (64 spheres, 2080 candidate pairs)
+    falls back to the general kernel and still matches the oracle bit for bit."""
+    xml = scenes.collision_stress(0)
+    w = ZenoWorld(mjcf_string=xml, num_envs=3, substeps=2)
+    o = OracleWorld(xml, num_envs=3, substeps=2)
+    assert w.get_launch()[0] >= 4
+    none = np.zeros((3, 0), np.float32)
+    for _ in range(3):
+        w.step(none)
+        o.step(none)
+    assert not diff_report(product_state(w), o.state())
+
+
+def test_hand_over_to_general_kernel():
+    """An environment whose stored contact list the fast kernel cannot represent (a slot
+    tuple that is not a broad-phase candidate) is stepped by the general kernel instead;
+    the result equals running the general kernel on every environment, and the hand-over
+    list is cleared so later steps are unaffected."""
+    E = 9
+    xml = CONFIGS["ant"]["xml"]()
+    rng = np.random.default_rng(5)
+    acts = actions(rng, 6, E, 8, 1.0)
+    runs = []
+    for lanes, epb in ((1, 32), (8, 4)):
+        w = ZenoWorld(mjcf_string=xml, num_envs=E, substeps=4)
+        w.set_launch(lanes, epb)
+        for s in range(3):
+            w.step(acts[s])
+        c = w.get_contacts()  # zero-copy view of the contact buffer
+        c["indices"][4, 0] = (1, 1, 1, 1)  # geom 1 with itself: not a candidate pair
+        for s in range(3, 6):
+            w.step(acts[s])
+        runs.append(product_state(w))
+    assert not diff_report(runs[0], runs[1])

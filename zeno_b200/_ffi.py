@@ -183,7 +183,7 @@ def model_tables(mjcf_string: str) -> Dict[str, bytes]:
     try:
         out = {}
         n = ffi.new("uint64_t*")
-        for name in ("bodies", "joints", "geoms", "actuators", "sensors", "constraints", "color_ranges"):
+        for name in ("bodies", "joints", "geoms", "actuators", "sensors", "constraints", "color_ranges", "pairs"):
             p = _lib.zeno_model_table(h, name.encode(), n)
             out[name] = bytes(ffi.buffer(p, n[0])) if p != ffi.NULL and n[0] else b""
         return out
@@ -243,9 +243,12 @@ class ZenoWorld:
 
     def __del__(self):
         h = getattr(self, "_handle", None)
-        if h is not None and h != ffi.NULL:
-            _lib.zeno_world_destroy(h)
-            self._handle = ffi.NULL
+        try:
+            if h is not None and h != ffi.NULL:
+                _lib.zeno_world_destroy(h)
+                self._handle = ffi.NULL
+        except Exception:  # interpreter teardown: cffi may already be gone
+            pass
 
     # ---- dimensions ----
     num_envs = property(lambda self: self._num_envs)

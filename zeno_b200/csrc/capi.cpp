@@ -324,6 +324,10 @@ const void* zeno_model_table(void* model, const char* name, uint64_t* nbytes) {
     if (nbytes) *nbytes = m.color_ranges.size() * 4;
     return m.color_ranges.data();
   }
+  if (n == "pairs") {  // broad-phase candidates (ga, gb, min_dist_sq, plane) in emission order
+    if (nbytes) *nbytes = m.pairs.size() * sizeof(zb::DPair);
+    return m.pairs.data();
+  }
   return nullptr;
 }
 

@@ -20,6 +20,9 @@ struct V3 {
 __device__ __forceinline__ V3 v3(float x, float y, float z) { return V3{x, y, z}; }
 __device__ __forceinline__ V3 v3(float4 a) { return V3{a.x, a.y, a.z}; }
 __device__ __forceinline__ float fma_(float a, float b, float c) { return __fmaf_rn(a, b, c); }
+// Correctly rounded 1/x.  Bit-identical to __frcp_rn(x) (both are the IEEE reciprocal in
+// round-to-nearest-even); the division form has the shorter latency on sm_100a.
+__device__ __forceinline__ float rcp_(float x) { return __fdiv_rn(1.0f, x); }
 
 __device__ __forceinline__ V3 operator+(V3 a, V3 b) { return V3{a.x + b.x, a.y + b.y, a.z + b.z}; }
 __device__ __forceinline__ V3 operator-(V3 a, V3 b) { return V3{a.x - b.x, a.y - b.y, a.z - b.z}; }
@@ -59,7 +62,7 @@ __device__ __forceinline__ float4 qmsub(float4 d, float s, float4 q) {
 __device__ __forceinline__ float4 qnormalize(float4 q) {
   float l = __fsqrt_rn(fma_(q.x, q.x, fma_(q.y, q.y, fma_(q.z, q.z, q.w * q.w))));
   if (l > 1e-8f) {
-    float inv = __frcp_rn(l);
+    float inv = rcp_(l);
     return make_float4(q.x * inv, q.y * inv, q.z * inv, q.w * inv);
   }
   return make_float4(0.0f, 0.0f, 0.0f, 1.0f);

@@ -1,0 +1,172 @@
+// Packs a HostModel into the constant-bank FModel of the environment-per-lane kernel.
+#include "fast_model.h"
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <vector>
+
+#include "model.h"
+#include "zeno_types.h"
+
+namespace zb {
+namespace {
+inline bool narrow_pair_supported(uint32_t ta, uint32_t tb) {  // narrow_core's type pairs
+  return (ta == 0 && tb == 0) || (ta == 0 && tb == 3) || (ta == 3 && tb == 0) || (ta == 1 && tb == 3) ||
+         (ta == 3 && tb == 1);
+}
+inline float4 f4(const float* v) { return make_float4(v[0], v[1], v[2], v[3]); }
+}  // namespace
+
+bool pack_fast_model(const HostModel& h, uint32_t max_contacts, FModel* out, std::vector<uint8_t>* hot,
+                     std::string* why) {
+  auto fail = [&](const char* msg) {
+    if (why) *why = msg;
+    return false;
+  };
+  const uint32_t P = uint32_t(h.pairs.size());
+  if (h.B > fm::kB) return fail("more bodies than the constant-bank model holds");
+  if (h.J > fm::kJ || h.jf_list.size() > fm::kJF) return fail("more joints than the constant-bank model holds");
+  if (h.K > fm::kK) return fail("more constraints than the constant-bank model holds");
+  if (h.G > fm::kG) return fail("more geoms than the constant-bank model holds");
+  if (P > fm::kP) return fail("more broad-phase candidates than the constant-bank model holds");
+  if (h.A > fm::kA) return fail("more actuators than the constant-bank model holds");
+  if (h.S > fm::kS || h.obs_dim > 0xFFFFu) return fail("more sensors than the constant-bank model holds");
+  if (max_contacts > fm::kMaxSlots) return fail("more contact slots per env than the per-slot byte fields index");
+
+  FModel& m = *out;
+  std::memset(&m, 0, sizeof(m));
+  for (uint32_t b = 0; b < h.B; ++b) {
+    const DBody& d = h.bodies[b];
+    if (d.type == 1 && d.inv_mass_inertia[0] >= 1e-8f) return fail("kinematic body with mass");
+    m.imi[b] = f4(d.inv_mass_inertia);
+    m.com[b] = f4(d.com);
+    m.body[b] = (d.type & 0xFFu) | (d.jf_begin << 8) | (d.jf_end << 16) | (std::min<uint32_t>(h.subtree[b], 255u) << 24);
+  }
+  for (size_t k = 0; k < h.jf_list.size(); ++k) {
+    const uint32_t ent = h.jf_list[k];
+    m.jf[k] = uint8_t((ent & 0x7Fu) | ((ent >> 31) ? 0x80u : 0u));
+  }
+  for (uint32_t j = 0; j < h.J; ++j) {
+    const DJoint& d = h.joints[j];
+    // The fused force + integration pass visits bodies children first; it needs every
+    // joint's parent body to precede its child (MJCF tree order guarantees it).
+    if (d.parent >= d.child) return fail("joint parent does not precede its child");
+    m.j_ap[j] = f4(d.anchor_parent);
+    m.j_ac[j] = f4(d.anchor_child);
+    m.j_axis[j] = f4(d.axis);
+    m.j_info[j] = (d.type & 0xFFu) | (d.parent << 8) | (d.child << 16);
+  }
+  for (uint32_t k = 0; k < h.K; ++k) {
+    const DConstraint& c = h.constraints[k];
+    m.c_aa[k] = f4(c.anchor_a);
+    m.c_ab[k] = f4(c.anchor_b);
+    m.c_at[k] = f4(c.axis_target);
+    m.c_lim[k] = f4(c.limits);
+    m.c_info[k] = (c.body_a & 0xFFu) | ((c.body_b & 0xFFu) << 8) | ((c.type & 0xFFu) << 16);
+  }
+  for (uint32_t g = 0; g < h.G; ++g) {
+    m.g_ps[g] = f4(h.geoms[g].pos_size0);
+    m.g_body[g] = h.geoms[g].body;
+  }
+  std::memset(m.gg_pair, int(fm::kNoPair), sizeof(m.gg_pair));
+
+  // sort_contacts key (min body << 16 | max body in the reference); only its order is
+  // used, so the kernel carries the dense rank of each candidate's key.
+  std::vector<uint32_t> keys(P);
+  for (uint32_t p = 0; p < P; ++p) {
+    const uint32_t ba = h.geoms[h.pairs[p].ga].body, bb = h.geoms[h.pairs[p].gb].body;
+    keys[p] = (std::min(ba, bb) << 16) | std::max(ba, bb);
+  }
+  std::vector<uint32_t> distinct = keys;
+  std::sort(distinct.begin(), distinct.end());
+  distinct.erase(std::unique(distinct.begin(), distinct.end()), distinct.end());
+
+  uint32_t H = 0;
+  for (uint32_t p = 0; p < P; ++p) {
+    const DPair& pr = h.pairs[p];
+    const DGeom &ga = h.geoms[pr.ga], &gb = h.geoms[pr.gb];
+    const uint32_t rank = uint32_t(std::lower_bound(distinct.begin(), distinct.end(), keys[p]) - distinct.begin());
+    uint32_t hidx = fm::kNoHit;
+    if (narrow_pair_supported(ga.type, gb.type)) {
+      if (H >= fm::kH) return fail("more hittable candidates than the constant-bank model holds");
+      hidx = H++;
+      m.h_pair[hidx] = p;
+      m.h_info[hidx] = (ga.type & 0xFFu) | ((gb.type & 0xFFu) << 8) | (ga.body << 16) | (gb.body << 24);
+      m.h_ga[hidx] = f4(ga.pos_size0);
+      m.h_gb[hidx] = f4(gb.pos_size0);
+      const DGeom& cap = ga.type == 1 ? ga : gb;
+      m.h_cq[hidx] = f4(cap.quat);
+      m.h_hl[hidx] = cap.size12_fr_rest[0];
+      const float fp = ga.size12_fr_rest[2] * gb.size12_fr_rest[2];  // one IEEE product, then sqrt
+      m.h_fr[hidx] = std::sqrt(fp);
+    }
+    m.p_info[p] = pr.ga | (pr.gb << 8) | (hidx << 16) | (rank << 24);
+    m.p_body[p] = ga.body | (gb.body << 8) | ((pr.plane ? 1u : 0u) << 16);
+    m.p_md2[p] = pr.min_dist_sq;
+    m.gg_pair[pr.ga * fm::kG + pr.gb] = uint8_t(p);
+  }
+  for (uint32_t k = 0; k < h.A; ++k) {
+    const DActuator& d = h.actuators[k];
+    if (d.joint >= h.J) return fail("actuator on a joint index outside the model");
+    m.a_joint[k] = d.joint;
+    m.a_cmin[k] = d.ctrl_min, m.a_cmax[k] = d.ctrl_max, m.a_gear[k] = d.gear;
+    m.a_fmin[k] = d.force_min, m.a_fmax[k] = d.force_max;
+  }
+  for (uint32_t s = 0; s < h.S; ++s) {
+    const DSensor& d = h.sensors[s];
+    const bool joint_sensor = d.type == 0 || d.type == 1;
+    if (d.object >= (joint_sensor ? h.J : h.B)) return fail("sensor object index outside the model");
+    m.s_info[s] = (d.type & 0xFFu) | ((d.object & 0xFFu) << 8) | (d.offset << 16);
+  }
+  m.P = P, m.H = H, m.G = h.G;
+
+  // hot image
+  std::vector<uint8_t>& img = *hot;
+  img.clear();
+  auto section = [&](uint32_t bytes) {
+    const uint32_t off = uint32_t((img.size() + 15) & ~size_t(15));
+    img.resize(off + ((bytes + 15) & ~15u), 0);
+    return off;
+  };
+  auto put = [&](uint32_t off, const void* src, size_t bytes) {
+    if (bytes) std::memcpy(img.data() + off, src, bytes);
+  };
+  const uint32_t B = h.B, J = h.J, K = h.K, G = h.G, JF = uint32_t(h.jf_list.size());
+  m.o_imi = section(16 * B), put(m.o_imi, m.imi, 16 * B);
+  m.o_com = section(16 * B), put(m.o_com, m.com, 16 * B);
+  m.o_body = section(4 * B), put(m.o_body, m.body, 4 * B);
+  m.o_jf = section(4 * JF);
+  for (uint32_t k = 0; k < JF; ++k) {
+    const uint32_t v = m.jf[k];
+    put(m.o_jf + 4 * k, &v, 4);
+  }
+  m.o_jaxis = section(16 * J), put(m.o_jaxis, m.j_axis, 16 * J);
+  m.o_jinfo = section(4 * J), put(m.o_jinfo, m.j_info, 4 * J);
+  m.o_caa = section(16 * K), put(m.o_caa, m.c_aa, 16 * K);
+  m.o_cab = section(16 * K), put(m.o_cab, m.c_ab, 16 * K);
+  m.o_cat = section(16 * K), put(m.o_cat, m.c_at, 16 * K);
+  m.o_clim = section(16 * K), put(m.o_clim, m.c_lim, 16 * K);
+  m.o_cinfo = section(4 * K), put(m.o_cinfo, m.c_info, 4 * K);
+  m.o_pbody = section(4 * P), put(m.o_pbody, m.p_body, 4 * P);
+  m.o_pinfo = section(4 * P), put(m.o_pinfo, m.p_info, 4 * P);
+  m.o_pmd2 = section(4 * P), put(m.o_pmd2, m.p_md2, 4 * P);
+  m.o_gps = section(16 * G), put(m.o_gps, m.g_ps, 16 * G);
+  m.o_hinfo = section(4 * H), put(m.o_hinfo, m.h_info, 4 * H);
+  m.o_hga = section(16 * H), put(m.o_hga, m.h_ga, 16 * H);
+  m.o_hgb = section(16 * H), put(m.o_hgb, m.h_gb, 16 * H);
+  m.o_hcq = section(16 * H), put(m.o_hcq, m.h_cq, 16 * H);
+  m.o_hhl = section(4 * H), put(m.o_hhl, m.h_hl, 4 * H);
+  m.o_hfr = section(4 * H), put(m.o_hfr, m.h_fr, 4 * H);
+  m.o_hpair = section(4 * H), put(m.o_hpair, m.h_pair, 4 * H);
+  m.o_gbody = section(4 * G), put(m.o_gbody, m.g_body, 4 * G);
+  m.o_ggpair = section(G * G);
+  for (uint32_t ga = 0; ga < G; ++ga) put(m.o_ggpair + ga * G, &m.gg_pair[ga * fm::kG], G);
+  m.o_gforce = section(16 * B);
+  section(0);
+  m.hot_bytes = uint32_t(img.size());
+  m.hot = nullptr;
+  return true;
+}
+
+}  // namespace zb

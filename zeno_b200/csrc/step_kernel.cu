@@ -28,6 +28,8 @@
 #include <algorithm>
 
 #include "devmath.cuh"
+#include "model_access.cuh"
+#include "physics.cuh"
 #include "step_kernel.h"
 #include "zeno_types.h"
 
@@ -111,235 +113,16 @@ __device__ __forceinline__ T* sm(unsigned char* base, uint32_t off) {
   return reinterpret_cast<T*>(base + off);
 }
 
-// ------------------------------------------------------------------------------------
-// XPBD joint constraint (solve_joints, all_shaders.metal:909-1399).  The multiplier is
-// not tracked: with compliance 0, alpha~ = 0 and dlambda = -C / w exactly.
-// ------------------------------------------------------------------------------------
-__device__ __forceinline__ void solve_constraint(const DConstraint& c, const DBody* bodies, float4* pos,
-                                                 float4* quat) {
-  const uint32_t type = c.type & 0xFFu;
-  if (type > 10) return;
-  const uint32_t ia = c.body_a, ib = c.body_b;
-  const float4 mia = __ldg(reinterpret_cast<const float4*>(bodies[ia].inv_mass_inertia));
-  const float4 mib = __ldg(reinterpret_cast<const float4*>(bodies[ib].inv_mass_inertia));
-  const V3 Ia{mia.y, mia.z, mia.w}, Ib{mib.y, mib.z, mib.w};
-  const float ima = mia.x, imb = mib.x;
-  if (ima + imb < 1e-8f) return;
-  const V3 pa = v3(pos[ia]), pb = v3(pos[ib]);
-  const float4 qa = quat[ia], qb = quat[ib];
-  const V3 aa = v3(c.anchor_a[0], c.anchor_a[1], c.anchor_a[2]);
-  const V3 ab = v3(c.anchor_b[0], c.anchor_b[1], c.anchor_b[2]);
+// Body state of one environment group (arrays in the group's shared-memory plan).
+struct ArrBodies {
+  float4 *p, *q, *v, *w;
+  __device__ __forceinline__ float4& pos(uint32_t b) { return p[b]; }
+  __device__ __forceinline__ float4& quat(uint32_t b) { return q[b]; }
+  __device__ __forceinline__ float4& vel(uint32_t b) { return v[b]; }
+  __device__ __forceinline__ float4& ang(uint32_t b) { return w[b]; }
+};
 
-  if (type == 2) {  // positional
-    const V3 ra = rotate(aa, qa), rb = rotate(ab, qb);
-    const V3 diff = (pa + ra) - (pb + rb);
-    const float C = len(diff);
-    if (C > 1e-6f) {
-      const V3 n = diff * __frcp_rn(C);
-      const V3 rna = cross(ra, n), rnb = cross(rb, n);
-      const float wa = ima + dot(hadamard(rna, Ia), rna);
-      const float wb = imb + dot(hadamard(rnb, Ib), rnb);
-      const float dl = __fdiv_rn(-C, wa + wb);
-      const V3 imp = n * dl;
-      const float4 ca = __ldg(reinterpret_cast<const float4*>(bodies[ia].com));
-      const float4 cb = __ldg(reinterpret_cast<const float4*>(bodies[ib].com));
-      const V3 rca = ra - rotate(v3(ca), qa), rcb = rb - rotate(v3(cb), qb);
-      if (ima > 0.0f) {
-        pos[ia] = with_w(madd(imp, ima, pa), pos[ia].w);
-        quat[ia] = qnormalize(qmadd(qmul_v(hadamard(cross(rca, imp), Ia), qa), 0.5f, qa));
-      }
-      if (imb > 0.0f) {
-        pos[ib] = with_w(msub(imp, imb, pb), pos[ib].w);
-        quat[ib] = qnormalize(qmsub(qmul_v(hadamard(cross(rcb, imp), Ib), qb), 0.5f, qb));
-      }
-    }
-  } else if (type == 7) {  // weld: corrections on body b only
-    const V3 ra = rotate(aa, qa), rb = rotate(ab, qb);
-    const V3 diff = (pa + ra) - (pb + rb);
-    const float C = len(diff);
-    if (C > 1e-6f) {
-      const V3 n = diff * __frcp_rn(C);
-      const V3 rnb = cross(rb, n);
-      const float wb = imb + dot(hadamard(rnb, Ib), rnb);
-      if (wb > 1e-8f) {
-        const V3 imp = n * __fdiv_rn(-C, wb);
-        pos[ib] = with_w(msub(imp, imb, pb), pos[ib].w);
-        quat[ib] = qnormalize(qmsub(qmul_v(hadamard(cross(rb, imp), Ib), qb), 0.5f, qb));
-      }
-    }
-    const float4 qau = quat[ia], qbu = quat[ib];
-    const float4 tgt = make_float4(c.axis_target[0], c.axis_target[1], c.axis_target[2], c.axis_target[3]);
-    float4 qerr = qmul(qmul(qconj(qau), qbu), qconj(tgt));
-    if (qerr.w < 0.0f) qerr = qneg(qerr);
-    const V3 ev = xyz(qerr);
-    const float sh = len(ev);
-    if (sh > 1e-6f) {
-      const V3 axr = ev * __frcp_rn(sh);
-      const float ang = 2.0f * atan2r(sh, qerr.w);
-      const V3 aw = rotate(axr, qau);
-      const float wb = dot(hadamard(aw, Ib), aw);
-      if (wb > 1e-8f) {
-        const V3 ai = aw * __fdiv_rn(ang, wb);
-        if (imb > 0.0f) quat[ib] = qnormalize(qmsub(qmul_v(hadamard(ai, Ib), qbu), 0.5f, qbu));
-      }
-    }
-  } else if (type == 3) {  // angular: keep hinge axes parallel
-    const V3 aaw = rotate(aa, qa), abw = rotate(ab, qb);
-    const V3 cr = cross(aaw, abw);
-    const float sa = len(cr);
-    if (sa > 1e-6f) {
-      const V3 n = cr * __frcp_rn(sa);
-      const float angC = asinr(clampf(sa, -1.0f, 1.0f));
-      const float w = dot(hadamard(n, Ia), n) + dot(hadamard(n, Ib), n);
-      if (w > 1e-8f) {
-        const float dl = __fdiv_rn(-angC, w);
-        if (ima > 0.0f) quat[ia] = qnormalize(qmadd(qmul_v(hadamard(n * dl, Ia), qa), 0.5f, qa));
-        if (imb > 0.0f) quat[ib] = qnormalize(qmadd(qmul_v(hadamard(n * (-dl), Ib), qb), 0.5f, qb));
-      }
-    }
-  } else if (type == 4) {  // angular limit
-    const float lo = c.limits[0], hi = c.limits[1];
-    const float4 qrel = qmul(qconj(qa), qb);
-    const float angle = 2.0f * atan2r(dot(xyz(qrel), aa), qrel.w);
-    float viol = 0.0f;
-    if (angle < lo) viol = lo - angle;
-    else if (angle > hi) viol = hi - angle;
-    if (fabsf(viol) > 1e-6f) {
-      const V3 aw = rotate(aa, qa);
-      const float w = dot(hadamard(aw, Ia), aw) + dot(hadamard(aw, Ib), aw);
-      if (w > 1e-8f) {
-        const V3 ai = aw * __fdiv_rn(viol, w);
-        if (ima > 0.0f) quat[ia] = qnormalize(qmadd(qmul_v(hadamard(ai, Ia), qa), 0.5f, qa));
-        if (imb > 0.0f) quat[ib] = qnormalize(qmsub(qmul_v(hadamard(ai, Ib), qb), 0.5f, qb));
-      }
-    }
-  } else if (type == 5) {  // linear limit
-    const float lo = c.limits[0], hi = c.limits[1];
-    const V3 ra = rotate(v3(0.0f, 0.0f, 0.0f), qa), rb = rotate(ab, qb);
-    const V3 aw = rotate(aa, qa);
-    const float dist = dot((pb + rb) - (pa + ra), aw);
-    float viol = 0.0f;
-    if (dist < lo) viol = lo - dist;
-    else if (dist > hi) viol = hi - dist;
-    if (fabsf(viol) > 1e-6f) {
-      const V3 n = viol > 0.0f ? aw : -aw;
-      const V3 rna = cross(ra, n), rnb = cross(rb, n);
-      const float wa = ima + dot(hadamard(rna, Ia), rna);
-      const float wb = imb + dot(hadamard(rnb, Ib), rnb);
-      const float w = wa + wb;
-      if (w > 1e-8f) {
-        const V3 imp = n * __fdiv_rn(fabsf(viol), w);
-        if (ima > 0.0f) pos[ia] = with_w(msub(imp, ima, pa), pos[ia].w);
-        if (imb > 0.0f) pos[ib] = with_w(madd(imp, imb, pb), pos[ib].w);
-      }
-    }
-  } else if (type == 10) {  // slider: perpendicular lock + relative-orientation weld
-    const V3 ra = rotate(aa, qa), rb = rotate(ab, qb);
-    const V3 diff = (pa + ra) - (pb + rb);
-    const V3 aw = rotate(v3(c.axis_target[0], c.axis_target[1], c.axis_target[2]), qa);
-    const V3 perp = msub(aw, dot(diff, aw), diff);
-    const float pl = len(perp);
-    if (pl > 1e-6f) {
-      const V3 n = perp * __frcp_rn(pl);
-      const V3 rna = cross(ra, n), rnb = cross(rb, n);
-      const float wa = ima + dot(hadamard(rna, Ia), rna);
-      const float wb = imb + dot(hadamard(rnb, Ib), rnb);
-      const V3 imp = n * __fdiv_rn(-pl, wa + wb);
-      if (ima > 0.0f) {
-        pos[ia] = with_w(madd(imp, ima, pa), pos[ia].w);
-        quat[ia] = qnormalize(qmadd(qmul_v(hadamard(cross(ra, imp), Ia), qa), 0.5f, qa));
-      }
-      if (imb > 0.0f) {
-        pos[ib] = with_w(msub(imp, imb, pb), pos[ib].w);
-        quat[ib] = qnormalize(qmsub(qmul_v(hadamard(cross(rb, imp), Ib), qb), 0.5f, qb));
-      }
-    }
-    const float4 qau = quat[ia], qbu = quat[ib];
-    const float4 tgt = make_float4(c.limits[0], c.limits[1], c.limits[2], c.limits[3]);
-    float4 qerr = qmul(qmul(qconj(qau), qbu), qconj(tgt));
-    if (qerr.w < 0.0f) qerr = qneg(qerr);
-    const V3 ev = xyz(qerr);
-    const float sh = len(ev);
-    if (sh > 1e-6f) {
-      const V3 axe = ev * __frcp_rn(sh);
-      const float ae = 2.0f * atan2r(sh, qerr.w);
-      const V3 aw2 = rotate(axe, qau);
-      const float w = dot(hadamard(aw2, Ia), aw2) + dot(hadamard(aw2, Ib), aw2);
-      if (w > 1e-8f) {
-        const V3 ai = aw2 * __fdiv_rn(ae, w);
-        if (ima > 0.0f) quat[ia] = qnormalize(qmadd(qmul_v(hadamard(ai, Ia), qau), 0.5f, qau));
-        if (imb > 0.0f) quat[ib] = qnormalize(qmsub(qmul_v(hadamard(ai, Ib), qbu), 0.5f, qbu));
-      }
-    }
-  }
-}
-
-// ------------------------------------------------------------------------------------
-// Contact solve for one slot (solve_contacts, all_shaders.metal:1644-1793)
-// ------------------------------------------------------------------------------------
-__device__ __forceinline__ void solve_contact(float4& cpp, float4& cnf, float4& cim, uint32_t pk,
-                                              const DBody* bodies, float4* pos, float4* vel, float4* ang,
-                                              float dt, float baumgarte, float slop) {
-  const uint32_t ia = pk_a(pk), ib = pk_b(pk);
-  const float4 mia = __ldg(reinterpret_cast<const float4*>(bodies[ia].inv_mass_inertia));
-  const float4 mib = __ldg(reinterpret_cast<const float4*>(bodies[ib].inv_mass_inertia));
-  const V3 Ia{mia.y, mia.z, mia.w}, Ib{mib.y, mib.z, mib.w};
-  const float ima = mia.x, imb = mib.x;
-  const float isum = ima + imb;
-  if (isum < 1e-8f) return;
-  const V3 n = xyz(cnf);
-  const float pen = cpp.w, fr = cnf.w;
-  const V3 cp = xyz(cpp);
-  const V3 ra = cp - v3(pos[ia]), rb = cp - v3(pos[ib]);
-  const V3 va = v3(vel[ia]) + cross(v3(ang[ia]), ra);
-  const V3 vb = v3(vel[ib]) + cross(v3(ang[ib]), rb);
-  const V3 rv = va - vb;
-  const float vn = dot(rv, n);
-  const V3 vt = msub(n, vn, rv);
-  const float ts = len(vt);
-  const V3 rna = cross(ra, n), rnb = cross(rb, n);
-  const float wn = (ima + dot(hadamard(rna, Ia), rna)) + (imb + dot(hadamard(rnb, Ib), rnb));
-  if (wn < 1e-8f) return;
-  const float excess = fmaxf(pen - slop, 0.0f);
-  const float bias = __fdiv_rn(baumgarte * excess, dt);
-  const float vrest = vn < -0.5f ? cim.w * vn : 0.0f;
-  const float jn = fmaxf(__fdiv_rn(-(vn + vrest) + bias, wn), 0.0f);
-  const V3 in_ = n * jn;
-  const float pcorr = baumgarte * excess;
-  if (ima > 1e-8f) {
-    vel[ia] = with_w(madd(in_, ima, v3(vel[ia])), vel[ia].w);
-    ang[ia] = with_w(v3(ang[ia]) + hadamard(cross(ra, in_), Ia), ang[ia].w);
-    pos[ia] = with_w(madd(n, pcorr * __fdiv_rn(ima, isum), v3(pos[ia])), pos[ia].w);
-  }
-  if (imb > 1e-8f) {
-    vel[ib] = with_w(msub(in_, imb, v3(vel[ib])), vel[ib].w);
-    ang[ib] = with_w(v3(ang[ib]) - hadamard(cross(rb, in_), Ib), ang[ib].w);
-    pos[ib] = with_w(msub(n, pcorr * __fdiv_rn(imb, isum), v3(pos[ib])), pos[ib].w);
-  }
-  const float jacc = cim.x + jn;
-  if (ts > 1e-6f && jacc > 1e-6f) {
-    const V3 t = vt * __frcp_rn(ts);
-    const V3 rta = cross(ra, t), rtb = cross(rb, t);
-    const float wt = (ima + dot(hadamard(rta, Ia), rta)) + (imb + dot(hadamard(rtb, Ib), rtb));
-    if (wt > 1e-8f) {
-      const float jt = fminf(__fdiv_rn(ts, wt), fr * jacc);
-      const V3 it = t * jt;
-      if (ima > 1e-8f) {
-        vel[ia] = with_w(msub(it, ima, v3(vel[ia])), vel[ia].w);
-        ang[ia] = with_w(v3(ang[ia]) - hadamard(cross(ra, it), Ia), ang[ia].w);
-      }
-      if (imb > 1e-8f) {
-        vel[ib] = with_w(madd(it, imb, v3(vel[ib])), vel[ib].w);
-        ang[ib] = with_w(v3(ang[ib]) + hadamard(cross(rb, it), Ib), ang[ib].w);
-      }
-    }
-  }
-  cim.x = jn;
-}
-
-// ------------------------------------------------------------------------------------
 // Narrow phase for one slot (narrow_phase, all_shaders.metal:751-894)
-// ------------------------------------------------------------------------------------
 __device__ __forceinline__ void narrow(uint32_t pk, const DGeom* geoms, const float4* pos, float restitution,
                                        float4& cpp, float4& cnf, float4& cim) {
   const DGeom& gA = geoms[pk_ga(pk)];
@@ -348,47 +131,11 @@ __device__ __forceinline__ void narrow(uint32_t pk, const DGeom* geoms, const fl
   const float4 gb0 = __ldg(reinterpret_cast<const float4*>(gB.pos_size0));
   const V3 pa = v3(pos[pk_a(pk)]) + v3(ga0), pb = v3(pos[pk_b(pk)]) + v3(gb0);
   const uint32_t ta = __ldg(&gA.type), tb = __ldg(&gB.type);
+  const DGeom& cg = ta == 1 ? gA : gB;
   V3 normal{0, 0, 0}, point{0, 0, 0};
   float pen = 0.0f;
-  bool hit = false;
-  if (ta == 0 && tb == 0) {
-    const V3 d = pb - pa;
-    const float dist = len(d);
-    const float md = ga0.w + gb0.w;
-    if (dist < md && dist > 1e-6f) {
-      normal = d * __frcp_rn(dist);
-      pen = md - dist;
-      point = madd(normal, ga0.w - pen * 0.5f, pa);
-      hit = true;
-    }
-  } else if ((ta == 0 && tb == 3) || (ta == 3 && tb == 0)) {
-    const V3 sp = ta == 0 ? pa : pb, pp = ta == 0 ? pb : pa;
-    const float sr = ta == 0 ? ga0.w : gb0.w;
-    const V3 pn{0.0f, 0.0f, 1.0f};
-    const float sd = dot(sp - pp, pn);
-    if (sd < sr) {
-      normal = ta == 3 ? -pn : pn;
-      pen = sr - sd;
-      point = msub(pn, sd + pen * 0.5f, sp);
-      hit = true;
-    }
-  } else if ((ta == 1 && tb == 3) || (ta == 3 && tb == 1)) {
-    const DGeom& cg = ta == 1 ? gA : gB;
-    const V3 cpos = ta == 1 ? pa : pb;
-    const float cr = ta == 1 ? ga0.w : gb0.w;
-    const float hl = __ldg(&cg.size12_fr_rest[0]);
-    const float4 cq = __ldg(reinterpret_cast<const float4*>(cg.quat));
-    const V3 axis = rotate(v3(0.0f, 0.0f, 1.0f), cq);
-    const V3 p1 = msub(axis, hl, cpos), p2 = madd(axis, hl, cpos);
-    const float d1 = p1.z - cr, d2 = p2.z - cr;
-    if (d1 < 0.0f || d2 < 0.0f) {
-      point = d1 < d2 ? p1 : p2;
-      point.z = 0.0f;
-      pen = -fminf(d1, d2);
-      normal = ta == 1 ? v3(0.0f, 0.0f, 1.0f) : v3(0.0f, 0.0f, -1.0f);
-      hit = true;
-    }
-  }
+  const bool hit = narrow_core(ta, tb, pa, pb, ga0.w, gb0.w, __ldg(&cg.size12_fr_rest[0]),
+                               __ldg(reinterpret_cast<const float4*>(cg.quat)), point, normal, pen);
   if (hit) {
     const float fr = __fsqrt_rn(__ldg(&gA.size12_fr_rest[2]) * __ldg(&gB.size12_fr_rest[2]));
     cpp = with_w(point, pen);
@@ -446,18 +193,14 @@ __device__ void reset_env_noise(const StepArgs& a, uint32_t e, float4* pos, floa
 }
 
 // ------------------------------------------------------------------------------------
-// The kernel.  L lanes per environment, blockDim.x / L environments per block.
+// One environment, stepped by the L lanes of group g (syncs are group-local).
 // ------------------------------------------------------------------------------------
 template <int L>
-__global__ void __launch_bounds__(256) step_kernel(StepArgs a) {
-  extern __shared__ __align__(16) unsigned char smem_raw[];
-  const uint32_t NE = blockDim.x / L;
-  const uint32_t g = threadIdx.x / L;
-  const uint32_t l = threadIdx.x % L;
-  const uint32_t e = blockIdx.x * NE + g;
-  if (e >= a.num_envs) return;  // whole groups retire together; syncs are group-local
+__device__ __forceinline__ void step_env(const StepArgs& a, uint32_t e, unsigned char* smem_raw, uint32_t g,
+                                         uint32_t l) {
   const unsigned gmask = L == 32 ? 0xFFFFFFFFu : (((1u << L) - 1u) << ((threadIdx.x & 31u) & ~(L - 1u)));
   const uint32_t gshift = (threadIdx.x & 31u) & ~(L - 1u);
+  const ModelG mg{a.bodies, a.constraints};
 
   const uint32_t B = a.B, J = a.J, A = a.A, M = a.M;
   const Plan P = make_plan(B, J, M);
@@ -488,6 +231,7 @@ __global__ void __launch_bounds__(256) step_kernel(StepArgs a) {
   uint16_t* lcur = sm<uint16_t>(base, P.lcur);
   uint16_t* blev = sm<uint16_t>(base, P.blev);
   uint32_t* flags = sm<uint32_t>(base, P.flags);
+  ArrBodies bodies{pos, quat, vel, ang};
 
   // ---------------- load the environment ----------------
   const size_t eb = size_t(e) * B;
@@ -560,7 +304,7 @@ __global__ void __launch_bounds__(256) step_kernel(StepArgs a) {
         frc[b] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
         trq[b] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
       } else {
-        const V3 f = grav * __frcp_rn(im);
+        const V3 f = grav * rcp_(im);
         const float4 com = __ldg(reinterpret_cast<const float4*>(bd.com));
         frc[b] = with_w(f, 0.0f);
         trq[b] = with_w(cross(rotate(v3(com), quat[b]), f), 0.0f);
@@ -694,10 +438,7 @@ __global__ void __launch_bounds__(256) step_kernel(StepArgs a) {
     for (uint32_t it = 0; it < a.iterations; ++it) {
       for (uint32_t col = 0; col < a.num_colors; ++col) {
         const uint32_t off = __ldg(&a.color_ranges[2 * col]), cnt = __ldg(&a.color_ranges[2 * col + 1]);
-        for (uint32_t k = l; k < cnt; k += L) {
-          const DConstraint c = a.constraints[off + k];
-          solve_constraint(c, a.bodies, pos, quat);
-        }
+        for (uint32_t k = l; k < cnt; k += L) solve_constraint(mg, mg.constraint(off + k), bodies);
         __syncwarp(gmask);
       }
     }
@@ -738,7 +479,10 @@ __global__ void __launch_bounds__(256) step_kernel(StepArgs a) {
         const uint32_t k0 = lvl[lv], k1 = lvl[lv + 1];
         for (uint32_t k = k0 + l; k < k1; k += L) {
           const uint32_t st = ord[sched[k]];
-          solve_contact(cpp[st], cnf[st], cim[st], cpk[st], a.bodies, pos, vel, ang, dt, a.baumgarte, a.slop);
+          float jx = cim[st].x;
+          solve_contact(mg, cpp[st], cnf[st], jx, cim[st].w, pk_a(cpk[st]), pk_b(cpk[st]), bodies, dt, a.baumgarte,
+                        a.slop);
+          cim[st].x = jx;
         }
         __syncwarp(gmask);
       }
@@ -893,8 +637,39 @@ __global__ void __launch_bounds__(256) step_kernel(StepArgs a) {
   }
   if (l == 0) {
     a.counts[e] = count_out;
-    a.prev_counts[e] = prev_count;
-    a.prev_sep[e] = 0;
+    if (stepped) {
+      a.prev_counts[e] = prev_count;
+      a.prev_sep[e] = 0;
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------------
+// The kernel.  L lanes per environment, blockDim.x / L environments per block.  With
+// env_list set, the grid strides over the *env_count listed environments instead (the
+// ones the environment-per-lane kernel handed over); the last block to finish clears
+// the count for the next step.
+// ------------------------------------------------------------------------------------
+template <int L>
+__global__ void __launch_bounds__(256) step_kernel(StepArgs a) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  const uint32_t NE = blockDim.x / L;
+  const uint32_t g = threadIdx.x / L;
+  const uint32_t l = threadIdx.x % L;
+  if (a.env_list == nullptr) {
+    const uint32_t e = blockIdx.x * NE + g;
+    if (e < a.num_envs) step_env<L>(a, e, smem_raw, g, l);  // whole groups retire together
+    return;
+  }
+  const uint32_t cnt = *a.env_count;
+  for (uint32_t i = blockIdx.x * NE + g; i < cnt; i += gridDim.x * NE) step_env<L>(a, a.env_list[i], smem_raw, g, l);
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    if (atomicAdd(a.env_done, 1u) == gridDim.x - 1) {
+      *a.env_count = 0;
+      *a.env_done = 0;
+    }
   }
 }
 
@@ -905,7 +680,9 @@ cudaError_t launch_step(const StepArgs& args, int lanes, int envs_per_block, cud
   if (args.num_envs == 0) return cudaSuccess;
   const uint32_t env_bytes = env_smem_bytes(args.B, args.J, args.M);
   const uint32_t threads = uint32_t(lanes * envs_per_block);
-  const uint32_t blocks = (args.num_envs + envs_per_block - 1) / envs_per_block;
+  const uint32_t full = (args.num_envs + envs_per_block - 1) / envs_per_block;
+  // list mode: enough blocks for one group per SM sub-partition, strided over the list
+  const uint32_t blocks = args.env_list ? std::min<uint32_t>(full, 148u * 4u) : full;
   const size_t smem = size_t(env_bytes) * envs_per_block;
   cudaError_t err = cudaSuccess;
   switch (lanes) {

@@ -7,6 +7,7 @@
 // next step.  Model tables and internal caches are plain device memory.
 #include "world.h"
 
+#include <algorithm>
 #include <chrono>
 #include <cstring>
 #include <vector>
@@ -71,12 +72,16 @@ World* World::create(const Scene& sc, const WorldConfig& cfg, std::string* err) 
   const uint32_t E = cfg.num_envs, B = m.B, J1 = m.J ? m.J : 1, M = cfg.max_contacts_per_env;
   if (M > 65535) return fail("max_contacts_per_env above 65535", w);
 
-  // launch shape: 8 lanes per env, as many envs per block as shared memory allows (<= 16)
+  // general kernel shape: 8 lanes per env, 4 envs per block (small blocks pack the SM's
+  // shared memory tightly and balance the tail wave better)
   const uint32_t env_bytes = env_smem_bytes(B, m.J, M);
   const int smem_cap = opt_in_smem(w->device_);
   if (env_bytes > uint32_t(smem_cap)) return fail("model does not fit in shared memory (reduce max_contacts_per_env)", w);
   w->lanes_ = 8;
-  w->envs_per_block_ = int(std::min<uint32_t>(16u, uint32_t(smem_cap) / env_bytes));
+  w->envs_per_block_ = int(std::min<uint32_t>(4u, uint32_t(smem_cap) / env_bytes));
+  // environment-per-lane kernel when the model packs into its fixed-capacity tables
+  std::string why;
+  w->fast_ok_ = pack_fast_model(m, M, &w->fmodel_, &w->hot_image_, &why);
 
   if (cudaStreamCreateWithFlags(&w->own_stream_, cudaStreamNonBlocking) != cudaSuccess) return fail("stream", w);
   w->stream_ = w->own_stream_;
@@ -102,6 +107,7 @@ World* World::create(const Scene& sc, const WorldConfig& cfg, std::string* err) 
   e = e ? e : w->device_buf(&w->d_actions_, size_t(E) * (m.A ? m.A : 1));
   e = e ? e : w->device_buf(&w->d_mask_, E);
   e = e ? e : w->device_buf(&w->d_status_, 4);
+  e = e ? e : w->device_buf(&w->d_odd_, size_t(E) + 2);
   auto upload = [&](auto** dst, const auto& v) {
     if (e != cudaSuccess) return;
     e = w->device_buf(dst, v.size());
@@ -118,13 +124,45 @@ World* World::create(const Scene& sc, const WorldConfig& cfg, std::string* err) 
   upload(&w->d_colors_, m.color_ranges);
   upload(&w->d_subtree_, m.subtree);
   upload(&w->d_init_, m.init_state);
+  if (w->fast_ok_) {
+    upload(&w->d_hot_, w->hot_image_);
+    w->fmodel_.hot = reinterpret_cast<const uint4*>(w->d_hot_);
+    e = e ? e : w->device_buf(&w->pose_scratch_, size_t(2) * B * E);
+  }
   if (e != cudaSuccess) return fail(std::string("CUDA allocation failed: ") + cudaGetErrorString(e), w);
 
   // initializeState (world.zig:663-691): every env starts from the body definitions
   e = launch_reset(w->pos, w->quat, w->vel, w->angvel, w->jpos, w->jvel, w->d_init_, E, B, m.J, nullptr, w->stream_);
   if (e == cudaSuccess) e = cudaStreamSynchronize(w->stream_);
   if (e != cudaSuccess) return fail(std::string("CUDA init failed: ") + cudaGetErrorString(e), w);
+  if (w->fast_ok_) w->choose_fast_shape();
   return w;
+}
+
+// envs_per_block for the environment-per-lane kernel: the widest block (fullest warps)
+// that still lets every environment be resident at once; when none does, the shape
+// with the most resident environments per SM.
+void World::choose_fast_shape() {
+  int sms = 148;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device_);
+  const StepArgs a = args(cfg_.substeps, nullptr, nullptr);
+  int best = 0, best_res = 0;
+  for (int epb = 32; epb >= 1; --epb) {
+    const int bps = fast_max_active_blocks(a, fmodel_, epb);
+    if (bps <= 0) continue;
+    const uint64_t resident = uint64_t(bps) * epb;
+    if (resident * uint64_t(sms) >= cfg_.num_envs) {
+      best = epb;
+      break;
+    }
+    if (int(resident) > best_res) best_res = int(resident), best = epb;
+  }
+  if (best == 0) {
+    fast_ok_ = false;
+    return;
+  }
+  fast_epb_ = best;
+  use_fast_ = true;
 }
 
 World::~World() {
@@ -157,11 +195,22 @@ StepArgs World::args(uint32_t substeps, const float* actions, const uint8_t* mas
   a.prev_sep = prev_sep_, a.episode = episode_, a.actions = actions, a.step_mask = mask;
   a.task = task_;
   a.status = d_status_;
+  a.odd_count = d_odd_;
+  a.odd_list = d_odd_ + 2;
+  a.pose_scratch = pose_scratch_;
   return a;
 }
 
 cudaError_t World::launch(uint32_t substeps, const float* actions, const uint8_t* mask) {
-  return launch_step(args(substeps, actions, mask), lanes_, envs_per_block_, stream_);
+  StepArgs a = args(substeps, actions, mask);
+  if (!use_fast_) return launch_step(a, lanes_, envs_per_block_, stream_);
+  cudaError_t e = launch_fast_step(a, fmodel_, fast_epb_, stream_);
+  if (e != cudaSuccess) return e;
+  // environments the fast kernel handed over (normally none): general kernel, list mode
+  a.env_list = d_odd_ + 2;
+  a.env_count = d_odd_;
+  a.env_done = d_odd_ + 1;
+  return launch_step(a, lanes_, envs_per_block_, stream_);
 }
 
 cudaError_t World::step(const float* actions, uint32_t substeps, bool async) {
@@ -329,6 +378,13 @@ int World::set_task(const DTask& t) {
 }
 
 int World::set_launch(int lanes, int envs_per_block) {
+  if (lanes == 1) {
+    if (!fast_ok_ || envs_per_block < 1 || envs_per_block > 32) return -6;
+    if (fast_max_active_blocks(args(cfg_.substeps, nullptr, nullptr), fmodel_, envs_per_block) <= 0) return -6;
+    fast_epb_ = envs_per_block;
+    use_fast_ = true;
+    return 0;
+  }
   if (lanes != 4 && lanes != 8 && lanes != 16 && lanes != 32) return -6;
   const uint32_t env_bytes = env_smem_bytes(model_.B, model_.J, cfg_.max_contacts_per_env);
   if (envs_per_block < 1 || lanes * envs_per_block > 256 ||
@@ -336,6 +392,7 @@ int World::set_launch(int lanes, int envs_per_block) {
     return -6;
   lanes_ = lanes;
   envs_per_block_ = envs_per_block;
+  use_fast_ = false;
   return 0;
 }
 

@@ -7,6 +7,7 @@
 #include <cstdint>
 #include <string>
 
+#include "fast_model.h"
 #include "model.h"
 #include "zeno_types.h"
 
@@ -50,6 +51,8 @@ class World {
   void set_gravity(float gx, float gy, float gz);
   int set_timestep(float ts);
   int set_task(const DTask& t);
+  // lanes 1: environment-per-lane kernel with envs_per_block (1..32) lanes per block;
+  // lanes 4/8/16/32: general kernel only.  -6 when the shape is invalid or unsupported.
   int set_launch(int lanes, int envs_per_block);
   cudaError_t synchronize();
   void set_stream(cudaStream_t s) { stream_ = s ? s : own_stream_; }
@@ -62,8 +65,9 @@ class World {
   int device() const { return device_; }
   Profiling profiling() const { return prof_; }
   void reset_profiling() { prof_ = Profiling{}; }
-  int lanes() const { return lanes_; }
-  int envs_per_block() const { return envs_per_block_; }
+  int lanes() const { return use_fast_ ? 1 : lanes_; }
+  int envs_per_block() const { return use_fast_ ? fast_epb_ : envs_per_block_; }
+  bool fast_available() const { return fast_ok_; }
 
   // ABI-visible state (managed memory: host and device addressable)
   float* pos = nullptr;
@@ -83,6 +87,7 @@ class World {
  private:
   World() = default;
   StepArgs args(uint32_t substeps, const float* actions, const uint8_t* mask) const;
+  void choose_fast_shape();
   cudaError_t launch(uint32_t substeps, const float* actions, const uint8_t* mask);
   template <class T>
   cudaError_t managed(T** p, size_t n);
@@ -95,8 +100,15 @@ class World {
   float timestep_ = 0.0f;
   float gravity_[3] = {0, 0, -9.81f};
   int device_ = 0;
-  int lanes_ = 8;
-  int envs_per_block_ = 16;
+  int lanes_ = 8;            // general kernel shape (also the hand-over launch)
+  int envs_per_block_ = 4;
+  bool fast_ok_ = false;     // the model packs into FModel
+  bool use_fast_ = false;
+  int fast_epb_ = 32;
+  FModel fmodel_{};
+  std::vector<uint8_t> hot_image_;
+  uint8_t* d_hot_ = nullptr;
+  float4* pose_scratch_ = nullptr;
   uint64_t bytes_ = 0;
   cudaStream_t own_stream_ = nullptr;
   cudaStream_t stream_ = nullptr;
@@ -122,6 +134,7 @@ class World {
   float* d_actions_ = nullptr;
   uint8_t* d_mask_ = nullptr;
   uint32_t* d_status_ = nullptr;
+  uint32_t* d_odd_ = nullptr;  // [0] hand-over count, [1] blocks done, [2..] env indices
   std::vector<void*> allocations_;
 };
 

@@ -14,6 +14,7 @@
 //    dlambda = (-C - alpha~*lambda)/(w + alpha~) does not read lambda.
 #pragma once
 #include <stdint.h>
+#include <vector_types.h>
 
 #ifdef __CUDACC__
 #define ZB_HD __host__ __device__
@@ -136,6 +137,13 @@ struct StepArgs {
   const uint8_t* step_mask;  // null, or per-env: 0 = compute but publish only the caches
   DTask task;
   uint32_t* status;          // device status word (bit 0: shared-memory plan exceeded)
+  // hand-over from the environment-per-lane kernel to the general kernel
+  uint32_t* odd_list;        // environments the fast kernel left untouched
+  uint32_t* odd_count;
+  const uint32_t* env_list;  // general kernel: step only these (null: all envs)
+  uint32_t* env_count;
+  uint32_t* env_done;        // blocks finished (the last one clears env_count)
+  float4* pose_scratch;      // environment-per-lane kernel: 2 * B * num_envs poses before integration
 };
 
 }  // namespace zb
