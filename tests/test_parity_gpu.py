@@ -159,10 +159,11 @@ def test_task_extension_bit_exact(auto_reset):
     assert saw_done
 
 
-@pytest.mark.parametrize("lanes,epb", [(1, 32), (1, 7), (1, 1), (4, 8), (8, 4), (16, 2), (32, 1)])
+@pytest.mark.parametrize("lanes,epb", [(1, 32), (1, 7), (1, 1), (2, 32), (2, 5), (4, 8), (4, 3), (8, 4), (16, 2),
+                                      (32, 1)])
 def test_launch_shapes_agree(lanes, epb):
-    """Every launch shape of both kernels computes the same bits: lanes 1 is the
-    environment-per-lane kernel, 4..32 the general kernel."""
+    """Every launch shape of both kernels computes the same bits: lanes 1, 2, 4 run the
+    compressed-state kernel, 8..32 the general kernel."""
     E = 13
     w, o, c = make_pair("ant", E)
     w.set_launch(lanes, epb)
@@ -203,10 +204,24 @@ def test_full_size_ant_sampled_envs_and_determinism():
 
 
 @pytest.mark.parametrize("name", ["ant", "humanoid", "cartpole", "pendulum", "pendulum_asset"])
-def test_default_kernel_is_environment_per_lane(name):
-    """Every scene of the parity suite runs on the environment-per-lane kernel by default."""
+def test_default_kernel_is_compressed_state(name):
+    """Every scene of the parity suite runs on the compressed-state kernel by default."""
     w, _, _ = make_pair(name, 4)
-    assert w.get_launch()[0] == 1
+    assert w.get_launch()[0] in (1, 2, 4)
+
+
+@pytest.mark.parametrize("lanes", [1, 2, 4])
+@pytest.mark.parametrize("name", ["humanoid", "cartpole", "pendulum_asset"])
+def test_scenes_on_every_lane_count(name, lanes):
+    """The compressed-state kernel with 1, 2 and 4 lanes per environment against the oracle."""
+    w, o, c = make_pair(name, 6)
+    w.set_launch(lanes, 4)
+    rng = np.random.default_rng(11)
+    acts = actions(rng, 8, 6, w.action_dim, c["act"])
+    for s in range(8):
+        w.step(acts[s])
+        o.step(acts[s])
+    assert not diff_report(product_state(w), o.state())
 
 
 def test_large_scene_uses_general_kernel():
@@ -215,7 +230,7 @@ def test_large_scene_uses_general_kernel():
     xml = scenes.collision_stress(0)
     w = ZenoWorld(mjcf_string=xml, num_envs=3, substeps=2)
     o = OracleWorld(xml, num_envs=3, substeps=2)
-    assert w.get_launch()[0] >= 4
+    assert w.get_launch()[0] >= 8
     none = np.zeros((3, 0), np.float32)
     for _ in range(3):
         w.step(none)
@@ -223,7 +238,8 @@ def test_large_scene_uses_general_kernel():
     assert not diff_report(product_state(w), o.state())
 
 
-def test_hand_over_to_general_kernel():
+@pytest.mark.parametrize("lanes", [1, 2, 4])
+def test_hand_over_to_general_kernel(lanes):
     """An environment whose stored contact list the fast kernel cannot represent (a slot
     tuple that is not a broad-phase candidate) is stepped by the general kernel instead;
     the result equals running the general kernel on every environment, and the hand-over
@@ -233,9 +249,9 @@ def test_hand_over_to_general_kernel():
     rng = np.random.default_rng(5)
     acts = actions(rng, 6, E, 8, 1.0)
     runs = []
-    for lanes, epb in ((1, 32), (8, 4)):
+    for ln, epb in ((lanes, 32), (8, 4)):
         w = ZenoWorld(mjcf_string=xml, num_envs=E, substeps=4)
-        w.set_launch(lanes, epb)
+        w.set_launch(ln, epb)
         for s in range(3):
             w.step(acts[s])
         c = w.get_contacts()  # zero-copy view of the contact buffer

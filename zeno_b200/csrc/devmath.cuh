@@ -58,14 +58,17 @@ __device__ __forceinline__ float4 qmadd(float4 d, float s, float4 q) {
 __device__ __forceinline__ float4 qmsub(float4 d, float s, float4 q) {
   return make_float4(fma_(-d.x, s, q.x), fma_(-d.y, s, q.y), fma_(-d.z, s, q.z), fma_(-d.w, s, q.w));
 }
-// quat_normalize (all_shaders.metal:99-102): len > 1e-8 ? q * (1/len) : identity
+// quat_normalize (all_shaders.metal:99-102): len > 1e-8 ? q * (1/len) : identity.
+// Written as a select (the reciprocal is computed either way): no branch on the chain.
 __device__ __forceinline__ float4 qnormalize(float4 q) {
-  float l = __fsqrt_rn(fma_(q.x, q.x, fma_(q.y, q.y, fma_(q.z, q.z, q.w * q.w))));
-  if (l > 1e-8f) {
-    float inv = rcp_(l);
-    return make_float4(q.x * inv, q.y * inv, q.z * inv, q.w * inv);
-  }
-  return make_float4(0.0f, 0.0f, 0.0f, 1.0f);
+  const float l = __fsqrt_rn(fma_(q.x, q.x, fma_(q.y, q.y, fma_(q.z, q.z, q.w * q.w))));
+  const float inv = rcp_(l);
+  const bool ok = l > 1e-8f;
+  return make_float4(ok ? q.x * inv : 0.0f, ok ? q.y * inv : 0.0f, ok ? q.z * inv : 0.0f, ok ? q.w * inv : 1.0f);
+}
+// c ? a : b per component
+__device__ __forceinline__ float4 sel4(bool c, float4 a, float4 b) {
+  return make_float4(c ? a.x : b.x, c ? a.y : b.y, c ? a.z : b.z, c ? a.w : b.w);
 }
 // rotate_by_quat (all_shaders.metal:92-97): v + 2*(w*(qv x v) + qv x (qv x v))
 __device__ __forceinline__ V3 rotate(V3 v, float4 q) {

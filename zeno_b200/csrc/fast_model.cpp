@@ -163,6 +163,12 @@ bool pack_fast_model(const HostModel& h, uint32_t max_contacts, FModel* out, std
   m.o_ggpair = section(G * G);
   for (uint32_t ga = 0; ga < G; ++ga) put(m.o_ggpair + ga * G, &m.gg_pair[ga * fm::kG], G);
   m.o_gforce = section(16 * B);
+  m.num_colors = h.num_colors;
+  m.o_color = section(4 * h.num_colors);
+  for (uint32_t col = 0; col < h.num_colors; ++col) {
+    const uint32_t v = h.color_ranges[2 * col] | (h.color_ranges[2 * col + 1] << 16);
+    put(m.o_color + 4 * col, &v, 4);
+  }
   section(0);
   m.hot_bytes = uint32_t(img.size());
   m.hot = nullptr;

@@ -1,14 +1,16 @@
-// Environment-per-lane step kernel for sm_100a.
+// Step kernel with compressed per-environment state, for sm_100a.
 //
 // One launch runs every substep of one World.step (src/world/world.zig:694-792).  Each
-// lane owns one environment and runs the whole step for it serially, in exactly the
-// order the reference's dispatch sequence defines (world.zig:934-1293), so no lane ever
-// waits for another: the warp executes one instruction stream for 32 environments of the
-// same model, and every model load is warp-uniform (served by the constant cache from
-// the __grid_constant__ FModel).
+// environment is owned by a group of L lanes (L = 1, 2 or 4) that runs the whole step for
+// it in the order the reference's dispatch sequence defines (world.zig:934-1293).  All
+// environments of a launch share one model, so a warp executes one coherent instruction
+// stream, and the model is read from a per-block shared-memory copy with warp-uniform
+// addresses.  With L = 1 a lane steps its environment alone; with L > 1 the lanes split
+// the constraints of a colour, the contacts of a level, and the per-body / per-pair loops,
+// and meet at __syncwarp on the group mask.
 //
 // Shared memory holds the environment's bodies, joint torques/states and a compressed
-// contact list, laid out [item][lane] so that the 32 lanes of a warp touch 32
+// contact list, laid out [item][environment] so that the groups of a warp touch
 // consecutive words.  The contact list is compressed by two facts of the reference
 // pipeline:
 //  * the narrow phase result of a slot depends only on its geom pair and the body poses
@@ -40,25 +42,27 @@ namespace zb {
 
 // ------------------------------------------------------------------------------------
 // Shared-memory plan: per-environment byte offsets, each section 16-byte aligned.  The
-// block region of a section is (per-env offset) * envs_per_block; element (item, lane)
-// sits at (item * envs_per_block + lane) * element size inside it.
+// block region of a section is (per-env offset) * envs_per_block; element (item, env)
+// sits at (item * envs_per_block + env) * element size inside it.
 // ------------------------------------------------------------------------------------
 struct FPlan {
-  uint32_t pos, quat, vel, ang;               // float4 [B]
-  uint32_t jt, jp, jv;                        // float [J]
-  uint32_t imp;                               // float [M]   normal impulse per slot
-  uint32_t meta;                              // u32 [M]     slot word (below)
-  uint32_t aux;                               // u8 [M]      prev key ranks (substep 0), then hit slots
-  uint32_t pp, nt;                            // float4 [H]  (point, pen), (normal, warm start)
-  uint32_t nlh;                               // u8 [H]      list length at the pair's last hit
-  uint32_t hdr;                               // u32 [4]     count, prev count, prev-separate, unusable
-  uint32_t flags;                             // u32
+  uint32_t pos, quat, vel, ang;  // float4 [B]
+  uint32_t jt, jp, jv;           // float [J]
+  uint32_t imp;                  // float [M]   normal impulse per slot
+  uint32_t meta;                 // u32 [M]     slot word (below)
+  uint32_t aux;                  // u8 [M]      prev key ranks (substep 0), then the contact schedule
+  uint32_t pp, nt;               // float4 [H]  (point, pen), (normal, warm start)
+  uint32_t nlh;                  // u8 [H]      list length at the pair's last hit
+  uint32_t blev;                 // u8 [B]      (L > 1) contact level per body
+  uint32_t lofs;                 // u8 [M + 1]  (L > 1) contact level offsets into the schedule
+  uint32_t hdr;                  // u32 [4]     count, prev count, prev-separate, unusable
+  uint32_t flags;                // u32
   uint32_t bytes;
 };
 
 __host__ __device__ inline uint32_t fa16(uint32_t x) { return (x + 15u) & ~15u; }
 
-__host__ __device__ inline FPlan fast_plan(uint32_t B, uint32_t J, uint32_t M, uint32_t H) {
+__host__ __device__ inline FPlan fast_plan(uint32_t B, uint32_t J, uint32_t M, uint32_t H, uint32_t L) {
   FPlan p;
   uint32_t o = 0;
   const uint32_t b4 = fa16(16u * B), j1 = fa16(4u * J), m4 = fa16(4u * M), m1 = fa16(M), h4 = fa16(16u * H),
@@ -76,13 +80,17 @@ __host__ __device__ inline FPlan fast_plan(uint32_t B, uint32_t J, uint32_t M, u
   p.pp = o, o += h4;
   p.nt = o, o += h4;
   p.nlh = o, o += h1;
+  p.blev = o, o += L > 1 ? fa16(B) : 0u;
+  p.lofs = o, o += L > 1 ? fa16(M + 1) : 0u;
   p.hdr = o, o += 16;
   p.flags = o, o += 16;
   p.bytes = o;
   return p;
 }
 
-uint32_t fast_env_smem_bytes(uint32_t B, uint32_t J, uint32_t M, uint32_t H) { return fast_plan(B, J, M, H).bytes; }
+uint32_t fast_env_smem_bytes(uint32_t B, uint32_t J, uint32_t M, uint32_t H, uint32_t L) {
+  return fast_plan(B, J, M, H, L).bytes;
+}
 
 // Slot word: candidate | origin << 8 | hittable index << 16 (7 bits) | visited << 23 | key rank << 24
 __device__ __forceinline__ uint32_t sw_pair(uint32_t w) { return w & 0xFFu; }
@@ -106,8 +114,8 @@ __device__ __forceinline__ uint32_t lookup_pair(const ModelS& m, uint4 ix) {
   return p;
 }
 
-// Body state of this lane's environment.
-struct LaneBodies {
+// Body state of one environment (stride: environments per block).
+struct EnvBodies {
   float4 *p, *q, *v, *w;
   uint32_t st;
   __device__ __forceinline__ float4& pos(uint32_t b) { return p[b * st]; }
@@ -116,8 +124,37 @@ struct LaneBodies {
   __device__ __forceinline__ float4& ang(uint32_t b) { return w[b * st]; }
 };
 
+// The L lanes that own one environment.  Every group of a warp runs the same sequence
+// of synchronisations (the model fixes the loop bounds; data-dependent ones run to the
+// warp's maximum), so all of them sync and shuffle on one warp-wide mask: __syncwarp with
+// a different mask per group costs about 200 cycles on sm_100a, with one mask a few.
+template <int L>
+struct Group {
+  uint32_t lane;  // 0 .. L-1
+  unsigned mask;  // the lanes of the warp's active groups
+  int src;        // warp lane of the group's lane 0
+  __device__ __forceinline__ void sync() const {
+    if constexpr (L > 1) __syncwarp(mask);
+  }
+  __device__ __forceinline__ uint32_t bcast(uint32_t v) const {
+    if constexpr (L > 1) return __shfl_sync(mask, v, src);
+    return v;
+  }
+  __device__ __forceinline__ uint64_t or_all(uint64_t v) const {
+    if constexpr (L > 1) {
+#pragma unroll
+      for (int o = 1; o < L; o <<= 1) v |= __shfl_xor_sync(mask, v, o);
+    }
+    return v;
+  }
+  __device__ __forceinline__ uint32_t warp_max(uint32_t v) const {
+    if constexpr (L > 1) return __reduce_max_sync(mask, v);
+    return v;
+  }
+};
+
 // Narrow phase of hittable pair h on the current poses.
-__device__ __forceinline__ bool narrow_h(const ModelS& m, uint32_t h, LaneBodies& S, V3& point, V3& normal,
+__device__ __forceinline__ bool narrow_h(const ModelS& m, uint32_t h, EnvBodies& S, V3& point, V3& normal,
                                          float& pen) {
   const uint32_t hi = m.hinfo(h);
   const float4 ga = m.hga(h), gb = m.hgb(h);
@@ -132,93 +169,89 @@ enum : uint32_t {
   kAccWritten = 4u,       // accelerations already written (auto-reset replaced the velocities)
 };
 
-// Everything one lane does for its environment between the cooperative load and store.
-// Returns false when the environment must go to the general kernel (nothing written).
-__device__ __forceinline__ bool run_env(const StepArgs& a, const FModel& f, const FPlan& pl, const unsigned char* hot,
-                                        unsigned char* blk, uint32_t epb, uint32_t l, uint32_t e, uint32_t& flags_out) {
+// Everything a group does for its environment between the cooperative load and store.
+// The block has already handed over the environments this kernel cannot represent.
+template <int L>
+__device__ __forceinline__ void run_env(const StepArgs& a, const FModel& f, const FPlan& pl, const unsigned char* hot,
+                                        unsigned char* blk, uint32_t ne, uint32_t g, const Group<L>& G, uint32_t e,
+                                        uint32_t& flags_out) {
   const ModelS m{hot, f};
   const uint32_t B = a.B, J = a.J, A = a.A, M = a.M, H = f.H, P = f.P;
-  LaneBodies S{reinterpret_cast<float4*>(blk + pl.pos * epb) + l, reinterpret_cast<float4*>(blk + pl.quat * epb) + l,
-               reinterpret_cast<float4*>(blk + pl.vel * epb) + l, reinterpret_cast<float4*>(blk + pl.ang * epb) + l,
-               epb};
+  const uint32_t lane = G.lane;
+  EnvBodies S{reinterpret_cast<float4*>(blk + pl.pos * ne) + g, reinterpret_cast<float4*>(blk + pl.quat * ne) + g,
+              reinterpret_cast<float4*>(blk + pl.vel * ne) + g, reinterpret_cast<float4*>(blk + pl.ang * ne) + g, ne};
   // pose before integration, read back by the velocity update: an L2-resident scratch,
   // [body][pos, quat][env] so that a warp's accesses are contiguous
   const size_t E = a.num_envs;
   float4* ppos = a.pose_scratch + e;
   float4* pquat = a.pose_scratch + E + e;
   const size_t pst = 2 * E;
-  float* jt = reinterpret_cast<float*>(blk + pl.jt * epb) + l;
-  float* jp = reinterpret_cast<float*>(blk + pl.jp * epb) + l;
-  float* jv = reinterpret_cast<float*>(blk + pl.jv * epb) + l;
-  float* imp = reinterpret_cast<float*>(blk + pl.imp * epb) + l;
-  uint32_t* meta = reinterpret_cast<uint32_t*>(blk + pl.meta * epb) + l;
-  uint8_t* aux = blk + pl.aux * epb + l;
-  float4* pp = reinterpret_cast<float4*>(blk + pl.pp * epb) + l;
-  float4* nt = reinterpret_cast<float4*>(blk + pl.nt * epb) + l;
-  uint8_t* nlh = blk + pl.nlh * epb + l;
-
-  uint32_t* hdr = reinterpret_cast<uint32_t*>(blk + pl.hdr * epb) + l;
+  float* jt = reinterpret_cast<float*>(blk + pl.jt * ne) + g;
+  float* jp = reinterpret_cast<float*>(blk + pl.jp * ne) + g;
+  float* jv = reinterpret_cast<float*>(blk + pl.jv * ne) + g;
+  float* imp = reinterpret_cast<float*>(blk + pl.imp * ne) + g;
+  uint32_t* meta = reinterpret_cast<uint32_t*>(blk + pl.meta * ne) + g;
+  uint8_t* aux = blk + pl.aux * ne + g;
+  float4* pp = reinterpret_cast<float4*>(blk + pl.pp * ne) + g;
+  float4* nt = reinterpret_cast<float4*>(blk + pl.nt * ne) + g;
+  uint8_t* nlh = blk + pl.nlh * ne + g;
+  uint8_t* blev = blk + pl.blev * ne + g;
+  uint8_t* lofs = blk + pl.lofs * ne + g;
+  uint32_t* hdr = reinterpret_cast<uint32_t*>(blk + pl.hdr * ne) + g;
 
   // ---------------- contact list of the previous step ----------------
-  // The block loaded the slots (slot words, impulses, previous-list key ranks) and marked
-  // lists whose tuples are not broad-phase candidates.  Both lists are sorted by key
-  // whenever this library wrote them; anything else goes to the general kernel.
-  if (hdr[3 * epb]) return false;
+  // loaded by the block: slot words, impulses, previous-list key ranks
   uint32_t count = hdr[0];
-  const uint32_t prev_count0 = hdr[epb];
-  const bool sep = hdr[2 * epb] != 0;
+  const uint32_t prev_count0 = hdr[ne];
+  const bool sep = hdr[2 * ne] != 0;
   const uint32_t n0 = count < M ? count : M;
   Contact* gc = a.contacts + size_t(e) * M;
   const Contact* gprev = sep ? a.prev_contacts + size_t(e) * M : gc;
   const uint32_t n_prev0 = prev_count0 < M ? prev_count0 : M;
-  uint32_t last = 0;
-  for (uint32_t i = 0; i < n0; ++i) {
-    const uint32_t r = sw_rank(meta[i * epb]);
-    if (r < last) return false;
-    last = r;
-  }
-  last = 0;
-  for (uint32_t j = 0; j < n_prev0; ++j) {  // previous-substep list (cache_contacts, 1454-1478)
-    const uint32_t r = aux[j * epb];
-    if (r < last) return false;
-    last = r;
-  }
-  for (uint32_t h = 0; h < H; ++h) nlh[h * epb] = 0;
+  (void)n0;
+  for (uint32_t h = lane; h < H; h += L) nlh[h * ne] = 0;
 
   const float dt = a.dt, inv_dt = a.inv_dt;
   const V3 grav{a.gravity[0], a.gravity[1], a.gravity[2]};
   const float* act = a.actions + size_t(e) * A;
-  // apply_actions (196-229): the torques are the same in every substep
-  if (a.substeps > 0)
-    for (uint32_t k = 0; k < A; ++k) {
+  // apply_actions (196-229): the torques are the same in every substep; actuators that
+  // share a joint are applied in index order by one lane
+  if (a.substeps > 0) {
+    const uint32_t k0 = a.actuators_unique ? lane : (lane == 0 ? 0u : A);
+    const uint32_t ks = a.actuators_unique ? uint32_t(L) : 1u;
+    for (uint32_t k = k0; k < A; k += ks) {
       const float tq = clampf(act[k], f.a_cmin[k], f.a_cmax[k]) * f.a_gear[k];
-      jt[f.a_joint[k] * epb] = clampf(tq, f.a_fmin[k], f.a_fmax[k]);
+      jt[f.a_joint[k] * ne] = clampf(tq, f.a_fmin[k], f.a_fmax[k]);
     }
+  }
+  G.sync();
 
   uint64_t prev_hit = 0;
   uint32_t n_prev = n_prev0;
+  bool moved = false;  // (lane 0) did sorting move a slot away from its original position
   for (uint32_t s = 0; s < a.substeps; ++s) {
     // ---- kinematic bodies (update_kinematic 304-339; massless, so no gravity wrench) ----
-    for (uint32_t b = 0; b < B; ++b) {
+    for (uint32_t b = lane; b < B; b += L) {
       if ((m.body(b) & 0xFFu) != 1u) continue;
       S.pos(b) = with_w(madd(v3(S.vel(b)), dt, v3(S.pos(b))), 0.0f);
       const float4 q = S.quat(b);
       S.quat(b) = qnormalize(qmadd(qmul_v((v3(S.ang(b)) * dt) * 0.5f, q), 1.0f, q));
     }
+    G.sync();
     // ---- wrench (compute_forces 345-388, apply_joint_forces 122-190) and semi-implicit
     //      Euler (save_prev_state 1900-1913, integrate 394-462), children first: a body's
     //      wrench reads only its own and its parent's orientation, neither yet integrated.
-    //      Four bodies at a time: all their wrenches first, then their integration, so
-    //      the four dependency chains overlap.
+    //      Four bodies per round: all their wrenches first, then their integration.
     for (uint32_t hi_b = B; hi_b > 0;) {
-      constexpr int kC = 4;
-      const uint32_t nc = hi_b < kC ? hi_b : kC;
+      constexpr int kC = 4 / L;  // bodies per lane per round
+      const uint32_t nc = hi_b < 4u ? hi_b : 4u;
       V3 F[kC], T[kC];
       float4 q[kC], x[kC], v0[kC], w0[kC];
 #pragma unroll
       for (int c = 0; c < kC; ++c) {
-        if (uint32_t(c) >= nc) continue;
-        const uint32_t b = hi_b - 1 - c;
+        const uint32_t idx = uint32_t(c) * L + lane;
+        if (idx >= nc) continue;
+        const uint32_t b = hi_b - 1 - idx;
         const float4 mi = m.imi(b);
         q[c] = S.quat(b);
         x[c] = S.pos(b);
@@ -232,7 +265,7 @@ __device__ __forceinline__ bool run_env(const StepArgs& a, const FModel& f, cons
         for (uint32_t k = k0; k < k1; ++k) {
           const uint32_t ent = m.jf(k);
           const uint32_t j = ent & 0x7Fu;
-          const float tau = jt[j * epb];
+          const float tau = jt[j * ne];
           if (fabsf(tau) < 1e-6f) continue;
           const uint32_t ji = m.jinfo(j);
           const V3 fj = rotate(v3(m.jaxis(j)), S.quat((ji >> 8) & 0xFFu)) * tau;
@@ -240,10 +273,12 @@ __device__ __forceinline__ bool run_env(const StepArgs& a, const FModel& f, cons
           else T[c] = (ent & 0x80u) ? T[c] - fj : T[c] + fj;
         }
       }
+      G.sync();
 #pragma unroll
       for (int c = 0; c < kC; ++c) {
-        if (uint32_t(c) >= nc) continue;
-        const uint32_t b = hi_b - 1 - c;
+        const uint32_t idx = uint32_t(c) * L + lane;
+        if (idx >= nc) continue;
+        const uint32_t b = hi_b - 1 - idx;
         const float4 mi = m.imi(b);
         ppos[b * pst] = x[c];
         pquat[b * pst] = q[c];
@@ -255,6 +290,7 @@ __device__ __forceinline__ bool run_env(const StepArgs& a, const FModel& f, cons
         S.ang(b) = with_w(w, 0.0f);
         S.quat(b) = qnormalize(qmadd(qmul_v((w * dt) * 0.5f, q[c]), 1.0f, q[c]));
       }
+      G.sync();
       hi_b -= nc;
     }
     // ---- broad phase (broad_phase 468-533): candidates in emission order ----
@@ -263,7 +299,7 @@ __device__ __forceinline__ bool run_env(const StepArgs& a, const FModel& f, cons
       const uint32_t pn = P - p0 < 64u ? P - p0 : 64u;
       uint64_t pass = 0;
 #pragma unroll 4
-      for (uint32_t i = 0; i < pn; ++i) {
+      for (uint32_t i = lane; i < pn; i += L) {
         const uint32_t p = p0 + i;
         const uint32_t pb = m.pbody(p);
         bool ok = true;
@@ -276,6 +312,7 @@ __device__ __forceinline__ bool run_env(const StepArgs& a, const FModel& f, cons
         }
         pass |= uint64_t(ok) << i;
       }
+      pass = G.or_all(pass);
       if (count >= M) {  // the list is frozen: only the counter advances
         count += uint32_t(__popcll(pass));
         continue;
@@ -283,28 +320,32 @@ __device__ __forceinline__ bool run_env(const StepArgs& a, const FModel& f, cons
       while (pass) {
         const uint32_t i = uint32_t(__ffsll(pass)) - 1u;
         pass &= pass - 1;
-        if (count < M) meta[count * epb] = slot_word(m, p0 + i, count);
+        if (count < M && lane == 0) meta[count * ne] = slot_word(m, p0 + i, count);
         ++count;
       }
     }
     const uint32_t n = count < M ? count : M;
     // ---- stable sort by key (sort_contacts 711-745): insert the new slots in order ----
-    for (uint32_t q = n_old; q < n; ++q) {
-      const uint32_t w = meta[q * epb];
-      const float x = imp[q * epb];
-      uint32_t r = q;
-      while (r > 0 && sw_rank(meta[(r - 1) * epb]) > sw_rank(w)) {
-        meta[r * epb] = meta[(r - 1) * epb];
-        imp[r * epb] = imp[(r - 1) * epb];
-        --r;
+    if (lane == 0) {
+      for (uint32_t q = n_old; q < n; ++q) {
+        const uint32_t w = meta[q * ne];
+        const float x = imp[q * ne];
+        uint32_t r = q;
+        while (r > 0 && sw_rank(meta[(r - 1) * ne]) > sw_rank(w)) {
+          meta[r * ne] = meta[(r - 1) * ne];
+          imp[r * ne] = imp[(r - 1) * ne];
+          --r;
+        }
+        moved |= r != q;
+        meta[r * ne] = w;
+        imp[r * ne] = x;
       }
-      meta[r * epb] = w;
-      imp[r * epb] = x;
     }
+    G.sync();
     // ---- narrow phase + warm start (narrow_phase 751-894, match_cached_contacts
     //      1483-1544), once per hittable pair.  First pass: the match, against the
     //      previous substep's points, which the second pass then overwrites.
-    for (uint32_t h = 0; h < H; ++h) {
+    for (uint32_t h = lane; h < H; h += L) {
       V3 point, normal;
       float pen;
       if (!narrow_h(m, h, S, point, normal, pen)) continue;
@@ -316,10 +357,10 @@ __device__ __forceinline__ bool run_env(const StepArgs& a, const FModel& f, cons
         uint32_t lo = 0, hi = n_prev;  // first previous slot with key >= this key
         while (lo < hi) {
           const uint32_t mid = (lo + hi) >> 1;
-          if (aux[mid * epb] < rank) lo = mid + 1;
+          if (aux[mid * ne] < rank) lo = mid + 1;
           else hi = mid;
         }
-        for (uint32_t j = lo; j < n_prev && aux[j * epb] == rank; ++j) {
+        for (uint32_t j = lo; j < n_prev && aux[j * ne] == rank; ++j) {
           const float4 q = *reinterpret_cast<const float4*>(gprev[j].position_pen);
           if (q.w < 0.0f) continue;
           const V3 d = xyz(q) - point;
@@ -329,94 +370,160 @@ __device__ __forceinline__ bool run_env(const StepArgs& a, const FModel& f, cons
             js = int(j);
           }
         }
-        if (js >= 0) {
-          const float4 pi = *reinterpret_cast<const float4*>(gprev[js].impulses);
-          // tangent impulses are never written by the solver; a stored non-zero value
-          // would have to be carried per slot, which only the general kernel does
-          if ((__float_as_uint(pi.y) | __float_as_uint(pi.z)) != 0u) return false;
-          val = pi.x * 0.8f;
-        }
+        // (tangent impulses of valid previous slots are zero: the block checked)
+        if (js >= 0) val = gprev[js].impulses[0] * 0.8f;
       } else {
         uint32_t lo = 0, hi = n;
         while (lo < hi) {
           const uint32_t mid = (lo + hi) >> 1;
-          if (sw_rank(meta[mid * epb]) < rank) lo = mid + 1;
+          if (sw_rank(meta[mid * ne]) < rank) lo = mid + 1;
           else hi = mid;
         }
         for (uint32_t j = lo; j < n; ++j) {
-          const uint32_t w = meta[j * epb];
+          const uint32_t w = meta[j * ne];
           if (sw_rank(w) != rank) break;
           if (sw_origin(w) >= n_prev) continue;  // appended in this substep
           const uint32_t hj = sw_hit(w);
           if (hj == fm::kNoHit || !((prev_hit >> hj) & 1ull)) continue;
-          const V3 d = xyz(pp[hj * epb]) - point;
+          const V3 d = xyz(pp[hj * ne]) - point;
           const float dsq = dot(d, d);
           if (dsq < best) {
             best = dsq;
             js = int(j);
           }
         }
-        if (js >= 0) val = imp[uint32_t(js) * epb] * 0.8f;
+        if (js >= 0) val = imp[uint32_t(js) * ne] * 0.8f;
       }
-      reinterpret_cast<float*>(&nt[h * epb])[3] = val;
+      reinterpret_cast<float*>(&nt[h * ne])[3] = val;
     }
+    G.sync();
     uint64_t hit_now = 0;
-    for (uint32_t h = 0; h < H; ++h) {
+    for (uint32_t h = lane; h < H; h += L) {
       V3 point, normal;
       float pen;
       if (narrow_h(m, h, S, point, normal, pen)) {
-        pp[h * epb] = with_w(point, pen);
-        const float warm = nt[h * epb].w;
-        nt[h * epb] = with_w(normal, warm);
-        nlh[h * epb] = uint8_t(n);
+        pp[h * ne] = with_w(point, pen);
+        const float warm = nt[h * ne].w;
+        nt[h * ne] = with_w(normal, warm);
+        nlh[h * ne] = uint8_t(n);
         hit_now |= 1ull << h;
       } else {
-        reinterpret_cast<float*>(&pp[h * epb])[3] = -1.0f;
+        reinterpret_cast<float*>(&pp[h * ne])[3] = -1.0f;
       }
     }
-    // slot impulses (narrow zeroes them, a match warm-starts them) and the hit-slot list
-    uint32_t nh = 0;
-    for (uint32_t i = 0; i < n; ++i) {
-      const uint32_t hh = sw_hit(meta[i * epb]);
-      if (hh != fm::kNoHit && ((hit_now >> hh) & 1ull)) {
-        imp[i * epb] = nt[hh * epb].w;
-        aux[nh * epb] = uint8_t(i);
-        ++nh;
-      }
+    hit_now = G.or_all(hit_now);
+    G.sync();
+    // slot impulses (narrow zeroes them, a match warm-starts them)
+    for (uint32_t i = lane; i < n; i += L) {
+      const uint32_t hh = sw_hit(meta[i * ne]);
+      if (hh != fm::kNoHit && ((hit_now >> hh) & 1ull)) imp[i * ne] = nt[hh * ne].w;
     }
-    // ---- XPBD joints (solve_joints 909-1399), colour by colour in batches ----
-    for (uint32_t it = 0; it < a.iterations; ++it)
-      for (uint32_t q = 0; q < a.K; ++q) solve_constraint(m, m.constraint(q), S);
-    // ---- contacts in slot order (solve_contacts 1644-1793) ----
-    for (uint32_t it = 0; it < a.iterations; ++it)
-      for (uint32_t v = 0; v < nh; ++v) {
-        const uint32_t i = aux[v * epb];
-        const uint32_t hh = sw_hit(meta[i * epb]);
-        const uint32_t hi = m.hinfo(hh);
-        const float4 nn = nt[hh * epb];
-        float jx = imp[i * epb];
-        solve_contact(m, pp[hh * epb], make_float4(nn.x, nn.y, nn.z, m.hfr(hh)), jx, a.restitution, (hi >> 16) & 0xFFu,
-                      hi >> 24, S, dt, a.baumgarte, a.slop);
-        imp[i * epb] = jx;
+    // contact schedule.  L = 1: the hit slots in slot order.  L > 1: the hit slots by
+    // level -- a slot's level is one more than the highest level of an earlier hit slot
+    // sharing a dynamic body -- stable within a level; solving level by level, a level's
+    // slots in parallel, equals solving the slots one after another in slot order.
+    uint32_t nh = 0, nlev = 0, nlev_w = 0;
+    if constexpr (L == 1) {
+      for (uint32_t i = 0; i < n; ++i) {
+        const uint32_t hh = sw_hit(meta[i * ne]);
+        if (hh != fm::kNoHit && ((hit_now >> hh) & 1ull)) aux[nh++ * ne] = uint8_t(i);
       }
+    } else {
+      if (lane == 0) {
+        for (int pass = 0; pass < 2; ++pass) {  // pass 0 counts per level, pass 1 places
+          for (uint32_t b = 0; b < B; ++b) blev[b * ne] = 0;
+          if (pass == 1) {
+            uint32_t acc = 0;
+            for (uint32_t v = 0; v <= nlev; ++v) {
+              const uint32_t c = lofs[v * ne];
+              lofs[v * ne] = uint8_t(acc);
+              acc += c;
+            }
+          } else {
+            for (uint32_t v = 0; v <= n; ++v) lofs[v * ne] = 0;
+          }
+          for (uint32_t i = 0; i < n; ++i) {
+            const uint32_t hh = sw_hit(meta[i * ne]);
+            if (hh == fm::kNoHit || !((hit_now >> hh) & 1ull)) continue;
+            const uint32_t hi = m.hinfo(hh);
+            const uint32_t ba = (hi >> 16) & 0xFFu, bb = hi >> 24;
+            const bool da = m.imi(ba).x > 1e-8f, db = m.imi(bb).x > 1e-8f;
+            uint32_t lv = 0;
+            if (da && blev[ba * ne] > lv) lv = blev[ba * ne];
+            if (db && blev[bb * ne] > lv) lv = blev[bb * ne];
+            if (da) blev[ba * ne] = uint8_t(lv + 1);
+            if (db) blev[bb * ne] = uint8_t(lv + 1);
+            if (pass == 0) {
+              lofs[lv * ne] = uint8_t(lofs[lv * ne] + 1);
+              if (lv + 1 > nlev) nlev = lv + 1;
+            } else {
+              aux[lofs[lv * ne] * ne] = uint8_t(i);
+              lofs[lv * ne] = uint8_t(lofs[lv * ne] + 1);
+            }
+          }
+        }
+        // lofs[v] now holds the end of level v: shift to starts with lofs[nlev] = end
+        for (uint32_t v = nlev; v > 0; --v) lofs[v * ne] = lofs[(v - 1) * ne];
+        lofs[0] = 0;
+      }
+      nlev = G.bcast(nlev);
+      nlev_w = G.warp_max(nlev);  // every group of the warp runs as many levels (and syncs)
+      G.sync();
+    }
+    // ---- XPBD joints (solve_joints 909-1399) ----
+    if constexpr (L == 1) {  // one after another in colour-sorted order (= colour by colour)
+      for (uint32_t it = 0; it < a.iterations; ++it)
+        for (uint32_t k = 0; k < a.K; ++k) solve_constraint(m, m.constraint(k), S);
+    } else {  // colour by colour, a colour's constraints (disjoint bodies) across the lanes
+      for (uint32_t it = 0; it < a.iterations; ++it)
+        for (uint32_t col = 0; col < f.num_colors; ++col) {
+          const uint32_t cr = m.color(col);
+          const uint32_t k0 = cr & 0xFFFFu, k1 = k0 + (cr >> 16);
+          for (uint32_t k = k0 + lane; k < k1; k += L) solve_constraint(m, m.constraint(k), S);
+          G.sync();
+        }
+    }
+    // ---- contacts (solve_contacts 1644-1793) ----
+    auto contact = [&](uint32_t i) {
+      const uint32_t hh = sw_hit(meta[i * ne]);
+      const uint32_t hi = m.hinfo(hh);
+      const float4 nn = nt[hh * ne];
+      float jx = imp[i * ne];
+      solve_contact(m, pp[hh * ne], make_float4(nn.x, nn.y, nn.z, m.hfr(hh)), jx, a.restitution, (hi >> 16) & 0xFFu,
+                    hi >> 24, S, dt, a.baumgarte, a.slop);
+      imp[i * ne] = jx;
+    };
+    if constexpr (L == 1) {
+      for (uint32_t it = 0; it < a.iterations; ++it)
+        for (uint32_t v = 0; v < nh; ++v) contact(aux[v * ne]);
+    } else {
+      for (uint32_t it = 0; it < a.iterations; ++it)
+        for (uint32_t lv = 0; lv < nlev_w; ++lv) {
+          const uint32_t v0 = lv < nlev ? lofs[lv * ne] : 0u, v1 = lv < nlev ? lofs[(lv + 1) * ne] : 0u;
+          for (uint32_t v = v0 + lane; v < v1; v += L) contact(aux[v * ne]);
+          G.sync();
+        }
+    }
     // ---- velocities from the position change (xpbd_update_velocities 1922-1961) ----
-    for (uint32_t b = 0; b < B; ++b) {
+    for (uint32_t b = lane; b < B; b += L) {
       if (m.imi(b).x < 1e-8f) continue;
       S.vel(b) = with_w((v3(S.pos(b)) - v3(ppos[b * pst])) * inv_dt, 0.0f);
       float4 dq = qmul(S.quat(b), qconj(pquat[b * pst]));
       if (dq.w < 0.0f) dq = qneg(dq);
       S.ang(b) = with_w((xyz(dq) * 2.0f) * inv_dt, 0.0f);
     }
+    G.sync();
     prev_hit = hit_now;
     n_prev = n;
   }
+  moved = G.bcast(moved ? 1u : 0u) != 0;
 
   // ---------------- joint states and sensors from the final substep ----------------
   uint32_t flags = 0;
   const bool stepped = a.substeps > 0;
   const bool publish = a.step_mask == nullptr || a.step_mask[e] != 0;
   if (stepped) {
-    for (uint32_t j = 0; j < J; ++j) {  // update_joint_states 1550-1638
+    for (uint32_t j = lane; j < J; j += L) {  // update_joint_states 1550-1638
       const uint32_t ji = m.jinfo(j);
       const uint32_t ty = ji & 0xFFu, ia = (ji >> 8) & 0xFFu, ib = (ji >> 16) & 0xFFu;
       float p = 0.0f, v = 0.0f;
@@ -435,18 +542,19 @@ __device__ __forceinline__ bool run_env(const StepArgs& a, const FModel& f, cons
         const V3 vpa = v3(S.vel(ia)) + cross(v3(S.ang(ia)), ra), vpb = v3(S.vel(ib)) + cross(v3(S.ang(ib)), rb);
         v = dot(vpb - vpa, aw);
       }
-      jp[j * epb] = p;
-      jv[j * epb] = v;
+      jp[j * ne] = p;
+      jv[j * ne] = v;
     }
+    G.sync();
     if (publish) {  // read_sensors 1799-1893
       float* gobs = a.obs + size_t(e) * a.obs_dim;
-      for (uint32_t si = 0; si < a.S; ++si) {
+      for (uint32_t si = lane; si < a.S; si += L) {
         const uint32_t sinfo = f.s_info[si];
         const uint32_t o = (sinfo >> 8) & 0xFFu;
         float* out = gobs + (sinfo >> 16);
         switch (sinfo & 0xFFu) {
-          case 0: out[0] = jp[o * epb]; break;
-          case 1: out[0] = jv[o * epb]; break;
+          case 0: out[0] = jp[o * ne]; break;
+          case 1: out[0] = jv[o * ne]; break;
           case 2: {
             const V3 lg = rotate(grav, qconj(S.quat(o)));
             out[0] = lg.x, out[1] = lg.y, out[2] = lg.z;
@@ -481,33 +589,35 @@ __device__ __forceinline__ bool run_env(const StepArgs& a, const FModel& f, cons
     // ---------------- contact slots back to memory ----------------
     // A slot whose pair made contact while the slot was in the list carries that pair's
     // last contact; any other slot keeps the record stored at its original position,
-    // marked invalid.  Sorting may have moved slots, so the in-place write follows the
-    // permutation's cycles.
+    // marked invalid.  When sorting moved slots, the in-place write follows the
+    // permutation's cycles (one lane) so that no record is overwritten before it is read.
     const uint32_t n_fin = count < M ? count : M;
     Contact* dst = publish ? gc : a.prev_contacts + size_t(e) * M;
     const bool inplace = publish;
-    for (uint32_t i = 0; i < n_fin; ++i) {
-      if (meta[i * epb] & kVisited) continue;
+    const uint32_t i0 = moved ? (lane == 0 ? 0u : n_fin) : lane;
+    const uint32_t istep = moved ? 1u : uint32_t(L);
+    for (uint32_t i = i0; i < n_fin; i += istep) {
+      if (meta[i * ne] & kVisited) continue;
       uint4 saved[4];
-      const uint32_t oi = sw_origin(meta[i * epb]);
+      const uint32_t oi = sw_origin(meta[i * ne]);
       const bool cycle = inplace && oi != i;
       if (cycle)
         for (int c = 0; c < 4; ++c) saved[c] = reinterpret_cast<const uint4*>(gc + i)[c];
       uint32_t j = i;
       for (uint32_t guard = 0; guard < n_fin; ++guard) {
-        const uint32_t w = meta[j * epb];
-        meta[j * epb] = w | kVisited;
+        const uint32_t w = meta[j * ne];
+        meta[j * ne] = w | kVisited;
         const uint32_t p = sw_pair(w), o = sw_origin(w), hh = sw_hit(w);
         const uint32_t pi = m.pinfo(p), pbody = m.pbody(p);
         const uint4 idx = make_uint4(pbody & 0xFFu, (pbody >> 8) & 0xFFu, pi & 0xFFu, (pi >> 8) & 0xFFu);
         uint4* out = reinterpret_cast<uint4*>(dst + j);
-        if (hh != fm::kNoHit && o < nlh[hh * epb]) {
-          const float4 nn = nt[hh * epb];
-          out[0] = *reinterpret_cast<const uint4*>(&pp[hh * epb]);
+        if (hh != fm::kNoHit && o < nlh[hh * ne]) {
+          const float4 nn = nt[hh * ne];
+          out[0] = *reinterpret_cast<const uint4*>(&pp[hh * ne]);
           const float4 nf = make_float4(nn.x, nn.y, nn.z, m.hfr(hh));
           out[1] = *reinterpret_cast<const uint4*>(&nf);
           out[2] = idx;
-          const float4 im = make_float4(imp[j * epb], 0.0f, 0.0f, a.restitution);
+          const float4 im = make_float4(imp[j * ne], 0.0f, 0.0f, a.restitution);
           out[3] = *reinterpret_cast<const uint4*>(&im);
         } else if (inplace && o == j) {
           reinterpret_cast<float*>(out)[3] = -1.0f;
@@ -529,123 +639,128 @@ __device__ __forceinline__ bool run_env(const StepArgs& a, const FModel& f, cons
     }
   }
 
-  // ---------------- caches, counters, task extension ----------------
+  // ---------------- caches, counters, task extension (one lane) ----------------
+  G.sync();
   if (!publish) {
     // step_subset: an env outside the mask keeps its public state, but the reference
     // still advanced its contact cache (world.zig:833-929 restores only public buffers).
-    if (stepped) {
+    if (stepped && lane == 0) {
       a.prev_counts[e] = count;
       a.prev_sep[e] = 1;
     }
     flags_out = flags | kSkipState;
-    return true;
+    return;
   }
-  uint32_t count_out = count;
   if (stepped) flags |= kWriteJointState;
-  if (a.task.enabled) {
-    const DTask& tk = a.task;
-    const uint32_t tb = tk.body;
-    const float z = S.pos(tb).z;
-    const bool done = !(z >= tk.z_min && z <= tk.z_max);
-    float ctrl = 0.0f;
-    for (uint32_t k = 0; k < A; ++k) ctrl = fma_(act[k], act[k], ctrl);
-    float r = fma_(tk.forward_weight, S.vel(tb).x, tk.alive_bonus);
-    r = fma_(-tk.ctrl_cost, ctrl, r);
-    a.rewards[e] = r;
-    a.dones[e] = done ? 1 : 0;
-    if (done && tk.auto_reset) {
-      // accelerations of the step just taken, before the state is replaced
-      const float4* gv0 = reinterpret_cast<const float4*>(a.vel) + size_t(e) * B;
-      float4* gacc = reinterpret_cast<float4*>(a.acc) + size_t(e) * B;
-      for (uint32_t b = 0; b < B; ++b) {
-        const float4 v0 = gv0[b], v1 = S.vel(b);
-        gacc[b] = make_float4((v1.x - v0.x) * a.inv_step, (v1.y - v0.y) * a.inv_step, (v1.z - v0.z) * a.inv_step, 0.0f);
-      }
-      flags |= kAccWritten | kWriteJointState;
-      // FK-consistent noisy reset from the initial template
-      const uint32_t ep = a.episode[e];
-      const float* t = a.init_state;
-      for (uint32_t b = 0; b < B; ++b) {
-        S.pos(b) = reinterpret_cast<const float4*>(t)[b];
-        S.quat(b) = reinterpret_cast<const float4*>(t)[B + b];
-        S.vel(b) = reinterpret_cast<const float4*>(t)[2 * B + b];
-        S.ang(b) = reinterpret_cast<const float4*>(t)[3 * B + b];
-      }
-      for (uint32_t j = 0; j < J; ++j) {
-        jp[j * epb] = t[16 * B + j];
-        jv[j * epb] = t[16 * B + J + j];
-      }
-      if (tk.noise != 0.0f) {
-        const uint64_t genv = uint64_t(e) + tk.env_offset;
-        const uint32_t rb = tk.body;
-        float4 x = S.pos(rb);
-        x.x = x.x + tk.noise * uniform_pm1(tk.seed, genv, ep, 0u);
-        x.y = x.y + tk.noise * uniform_pm1(tk.seed, genv, ep, 1u);
-        x.z = x.z + tk.noise * uniform_pm1(tk.seed, genv, ep, 2u);
-        S.pos(rb) = x;
+  if (lane == 0) {
+    uint32_t count_out = count;
+    if (a.task.enabled) {
+      const DTask& tk = a.task;
+      const uint32_t tb = tk.body;
+      const float z = S.pos(tb).z;
+      const bool done = !(z >= tk.z_min && z <= tk.z_max);
+      float ctrl = 0.0f;
+      for (uint32_t k = 0; k < A; ++k) ctrl = fma_(act[k], act[k], ctrl);
+      float r = fma_(tk.forward_weight, S.vel(tb).x, tk.alive_bonus);
+      r = fma_(-tk.ctrl_cost, ctrl, r);
+      a.rewards[e] = r;
+      a.dones[e] = done ? 1 : 0;
+      if (done && tk.auto_reset) {
+        // accelerations of the step just taken, before the state is replaced
+        const float4* gv0 = reinterpret_cast<const float4*>(a.vel) + size_t(e) * B;
+        float4* gacc = reinterpret_cast<float4*>(a.acc) + size_t(e) * B;
+        for (uint32_t b = 0; b < B; ++b) {
+          const float4 v0 = gv0[b], v1 = S.vel(b);
+          gacc[b] = make_float4((v1.x - v0.x) * a.inv_step, (v1.y - v0.y) * a.inv_step, (v1.z - v0.z) * a.inv_step, 0.0f);
+        }
+        flags |= kAccWritten | kWriteJointState;
+        // FK-consistent noisy reset from the initial template
+        const uint32_t ep = a.episode[e];
+        const float* t = a.init_state;
+        for (uint32_t b = 0; b < B; ++b) {
+          S.pos(b) = reinterpret_cast<const float4*>(t)[b];
+          S.quat(b) = reinterpret_cast<const float4*>(t)[B + b];
+          S.vel(b) = reinterpret_cast<const float4*>(t)[2 * B + b];
+          S.ang(b) = reinterpret_cast<const float4*>(t)[3 * B + b];
+        }
         for (uint32_t j = 0; j < J; ++j) {
-          const uint32_t ji = m.jinfo(j);
-          if ((ji & 0xFFu) != 1u) continue;
-          const float th = tk.noise * uniform_pm1(tk.seed, genv, ep, 3u + j);
-          const uint32_t pa = (ji >> 8) & 0xFFu, ch = (ji >> 16) & 0xFFu;
-          const float4 qp = S.quat(pa);
-          const V3 anchor = v3(S.pos(pa)) + rotate(v3(f.j_ap[j]), qp);
-          const V3 ax = rotate(v3(m.jaxis(j)), qp);
-          const float al = len(ax);
-          if (!(al > 1e-8f)) continue;
-          const V3 hv = ax * __fdiv_rn(0.5f * th, al);
-          const float4 qr = qnormalize(make_float4(hv.x, hv.y, hv.z, 1.0f));
-          const uint32_t end = ch + (m.body(ch) >> 24);
-          for (uint32_t d = ch; d < end; ++d) {
-            const V3 rel = v3(S.pos(d)) - anchor;
-            S.pos(d) = with_w(anchor + rotate(rel, qr), S.pos(d).w);
-            S.quat(d) = qnormalize(qmul(qr, S.quat(d)));
+          jp[j * ne] = t[16 * B + j];
+          jv[j * ne] = t[16 * B + J + j];
+        }
+        if (tk.noise != 0.0f) {
+          const uint64_t genv = uint64_t(e) + tk.env_offset;
+          const uint32_t rb = tk.body;
+          float4 x = S.pos(rb);
+          x.x = x.x + tk.noise * uniform_pm1(tk.seed, genv, ep, 0u);
+          x.y = x.y + tk.noise * uniform_pm1(tk.seed, genv, ep, 1u);
+          x.z = x.z + tk.noise * uniform_pm1(tk.seed, genv, ep, 2u);
+          S.pos(rb) = x;
+          for (uint32_t j = 0; j < J; ++j) {
+            const uint32_t ji = m.jinfo(j);
+            if ((ji & 0xFFu) != 1u) continue;
+            const float th = tk.noise * uniform_pm1(tk.seed, genv, ep, 3u + j);
+            const uint32_t pa = (ji >> 8) & 0xFFu, ch = (ji >> 16) & 0xFFu;
+            const float4 qp = S.quat(pa);
+            const V3 anchor = v3(S.pos(pa)) + rotate(v3(f.j_ap[j]), qp);
+            const V3 ax = rotate(v3(m.jaxis(j)), qp);
+            const float al = len(ax);
+            if (!(al > 1e-8f)) continue;
+            const V3 hv = ax * __fdiv_rn(0.5f * th, al);
+            const float4 qr = qnormalize(make_float4(hv.x, hv.y, hv.z, 1.0f));
+            const uint32_t end = ch + (m.body(ch) >> 24);
+            for (uint32_t d = ch; d < end; ++d) {
+              const V3 rel = v3(S.pos(d)) - anchor;
+              S.pos(d) = with_w(anchor + rotate(rel, qr), S.pos(d).w);
+              S.quat(d) = qnormalize(qmul(qr, S.quat(d)));
+            }
           }
         }
+        a.episode[e] = ep + 1;
+        count_out = 0;
       }
-      a.episode[e] = ep + 1;
-      count_out = 0;
+    }
+    a.counts[e] = count_out;
+    if (stepped) {
+      a.prev_counts[e] = count;
+      a.prev_sep[e] = 0;
     }
   }
-  a.counts[e] = count_out;
-  if (stepped) {
-    a.prev_counts[e] = count;
-    a.prev_sep[e] = 0;
-  }
   flags_out = flags;
-  return true;
 }
 
-__global__ void __launch_bounds__(32) fast_step_kernel(const __grid_constant__ StepArgs a,
-                                                       const __grid_constant__ FModel f) {
+// blockDim.x = envs_per_block * L threads (envs_per_block <= 32); group g (= threadIdx.x / L)
+// owns env e0 + g.
+template <int L>
+__global__ void __launch_bounds__(32 * L) fast_step_kernel(const __grid_constant__ StepArgs a,
+                                                        const __grid_constant__ FModel f) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  const uint32_t epb = blockDim.x, l = threadIdx.x;
-  const uint32_t e0 = blockIdx.x * epb;
+  const uint32_t nt = blockDim.x, tid = threadIdx.x;
+  const uint32_t ne = nt / L;  // environments per block
+  const uint32_t e0 = blockIdx.x * ne;
   if (e0 >= a.num_envs) return;
-  const uint32_t nb = min(epb, a.num_envs - e0);
-  const unsigned wmask = epb == 32 ? 0xFFFFFFFFu : ((1u << epb) - 1u);
+  const uint32_t nb = min(ne, a.num_envs - e0);
   const uint32_t B = a.B, J = a.J, M = a.M;
-  const FPlan pl = fast_plan(B, J, M, f.H);
+  const FPlan pl = fast_plan(B, J, M, f.H, L);
   // shared memory: the model's hot image, then the per-environment sections
   unsigned char* hot = smem_raw;
   unsigned char* blk = smem_raw + f.hot_bytes;
-  for (uint32_t t = l; t < f.hot_bytes / 16u; t += epb) reinterpret_cast<uint4*>(hot)[t] = f.hot[t];
-  __syncwarp(wmask);
+  for (uint32_t t = tid; t < f.hot_bytes / 16u; t += nt) reinterpret_cast<uint4*>(hot)[t] = f.hot[t];
+  __syncthreads();
   // gravity force per body for this step (compute_forces 345-388): g / (1/m), zero when massless
-  for (uint32_t b = l; b < B; b += epb) {
+  for (uint32_t b = tid; b < B; b += nt) {
     const float4 mi = reinterpret_cast<const float4*>(hot + f.o_imi)[b];
-    const V3 g{a.gravity[0], a.gravity[1], a.gravity[2]};
+    const V3 gv{a.gravity[0], a.gravity[1], a.gravity[2]};
     reinterpret_cast<float4*>(hot + f.o_gforce)[b] =
-        mi.x < 1e-8f ? make_float4(0.0f, 0.0f, 0.0f, 0.0f) : with_w(g * rcp_(mi.x), 0.0f);
+        mi.x < 1e-8f ? make_float4(0.0f, 0.0f, 0.0f, 0.0f) : with_w(gv * rcp_(mi.x), 0.0f);
   }
-  float4* s_pos = reinterpret_cast<float4*>(blk + pl.pos * epb);
-  float4* s_quat = reinterpret_cast<float4*>(blk + pl.quat * epb);
-  float4* s_vel = reinterpret_cast<float4*>(blk + pl.vel * epb);
-  float4* s_ang = reinterpret_cast<float4*>(blk + pl.ang * epb);
-  float* s_jt = reinterpret_cast<float*>(blk + pl.jt * epb);
-  float* s_jp = reinterpret_cast<float*>(blk + pl.jp * epb);
-  float* s_jv = reinterpret_cast<float*>(blk + pl.jv * epb);
-  uint32_t* s_flags = reinterpret_cast<uint32_t*>(blk + pl.flags * epb);
+  float4* s_pos = reinterpret_cast<float4*>(blk + pl.pos * ne);
+  float4* s_quat = reinterpret_cast<float4*>(blk + pl.quat * ne);
+  float4* s_vel = reinterpret_cast<float4*>(blk + pl.vel * ne);
+  float4* s_ang = reinterpret_cast<float4*>(blk + pl.ang * ne);
+  float* s_jt = reinterpret_cast<float*>(blk + pl.jt * ne);
+  float* s_jp = reinterpret_cast<float*>(blk + pl.jp * ne);
+  float* s_jv = reinterpret_cast<float*>(blk + pl.jv * ne);
+  uint32_t* s_flags = reinterpret_cast<uint32_t*>(blk + pl.flags * ne);
 
   // ---- coalesced load of the block's body state and joint torques ----
   const size_t eb = size_t(e0) * B;
@@ -654,8 +769,8 @@ __global__ void __launch_bounds__(32) fast_step_kernel(const __grid_constant__ S
   float4* gvel = reinterpret_cast<float4*>(a.vel) + eb;
   float4* gang = reinterpret_cast<float4*>(a.angvel) + eb;
   float4* gacc = reinterpret_cast<float4*>(a.acc) + eb;
-  for (uint32_t t = l; t < nb * B; t += epb) {
-    const uint32_t el = t / B, b = t - el * B, si = b * epb + el;
+  for (uint32_t t = tid; t < nb * B; t += nt) {
+    const uint32_t el = t / B, b = t - el * B, si = b * ne + el;
     s_pos[si] = gpos[t];
     s_quat[si] = gquat[t];
     s_vel[si] = gvel[t];
@@ -664,75 +779,95 @@ __global__ void __launch_bounds__(32) fast_step_kernel(const __grid_constant__ S
   float* gjt = a.jtorque + size_t(e0) * J;
   float* gjp = a.jpos + size_t(e0) * J;
   float* gjv = a.jvel + size_t(e0) * J;
-  for (uint32_t t = l; t < nb * J; t += epb) {
+  for (uint32_t t = tid; t < nb * J; t += nt) {
     const uint32_t el = t / J, j = t - el * J;
-    s_jt[j * epb + el] = gjt[t];
+    s_jt[j * ne + el] = gjt[t];
   }
   // ---- contact list headers, then the slots: slot words, impulses, previous-list ranks ----
-  uint32_t* s_hdr = reinterpret_cast<uint32_t*>(blk + pl.hdr * epb);
-  float* s_imp = reinterpret_cast<float*>(blk + pl.imp * epb);
-  uint32_t* s_meta = reinterpret_cast<uint32_t*>(blk + pl.meta * epb);
-  uint8_t* s_aux = blk + pl.aux * epb;
-  if (l < nb) {
-    const uint32_t e = e0 + l;
-    s_hdr[l] = a.counts[e];
-    s_hdr[epb + l] = a.prev_counts[e];
-    s_hdr[2 * epb + l] = a.prev_sep[e];
-    s_hdr[3 * epb + l] = 0;
+  uint32_t* s_hdr = reinterpret_cast<uint32_t*>(blk + pl.hdr * ne);
+  float* s_imp = reinterpret_cast<float*>(blk + pl.imp * ne);
+  uint32_t* s_meta = reinterpret_cast<uint32_t*>(blk + pl.meta * ne);
+  uint8_t* s_aux = blk + pl.aux * ne;
+  for (uint32_t el = tid; el < nb; el += nt) {
+    const uint32_t e = e0 + el;
+    s_hdr[el] = a.counts[e];
+    s_hdr[ne + el] = a.prev_counts[e];
+    s_hdr[2 * ne + el] = a.prev_sep[e];
+    s_hdr[3 * ne + el] = 0;
   }
-  __syncwarp(wmask);
+  __syncthreads();
   const ModelS m{hot, f};
   const Contact* gcb = a.contacts + size_t(e0) * M;
   constexpr uint32_t kU = 4;  // slots per thread per round: their loads are in flight together
-  for (uint32_t t0 = l; t0 < nb * M; t0 += kU * epb) {
-    uint4 ix[kU], px[kU];
-    float im[kU];
+  // An environment is handed over (s_hdr[3] set) when a slot tuple of either list is not
+  // a broad-phase candidate, when a list is not sorted by key, or when a valid previous
+  // slot carries non-zero tangent impulses (a warm start would copy them; this kernel
+  // keeps only normal impulses).  This library never writes any of these.
+  for (uint32_t t0 = tid; t0 < nb * M; t0 += kU * nt) {
+    uint4 ix[kU], px[kU], pim[kU];
+    float im[kU], ppen[kU];
 #pragma unroll
     for (uint32_t u = 0; u < kU; ++u) {
-      const uint32_t t = t0 + u * epb;
+      const uint32_t t = t0 + u * nt;
       if (t >= nb * M) continue;
       const uint32_t el = t / M, i = t - el * M;
       ix[u] = *reinterpret_cast<const uint4*>(gcb[t].indices);
       im[u] = gcb[t].impulses[0];
-      if (s_hdr[2 * epb + el] != 0 && i < s_hdr[epb + el])
-        px[u] = *reinterpret_cast<const uint4*>(a.prev_contacts[size_t(e0 + el) * M + i].indices);
-      else
-        px[u] = ix[u];
+      const Contact* pr = (s_hdr[2 * ne + el] != 0 && i < s_hdr[ne + el]) ? a.prev_contacts + size_t(e0 + el) * M + i
+                                                                          : gcb + t;
+      px[u] = *reinterpret_cast<const uint4*>(pr->indices);
+      pim[u] = *reinterpret_cast<const uint4*>(pr->impulses);
+      ppen[u] = pr->position_pen[3];
     }
 #pragma unroll
     for (uint32_t u = 0; u < kU; ++u) {
-      const uint32_t t = t0 + u * epb;
+      const uint32_t t = t0 + u * nt;
       if (t >= nb * M) continue;
       const uint32_t el = t / M, i = t - el * M;
-      s_imp[i * epb + el] = im[u];
+      s_imp[i * ne + el] = im[u];
       if (i < s_hdr[el]) {  // i < min(count, M)
         const uint32_t p = lookup_pair(m, ix[u]);
-        if (p == fm::kNoPair) s_hdr[3 * epb + el] = 1;
-        else s_meta[i * epb + el] = slot_word(m, p, i);
+        if (p == fm::kNoPair) s_hdr[3 * ne + el] = 1;
+        else s_meta[i * ne + el] = slot_word(m, p, i);
       }
-      if (i < s_hdr[epb + el]) {  // previous list
+      if (i < s_hdr[ne + el]) {  // previous list
         const uint32_t p = lookup_pair(m, px[u]);
-        if (p == fm::kNoPair) s_hdr[3 * epb + el] = 1;
-        else s_aux[i * epb + el] = uint8_t(m.pinfo(p) >> 24);
+        if (p == fm::kNoPair || (!(ppen[u] < 0.0f) && (pim[u].y | pim[u].z) != 0u)) s_hdr[3 * ne + el] = 1;
+        else s_aux[i * ne + el] = uint8_t(m.pinfo(p) >> 24);
       }
     }
   }
-  __syncwarp(wmask);
-
-  if (l < nb) {
-    uint32_t flags = kSkipState;
-    const uint32_t e = e0 + l;
-    if (!run_env(a, f, pl, hot, blk, epb, l, e, flags)) {
-      flags = kSkipState;
-      a.odd_list[atomicAdd(a.odd_count, 1u)] = e;
-    }
-    s_flags[l] = flags;
+  __syncthreads();
+  for (uint32_t t = tid; t < nb * M; t += nt) {  // both lists sorted by key
+    const uint32_t el = t / M, i = t - el * M;
+    if (i == 0 || s_hdr[3 * ne + el]) continue;
+    if (i < s_hdr[el] && sw_rank(s_meta[(i - 1) * ne + el]) > sw_rank(s_meta[i * ne + el])) s_hdr[3 * ne + el] = 1;
+    if (i < s_hdr[ne + el] && s_aux[(i - 1) * ne + el] > s_aux[i * ne + el]) s_hdr[3 * ne + el] = 1;
   }
-  __syncwarp(wmask);
+  __syncthreads();
+  for (uint32_t el = tid; el < nb; el += nt)
+    if (s_hdr[3 * ne + el]) {
+      a.odd_list[atomicAdd(a.odd_count, 1u)] = e0 + el;
+      s_flags[el] = kSkipState;
+    }
+
+  const uint32_t g = tid / L;
+  const bool active = g < nb && s_hdr[3 * ne + g] == 0;
+  const unsigned wmask = __ballot_sync(__activemask(), active);
+  if (active) {
+    Group<L> G;
+    G.lane = tid % L;
+    G.src = int((tid & 31u) - G.lane);
+    G.mask = wmask;
+    uint32_t flags = kSkipState;
+    run_env<L>(a, f, pl, hot, blk, ne, g, G, e0 + g, flags);
+    if (G.lane == 0) s_flags[g] = flags;
+  }
+  __syncthreads();
 
   // ---- coalesced store: state, accelerations, joint torques and states ----
-  for (uint32_t t = l; t < nb * B; t += epb) {
-    const uint32_t el = t / B, b = t - el * B, si = b * epb + el;
+  for (uint32_t t = tid; t < nb * B; t += nt) {
+    const uint32_t el = t / B, b = t - el * B, si = b * ne + el;
     const uint32_t fl = s_flags[el];
     if (fl & kSkipState) continue;
     const float4 v1 = s_vel[si];
@@ -745,45 +880,72 @@ __global__ void __launch_bounds__(32) fast_step_kernel(const __grid_constant__ S
     gvel[t] = v1;
     gang[t] = s_ang[si];
   }
-  for (uint32_t t = l; t < nb * J; t += epb) {
+  for (uint32_t t = tid; t < nb * J; t += nt) {
     const uint32_t el = t / J, j = t - el * J;
     const uint32_t fl = s_flags[el];
     if (fl & kSkipState) continue;
-    gjt[t] = s_jt[j * epb + el];
+    gjt[t] = s_jt[j * ne + el];
     if (fl & kWriteJointState) {
-      gjp[t] = s_jp[j * epb + el];
-      gjv[t] = s_jv[j * epb + el];
+      gjp[t] = s_jp[j * ne + el];
+      gjv[t] = s_jv[j * ne + el];
     }
   }
 }
 
-static size_t fast_smem(const StepArgs& args, const FModel& model, int envs_per_block) {
-  return size_t(model.hot_bytes) + size_t(fast_plan(args.B, args.J, args.M, model.H).bytes) * envs_per_block;
+static size_t fast_smem(const StepArgs& args, const FModel& model, int lanes, int envs_per_block) {
+  return size_t(model.hot_bytes) +
+         size_t(fast_plan(args.B, args.J, args.M, model.H, uint32_t(lanes)).bytes) * envs_per_block;
 }
 
-cudaError_t launch_fast_step(const StepArgs& args, const FModel& model, int envs_per_block, cudaStream_t stream) {
-  if (args.num_envs == 0) return cudaSuccess;
-  if (envs_per_block < 1 || envs_per_block > 32) return cudaErrorInvalidValue;
-  const size_t smem = fast_smem(args, model, envs_per_block);
-  cudaError_t err = cudaFuncSetAttribute(fast_step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+template <int L>
+static cudaError_t launch_l(const StepArgs& args, const FModel& model, int envs_per_block, cudaStream_t stream) {
+  const size_t smem = fast_smem(args, model, L, envs_per_block);
+  cudaError_t err = cudaFuncSetAttribute(fast_step_kernel<L>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
   if (err != cudaSuccess) return err;
   const uint32_t blocks = (args.num_envs + envs_per_block - 1) / envs_per_block;
-  fast_step_kernel<<<blocks, envs_per_block, smem, stream>>>(args, model);
+  fast_step_kernel<L><<<blocks, envs_per_block * L, smem, stream>>>(args, model);
   return cudaGetLastError();
 }
 
-int fast_max_active_blocks(const StepArgs& args, const FModel& model, int envs_per_block) {
-  const size_t smem = fast_smem(args, model, envs_per_block);
-  if (cudaFuncSetAttribute(fast_step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess) {
+bool fast_lanes_supported(int lanes) { return lanes == 1 || lanes == 2 || lanes == 4; }
+
+cudaError_t launch_fast_step(const StepArgs& args, const FModel& model, int lanes, int envs_per_block,
+                             cudaStream_t stream) {
+  if (args.num_envs == 0) return cudaSuccess;
+  if (envs_per_block < 1 || envs_per_block > 32) return cudaErrorInvalidValue;
+  switch (lanes) {
+    case 1: return launch_l<1>(args, model, envs_per_block, stream);
+    case 2: return launch_l<2>(args, model, envs_per_block, stream);
+    case 4: return launch_l<4>(args, model, envs_per_block, stream);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+template <int L>
+static int max_active_l(const StepArgs& args, const FModel& model, int envs_per_block) {
+  const size_t smem = fast_smem(args, model, L, envs_per_block);
+  if (cudaFuncSetAttribute(fast_step_kernel<L>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) !=
+      cudaSuccess) {
     cudaGetLastError();
     return 0;
   }
   int n = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, fast_step_kernel, envs_per_block, smem) != cudaSuccess) {
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, fast_step_kernel<L>, envs_per_block * L, smem) !=
+      cudaSuccess) {
     cudaGetLastError();
     return 0;
   }
   return n;
+}
+
+int fast_max_active_blocks(const StepArgs& args, const FModel& model, int lanes, int envs_per_block) {
+  if (envs_per_block < 1 || envs_per_block > 32) return 0;
+  switch (lanes) {
+    case 1: return max_active_l<1>(args, model, envs_per_block);
+    case 2: return max_active_l<2>(args, model, envs_per_block);
+    case 4: return max_active_l<4>(args, model, envs_per_block);
+    default: return 0;
+  }
 }
 
 }  // namespace zb

@@ -28,6 +28,9 @@ struct ConstraintV {
 template <int T, class M>
 __device__ __forceinline__ void cons_math(const M& m, const ConstraintV& c, float4 mia, float4 mib, float4& pa4,
                                           float4& qa, float4& pb4, float4& qb) {
+  // Each correction is computed unconditionally and kept with a select when the
+  // reference's guard holds; a discarded value is never stored, so the results equal the
+  // branching form while the dependency chain stays free of branches.
   const V3 Ia{mia.y, mia.z, mia.w}, Ib{mib.y, mib.z, mib.w};
   const float ima = mia.x, imb = mib.x;
   const V3 pa = v3(pa4), pb = v3(pb4);
@@ -36,66 +39,59 @@ __device__ __forceinline__ void cons_math(const M& m, const ConstraintV& c, floa
     const V3 ra = rotate(aa, qa), rb = rotate(ab, qb);
     const V3 diff = (pa + ra) - (pb + rb);
     const float C = len(diff);
-    if (C > 1e-6f) {
-      const V3 n = diff * rcp_(C);
-      const V3 rna = cross(ra, n), rnb = cross(rb, n);
-      const float wa = ima + dot(hadamard(rna, Ia), rna);
-      const float wb = imb + dot(hadamard(rnb, Ib), rnb);
-      const float dl = __fdiv_rn(-C, wa + wb);
-      const V3 imp = n * dl;
-      const V3 rca = ra - rotate(v3(m.com(c.a)), qa), rcb = rb - rotate(v3(m.com(c.b)), qb);
-      if (ima > 0.0f) {
-        pa4 = with_w(madd(imp, ima, pa), pa4.w);
-        qa = qnormalize(qmadd(qmul_v(hadamard(cross(rca, imp), Ia), qa), 0.5f, qa));
-      }
-      if (imb > 0.0f) {
-        pb4 = with_w(msub(imp, imb, pb), pb4.w);
-        qb = qnormalize(qmsub(qmul_v(hadamard(cross(rcb, imp), Ib), qb), 0.5f, qb));
-      }
-    }
+    const V3 n = diff * rcp_(C);
+    const V3 rna = cross(ra, n), rnb = cross(rb, n);
+    const float wa = ima + dot(hadamard(rna, Ia), rna);
+    const float wb = imb + dot(hadamard(rnb, Ib), rnb);
+    const float dl = __fdiv_rn(-C, wa + wb);
+    const V3 imp = n * dl;
+    const V3 rca = ra - rotate(v3(m.com(c.a)), qa), rcb = rb - rotate(v3(m.com(c.b)), qb);
+    const bool ok = C > 1e-6f;
+    const bool ua = ok && ima > 0.0f, ub = ok && imb > 0.0f;
+    const float4 pa_n = with_w(madd(imp, ima, pa), pa4.w);
+    const float4 qa_n = qnormalize(qmadd(qmul_v(hadamard(cross(rca, imp), Ia), qa), 0.5f, qa));
+    const float4 pb_n = with_w(msub(imp, imb, pb), pb4.w);
+    const float4 qb_n = qnormalize(qmsub(qmul_v(hadamard(cross(rcb, imp), Ib), qb), 0.5f, qb));
+    pa4 = sel4(ua, pa_n, pa4);
+    qa = sel4(ua, qa_n, qa);
+    pb4 = sel4(ub, pb_n, pb4);
+    qb = sel4(ub, qb_n, qb);
   } else if (T == 7) {  // weld: corrections on body b only
     const V3 ra = rotate(aa, qa), rb = rotate(ab, qb);
     const V3 diff = (pa + ra) - (pb + rb);
     const float C = len(diff);
-    if (C > 1e-6f) {
-      const V3 n = diff * rcp_(C);
-      const V3 rnb = cross(rb, n);
-      const float wb = imb + dot(hadamard(rnb, Ib), rnb);
-      if (wb > 1e-8f) {
-        const V3 imp = n * __fdiv_rn(-C, wb);
-        pb4 = with_w(msub(imp, imb, pb), pb4.w);
-        qb = qnormalize(qmsub(qmul_v(hadamard(cross(rb, imp), Ib), qb), 0.5f, qb));
-      }
-    }
+    const V3 n = diff * rcp_(C);
+    const V3 rnb = cross(rb, n);
+    const float wb = imb + dot(hadamard(rnb, Ib), rnb);
+    const V3 imp = n * __fdiv_rn(-C, wb);
+    const bool u1 = C > 1e-6f && wb > 1e-8f;
+    pb4 = sel4(u1, with_w(msub(imp, imb, pb), pb4.w), pb4);
+    qb = sel4(u1, qnormalize(qmsub(qmul_v(hadamard(cross(rb, imp), Ib), qb), 0.5f, qb)), qb);
     const float4 qau = qa, qbu = qb;
     float4 qerr = qmul(qmul(qconj(qau), qbu), qconj(c.at));
-    if (qerr.w < 0.0f) qerr = qneg(qerr);
+    qerr = sel4(qerr.w < 0.0f, qneg(qerr), qerr);
     const V3 ev = xyz(qerr);
     const float sh = len(ev);
-    if (sh > 1e-6f) {
-      const V3 axr = ev * rcp_(sh);
-      const float ang = 2.0f * atan2r(sh, qerr.w);
-      const V3 aw = rotate(axr, qau);
-      const float wb = dot(hadamard(aw, Ib), aw);
-      if (wb > 1e-8f) {
-        const V3 ai = aw * __fdiv_rn(ang, wb);
-        if (imb > 0.0f) qb = qnormalize(qmsub(qmul_v(hadamard(ai, Ib), qbu), 0.5f, qbu));
-      }
-    }
+    const V3 axr = ev * rcp_(sh);
+    const float ang = 2.0f * atan2r(sh, qerr.w);
+    const V3 aw = rotate(axr, qau);
+    const float w2 = dot(hadamard(aw, Ib), aw);
+    const V3 ai = aw * __fdiv_rn(ang, w2);
+    const bool u2 = sh > 1e-6f && w2 > 1e-8f && imb > 0.0f;
+    qb = sel4(u2, qnormalize(qmsub(qmul_v(hadamard(ai, Ib), qbu), 0.5f, qbu)), qb);
   } else if (T == 3) {  // angular: keep hinge axes parallel
     const V3 aaw = rotate(aa, qa), abw = rotate(ab, qb);
     const V3 cr = cross(aaw, abw);
     const float sa = len(cr);
-    if (sa > 1e-6f) {
-      const V3 n = cr * rcp_(sa);
-      const float angC = asinr(clampf(sa, -1.0f, 1.0f));
-      const float w = dot(hadamard(n, Ia), n) + dot(hadamard(n, Ib), n);
-      if (w > 1e-8f) {
-        const float dl = __fdiv_rn(-angC, w);
-        if (ima > 0.0f) qa = qnormalize(qmadd(qmul_v(hadamard(n * dl, Ia), qa), 0.5f, qa));
-        if (imb > 0.0f) qb = qnormalize(qmadd(qmul_v(hadamard(n * (-dl), Ib), qb), 0.5f, qb));
-      }
-    }
+    const V3 n = cr * rcp_(sa);
+    const float angC = asinr(clampf(sa, -1.0f, 1.0f));
+    const float w = dot(hadamard(n, Ia), n) + dot(hadamard(n, Ib), n);
+    const float dl = __fdiv_rn(-angC, w);
+    const bool ok = sa > 1e-6f && w > 1e-8f;
+    const float4 qa_n = qnormalize(qmadd(qmul_v(hadamard(n * dl, Ia), qa), 0.5f, qa));
+    const float4 qb_n = qnormalize(qmadd(qmul_v(hadamard(n * (-dl), Ib), qb), 0.5f, qb));
+    qa = sel4(ok && ima > 0.0f, qa_n, qa);
+    qb = sel4(ok && imb > 0.0f, qb_n, qb);
   } else if (T == 4) {  // angular limit
     const float lo = c.lim.x, hi = c.lim.y;
     const float4 qrel = qmul(qconj(qa), qb);
@@ -103,15 +99,15 @@ __device__ __forceinline__ void cons_math(const M& m, const ConstraintV& c, floa
     float viol = 0.0f;
     if (angle < lo) viol = lo - angle;
     else if (angle > hi) viol = hi - angle;
-    if (fabsf(viol) > 1e-6f) {
+    if (fabsf(viol) > 1e-6f) {  // rarely taken: keep the branch, skip the work
       const V3 aw = rotate(aa, qa);
       const float w = dot(hadamard(aw, Ia), aw) + dot(hadamard(aw, Ib), aw);
-      if (w > 1e-8f) {
-        const V3 ai = aw * __fdiv_rn(viol, w);
-        const float4 qa0 = qa, qb0 = qb;
-        if (ima > 0.0f) qa = qnormalize(qmadd(qmul_v(hadamard(ai, Ia), qa0), 0.5f, qa0));
-        if (imb > 0.0f) qb = qnormalize(qmsub(qmul_v(hadamard(ai, Ib), qb0), 0.5f, qb0));
-      }
+      const V3 ai = aw * __fdiv_rn(viol, w);
+      const bool ok = w > 1e-8f;
+      const float4 qa_n = qnormalize(qmadd(qmul_v(hadamard(ai, Ia), qa), 0.5f, qa));
+      const float4 qb_n = qnormalize(qmsub(qmul_v(hadamard(ai, Ib), qb), 0.5f, qb));
+      qa = sel4(ok && ima > 0.0f, qa_n, qa);
+      qb = sel4(ok && imb > 0.0f, qb_n, qb);
     }
   } else if (T == 5) {  // linear limit
     const float lo = c.lim.x, hi = c.lim.y;
@@ -127,11 +123,10 @@ __device__ __forceinline__ void cons_math(const M& m, const ConstraintV& c, floa
       const float wa = ima + dot(hadamard(rna, Ia), rna);
       const float wb = imb + dot(hadamard(rnb, Ib), rnb);
       const float w = wa + wb;
-      if (w > 1e-8f) {
-        const V3 imp = n * __fdiv_rn(fabsf(viol), w);
-        if (ima > 0.0f) pa4 = with_w(msub(imp, ima, pa), pa4.w);
-        if (imb > 0.0f) pb4 = with_w(madd(imp, imb, pb), pb4.w);
-      }
+      const V3 imp = n * __fdiv_rn(fabsf(viol), w);
+      const bool ok = w > 1e-8f;
+      pa4 = sel4(ok && ima > 0.0f, with_w(msub(imp, ima, pa), pa4.w), pa4);
+      pb4 = sel4(ok && imb > 0.0f, with_w(madd(imp, imb, pb), pb4.w), pb4);
     }
   } else if (T == 10) {  // slider: perpendicular lock + relative-orientation weld
     const V3 ra = rotate(aa, qa), rb = rotate(ab, qb);
@@ -139,38 +134,31 @@ __device__ __forceinline__ void cons_math(const M& m, const ConstraintV& c, floa
     const V3 aw = rotate(v3(c.at), qa);
     const V3 perp = msub(aw, dot(diff, aw), diff);
     const float pl = len(perp);
-    if (pl > 1e-6f) {
-      const V3 n = perp * rcp_(pl);
-      const V3 rna = cross(ra, n), rnb = cross(rb, n);
-      const float wa = ima + dot(hadamard(rna, Ia), rna);
-      const float wb = imb + dot(hadamard(rnb, Ib), rnb);
-      const V3 imp = n * __fdiv_rn(-pl, wa + wb);
-      const float4 qa0 = qa, qb0 = qb;
-      if (ima > 0.0f) {
-        pa4 = with_w(madd(imp, ima, pa), pa4.w);
-        qa = qnormalize(qmadd(qmul_v(hadamard(cross(ra, imp), Ia), qa0), 0.5f, qa0));
-      }
-      if (imb > 0.0f) {
-        pb4 = with_w(msub(imp, imb, pb), pb4.w);
-        qb = qnormalize(qmsub(qmul_v(hadamard(cross(rb, imp), Ib), qb0), 0.5f, qb0));
-      }
-    }
+    const V3 n = perp * rcp_(pl);
+    const V3 rna = cross(ra, n), rnb = cross(rb, n);
+    const float wa = ima + dot(hadamard(rna, Ia), rna);
+    const float wb = imb + dot(hadamard(rnb, Ib), rnb);
+    const V3 imp = n * __fdiv_rn(-pl, wa + wb);
+    const bool ok = pl > 1e-6f;
+    const float4 qa0 = qa, qb0 = qb;
+    const bool ua = ok && ima > 0.0f, ub = ok && imb > 0.0f;
+    pa4 = sel4(ua, with_w(madd(imp, ima, pa), pa4.w), pa4);
+    qa = sel4(ua, qnormalize(qmadd(qmul_v(hadamard(cross(ra, imp), Ia), qa0), 0.5f, qa0)), qa);
+    pb4 = sel4(ub, with_w(msub(imp, imb, pb), pb4.w), pb4);
+    qb = sel4(ub, qnormalize(qmsub(qmul_v(hadamard(cross(rb, imp), Ib), qb0), 0.5f, qb0)), qb);
     const float4 qau = qa, qbu = qb;
     float4 qerr = qmul(qmul(qconj(qau), qbu), qconj(c.lim));
-    if (qerr.w < 0.0f) qerr = qneg(qerr);
+    qerr = sel4(qerr.w < 0.0f, qneg(qerr), qerr);
     const V3 ev = xyz(qerr);
     const float sh = len(ev);
-    if (sh > 1e-6f) {
-      const V3 axe = ev * rcp_(sh);
-      const float ae = 2.0f * atan2r(sh, qerr.w);
-      const V3 aw2 = rotate(axe, qau);
-      const float w = dot(hadamard(aw2, Ia), aw2) + dot(hadamard(aw2, Ib), aw2);
-      if (w > 1e-8f) {
-        const V3 ai = aw2 * __fdiv_rn(ae, w);
-        if (ima > 0.0f) qa = qnormalize(qmadd(qmul_v(hadamard(ai, Ia), qau), 0.5f, qau));
-        if (imb > 0.0f) qb = qnormalize(qmsub(qmul_v(hadamard(ai, Ib), qbu), 0.5f, qbu));
-      }
-    }
+    const V3 axe = ev * rcp_(sh);
+    const float ae = 2.0f * atan2r(sh, qerr.w);
+    const V3 aw2 = rotate(axe, qau);
+    const float w = dot(hadamard(aw2, Ia), aw2) + dot(hadamard(aw2, Ib), aw2);
+    const V3 ai = aw2 * __fdiv_rn(ae, w);
+    const bool ok2 = sh > 1e-6f && w > 1e-8f;
+    qa = sel4(ok2 && ima > 0.0f, qnormalize(qmadd(qmul_v(hadamard(ai, Ia), qau), 0.5f, qau)), qa);
+    qb = sel4(ok2 && imb > 0.0f, qnormalize(qmsub(qmul_v(hadamard(ai, Ib), qbu), 0.5f, qbu)), qb);
   }
 }
 

@@ -18,16 +18,19 @@ uint32_t env_smem_bytes(uint32_t B, uint32_t J, uint32_t M);
 // lanes: threads per environment (4, 8, 16 or 32); envs_per_block * lanes threads per block.
 cudaError_t launch_step(const StepArgs& args, int lanes, int envs_per_block, cudaStream_t stream);
 
-// Shared memory one environment needs in the environment-per-lane kernel.
-uint32_t fast_env_smem_bytes(uint32_t B, uint32_t J, uint32_t M, uint32_t H);
+// Shared memory one environment needs in the compressed-state kernel with L lanes per env.
+uint32_t fast_env_smem_bytes(uint32_t B, uint32_t J, uint32_t M, uint32_t H, uint32_t L);
 
-// Environment-per-lane kernel: envs_per_block (1..32) lanes per block, one environment
-// each.  Environments it cannot represent are appended to args.odd_list / odd_count
-// untouched, for a following list-mode launch_step.
-cudaError_t launch_fast_step(const StepArgs& args, const FModel& model, int envs_per_block, cudaStream_t stream);
+// Compressed-state kernel: `lanes` (1, 2 or 4) lanes per environment, envs_per_block
+// (1..32) environments per block.  Environments it cannot
+// represent are appended to args.odd_list / odd_count untouched, for a following
+// list-mode launch_step.
+bool fast_lanes_supported(int lanes);
+cudaError_t launch_fast_step(const StepArgs& args, const FModel& model, int lanes, int envs_per_block,
+                             cudaStream_t stream);
 
-// Resident blocks per SM for a given envs_per_block (0 when it does not fit).
-int fast_max_active_blocks(const StepArgs& args, const FModel& model, int envs_per_block);
+// Resident blocks per SM for a given shape (0 when it does not fit).
+int fast_max_active_blocks(const StepArgs& args, const FModel& model, int lanes, int envs_per_block);
 
 // Masked restore of the initial template (mask == nullptr: every env).
 cudaError_t launch_reset(float* pos, float* quat, float* vel, float* ang, float* jpos, float* jvel, const float* init,

@@ -139,16 +139,17 @@ World* World::create(const Scene& sc, const WorldConfig& cfg, std::string* err) 
   return w;
 }
 
-// envs_per_block for the environment-per-lane kernel: the widest block (fullest warps)
-// that still lets every environment be resident at once; when none does, the shape
-// with the most resident environments per SM.
+// Shape of the compressed-state kernel: kDefaultLanes lanes per environment and the
+// largest envs_per_block (fullest blocks) that still lets every environment be resident
+// at once; when none does, the shape with the most resident environments per SM.
 void World::choose_fast_shape() {
+  constexpr int kDefaultLanes = 2;
   int sms = 148;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device_);
   const StepArgs a = args(cfg_.substeps, nullptr, nullptr);
   int best = 0, best_res = 0;
   for (int epb = 32; epb >= 1; --epb) {
-    const int bps = fast_max_active_blocks(a, fmodel_, epb);
+    const int bps = fast_max_active_blocks(a, fmodel_, kDefaultLanes, epb);
     if (bps <= 0) continue;
     const uint64_t resident = uint64_t(bps) * epb;
     if (resident * uint64_t(sms) >= cfg_.num_envs) {
@@ -161,6 +162,7 @@ void World::choose_fast_shape() {
     fast_ok_ = false;
     return;
   }
+  fast_lanes_ = kDefaultLanes;
   fast_epb_ = best;
   use_fast_ = true;
 }
@@ -204,7 +206,7 @@ StepArgs World::args(uint32_t substeps, const float* actions, const uint8_t* mas
 cudaError_t World::launch(uint32_t substeps, const float* actions, const uint8_t* mask) {
   StepArgs a = args(substeps, actions, mask);
   if (!use_fast_) return launch_step(a, lanes_, envs_per_block_, stream_);
-  cudaError_t e = launch_fast_step(a, fmodel_, fast_epb_, stream_);
+  cudaError_t e = launch_fast_step(a, fmodel_, fast_lanes_, fast_epb_, stream_);
   if (e != cudaSuccess) return e;
   // environments the fast kernel handed over (normally none): general kernel, list mode
   a.env_list = d_odd_ + 2;
@@ -378,14 +380,16 @@ int World::set_task(const DTask& t) {
 }
 
 int World::set_launch(int lanes, int envs_per_block) {
-  if (lanes == 1) {
+  if (fast_lanes_supported(lanes)) {
     if (!fast_ok_ || envs_per_block < 1 || envs_per_block > 32) return -6;
-    if (fast_max_active_blocks(args(cfg_.substeps, nullptr, nullptr), fmodel_, envs_per_block) <= 0) return -6;
+    if (fast_max_active_blocks(args(cfg_.substeps, nullptr, nullptr), fmodel_, lanes, envs_per_block) <= 0)
+      return -6;
+    fast_lanes_ = lanes;
     fast_epb_ = envs_per_block;
     use_fast_ = true;
     return 0;
   }
-  if (lanes != 4 && lanes != 8 && lanes != 16 && lanes != 32) return -6;
+  if (lanes != 8 && lanes != 16 && lanes != 32) return -6;
   const uint32_t env_bytes = env_smem_bytes(model_.B, model_.J, cfg_.max_contacts_per_env);
   if (envs_per_block < 1 || lanes * envs_per_block > 256 ||
       uint64_t(env_bytes) * envs_per_block > uint64_t(opt_in_smem(device_)))

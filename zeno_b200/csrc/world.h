@@ -51,8 +51,9 @@ class World {
   void set_gravity(float gx, float gy, float gz);
   int set_timestep(float ts);
   int set_task(const DTask& t);
-  // lanes 1: environment-per-lane kernel with envs_per_block (1..32) lanes per block;
-  // lanes 4/8/16/32: general kernel only.  -6 when the shape is invalid or unsupported.
+  // lanes 1, 2, 4: compressed-state kernel with that many lanes per environment and
+  // envs_per_block (1..32) environments per block; lanes 8, 16, 32: general kernel only.
+  // -6 when the shape is invalid or unsupported.
   int set_launch(int lanes, int envs_per_block);
   cudaError_t synchronize();
   void set_stream(cudaStream_t s) { stream_ = s ? s : own_stream_; }
@@ -65,7 +66,7 @@ class World {
   int device() const { return device_; }
   Profiling profiling() const { return prof_; }
   void reset_profiling() { prof_ = Profiling{}; }
-  int lanes() const { return use_fast_ ? 1 : lanes_; }
+  int lanes() const { return use_fast_ ? fast_lanes_ : lanes_; }
   int envs_per_block() const { return use_fast_ ? fast_epb_ : envs_per_block_; }
   bool fast_available() const { return fast_ok_; }
 
@@ -104,6 +105,7 @@ class World {
   int envs_per_block_ = 4;
   bool fast_ok_ = false;     // the model packs into FModel
   bool use_fast_ = false;
+  int fast_lanes_ = 2;
   int fast_epb_ = 32;
   FModel fmodel_{};
   std::vector<uint8_t> hot_image_;
