@@ -41,6 +41,8 @@ sys.path.insert(0, str(ROOT))
 ENVS_PER_GPU = 16384
 ACTION_RING = 64   # distinct pre-generated action batches, resident in HBM, cycled over the steps
 E2E_STEPS = 200    # steps of the end-to-end leg
+CPU_SAMPLE_ENVS = 2048  # cpu_baseline: envs stepped by the CPU oracle ...
+CPU_SAMPLE_S = 10.0     # ... for about this many seconds
 SUBSTEPS = 4
 ITERATIONS = 4
 MAX_CONTACTS = 64
@@ -147,19 +149,27 @@ def measured_peaks():
     return 6650.0, "fallback"
 
 
-def cpu_baseline(xml, steps, sample_envs, threads):
-    """The CPU oracle (reference algorithm restated) on a bounded sample of envs."""
+def cpu_baseline(xml, steps, sample_envs, threads, target_s=None):
+    """The CPU oracle (reference algorithm restated) on a bounded sample of envs: `steps`
+    steps, or (target_s set) as many 10-step batches as fill about target_s seconds.
+    Returns (env-steps/s, seconds, steps run)."""
     from oracle.zeno_oracle import OracleWorld
     o = OracleWorld(xml, num_envs=sample_envs, substeps=SUBSTEPS, contact_iterations=ITERATIONS,
                     max_contacts_per_env=MAX_CONTACTS)
     o.set_task(body=1, z_min=0.2, z_max=1.0, auto_reset=True, noise=0.1, seed=1)
     rng = np.random.default_rng(0)
-    acts = rng.uniform(-1, 1, size=(steps, sample_envs, 8)).astype(np.float32)
+    batch = 10 if target_s else steps
+    acts = rng.uniform(-1, 1, size=(batch, sample_envs, 8)).astype(np.float32)
     o.run(acts[:1], threads=threads)  # warm-up
+    done = 0
     t0 = time.perf_counter()
-    o.run(acts, threads=threads)
-    dt = time.perf_counter() - t0
-    return steps * sample_envs / dt, dt
+    while True:
+        o.run(acts, threads=threads)
+        done += batch
+        dt = time.perf_counter() - t0
+        if not target_s or dt >= target_s:
+            break
+    return done * sample_envs / dt, dt, done
 
 
 def run_reference(args, rank):
@@ -169,7 +179,7 @@ def run_reference(args, rank):
     threads = os.cpu_count() or 1
     sample = 2048
     xml = scenes.ant()
-    val, dt = cpu_baseline(xml, args.warmup + args.steps, sample, threads)
+    val, dt, _ = cpu_baseline(xml, args.warmup + args.steps, sample, threads)
     line = {
         "impl": "reference", "metric": METRIC, "value": val, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": 1000.0 * sample / val, "higher_is_better": True, "scaling": "weak",
@@ -292,9 +302,10 @@ def run_ours(args, rank, world_size, local_rank):
         achieved = bpe * E / (mean_ms / 1000.0) / 1e9
         peak, peak_kind = measured_peaks()
         lanes, epb = w.get_launch()
-        kernel = "zb::fast_step_kernel" if lanes == 1 else f"zb::step_kernel<{lanes}>"
+        kernel = f"zb::fast_step_kernel<{lanes}>" if lanes in (1, 2, 4) else f"zb::step_kernel<{lanes}>"
         traffic = dram_bytes_per_launch(kernel, E)
-        cpu_val, cpu_dt = cpu_baseline(xml, 10, 1024, os.cpu_count() or 1) if not args.no_cpu else (None, 0)
+        cpu_val, cpu_dt, cpu_steps = (cpu_baseline(xml, 0, CPU_SAMPLE_ENVS, os.cpu_count() or 1, CPU_SAMPLE_S)
+                                      if not args.no_cpu else (None, 0, 0))
         clocks = clk.summary()
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world_size, "steps": args.steps,
@@ -311,11 +322,12 @@ def run_ours(args, rank, world_size, local_rank):
                          "bytes_per_env_step": bpe, "kernel": kernel,
                          "mean_launch_ms": mean_ms},
             "cpu_baseline": {"value": cpu_val, "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
-                             "sample": f"1024 Ant envs x 10 steps, oracle on {os.cpu_count()} threads ({cpu_dt:.1f} s)"},
+                             "sample": f"{CPU_SAMPLE_ENVS} Ant envs x {cpu_steps} steps, oracle on "
+                                       f"{os.cpu_count()} threads ({cpu_dt:.1f} s)"},
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": int(d2h)},
             # per step: the step kernel, plus (environment-per-lane kernel) the hand-over
             # launch of the general kernel, which exits at once when nothing was handed over
-            "gpu_launches": args.steps * (2 if lanes == 1 else 1),
+            "gpu_launches": args.steps * (2 if lanes in (1, 2, 4) else 1),
             "clocks": clocks,
             "wall_s_timed_region": wall,
             "dones_in_last_step": dones_seen,

@@ -163,12 +163,23 @@ bool pack_fast_model(const HostModel& h, uint32_t max_contacts, FModel* out, std
   m.o_ggpair = section(G * G);
   for (uint32_t ga = 0; ga < G; ++ga) put(m.o_ggpair + ga * G, &m.gg_pair[ga * fm::kG], G);
   m.o_gforce = section(16 * B);
-  m.num_colors = h.num_colors;
-  m.o_color = section(4 * h.num_colors);
+  // The colour sweep as runs of one constraint type: each colour split into maximal runs
+  // of equal type, in order.  A run's constraints belong to one colour (disjoint bodies),
+  // and the type dispatch happens once per run instead of once per constraint.
+  std::vector<uint32_t> runs;
   for (uint32_t col = 0; col < h.num_colors; ++col) {
-    const uint32_t v = h.color_ranges[2 * col] | (h.color_ranges[2 * col + 1] << 16);
-    put(m.o_color + 4 * col, &v, 4);
+    const uint32_t start = h.color_ranges[2 * col], cnt = h.color_ranges[2 * col + 1];
+    for (uint32_t k = start; k < start + cnt;) {
+      const uint32_t t = h.constraints[k].type & 0xFFu;
+      uint32_t n = 1;
+      while (k + n < start + cnt && (h.constraints[k + n].type & 0xFFu) == t) ++n;
+      if (k > 0xFFFu || n > 0xFFFu) return fail("constraint run out of range");
+      runs.push_back(k | (n << 12) | (t << 24));
+      k += n;
+    }
   }
+  m.num_runs = uint32_t(runs.size());
+  m.o_runs = section(4 * m.num_runs), put(m.o_runs, runs.data(), 4 * runs.size());
   section(0);
   m.hot_bytes = uint32_t(img.size());
   m.hot = nullptr;

@@ -67,8 +67,8 @@ struct FModel {
   uint32_t o_pbody, o_pinfo, o_pmd2, o_gps, o_hinfo, o_hga, o_hgb, o_hcq, o_hhl, o_hfr, o_hpair;
   uint32_t o_gbody, o_ggpair;  // geom -> body (u32[G]), (ga, gb) -> candidate (u8[G * G])
   uint32_t o_gforce;           // float4[B], filled by each block: gravity * mass (zero when massless)
-  uint32_t o_color;            // u32[num_colors]: first constraint | count << 16
-  uint32_t num_colors;
+  uint32_t o_runs;             // u32[num_runs]: first constraint | count << 12 | type << 24
+  uint32_t num_runs;
 };
 
 // Fills *out and the hot image *hot (to be uploaded and linked through out->hot); false

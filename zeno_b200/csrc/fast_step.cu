@@ -228,6 +228,7 @@ __device__ __forceinline__ void run_env(const StepArgs& a, const FModel& f, cons
 
   uint64_t prev_hit = 0;
   uint32_t n_prev = n_prev0;
+  uint32_t nh = 0, nlev = 0, nlev_w = 0;  // contact schedule: hit slots, levels (L > 1), warp max
   bool moved = false;  // (lane 0) did sorting move a slot away from its original position
   for (uint32_t s = 0; s < a.substeps; ++s) {
     // ---- kinematic bodies (update_kinematic 304-339; massless, so no gravity wrench) ----
@@ -413,23 +414,24 @@ __device__ __forceinline__ void run_env(const StepArgs& a, const FModel& f, cons
     }
     hit_now = G.or_all(hit_now);
     G.sync();
-    // slot impulses (narrow zeroes them, a match warm-starts them)
-    for (uint32_t i = lane; i < n; i += L) {
-      const uint32_t hh = sw_hit(meta[i * ne]);
-      if (hh != fm::kNoHit && ((hit_now >> hh) & 1ull)) imp[i * ne] = nt[hh * ne].w;
-    }
     // contact schedule.  L = 1: the hit slots in slot order.  L > 1: the hit slots by
     // level -- a slot's level is one more than the highest level of an earlier hit slot
     // sharing a dynamic body -- stable within a level; solving level by level, a level's
-    // slots in parallel, equals solving the slots one after another in slot order.
-    uint32_t nh = 0, nlev = 0, nlev_w = 0;
+    // slots in parallel, equals solving the slots one after another in slot order.  The
+    // schedule depends only on the slot list and the set of hit pairs, so it is kept from
+    // the previous substep when neither changed (aux holds it from substep 1 on).
+    const bool reuse = s > 0 && n == n_prev && hit_now == prev_hit;
     if constexpr (L == 1) {
-      for (uint32_t i = 0; i < n; ++i) {
-        const uint32_t hh = sw_hit(meta[i * ne]);
-        if (hh != fm::kNoHit && ((hit_now >> hh) & 1ull)) aux[nh++ * ne] = uint8_t(i);
+      if (!reuse) {
+        nh = 0;
+        for (uint32_t i = 0; i < n; ++i) {
+          const uint32_t hh = sw_hit(meta[i * ne]);
+          if (hh != fm::kNoHit && ((hit_now >> hh) & 1ull)) aux[nh++ * ne] = uint8_t(i);
+        }
       }
     } else {
-      if (lane == 0) {
+      if (lane == 0 && !reuse) {
+        nlev = 0;
         for (int pass = 0; pass < 2; ++pass) {  // pass 0 counts per level, pass 1 places
           for (uint32_t b = 0; b < B; ++b) blev[b * ne] = 0;
           if (pass == 1) {
@@ -469,20 +471,31 @@ __device__ __forceinline__ void run_env(const StepArgs& a, const FModel& f, cons
       nlev = G.bcast(nlev);
       nlev_w = G.warp_max(nlev);  // every group of the warp runs as many levels (and syncs)
       G.sync();
+      nh = lofs[nlev * ne];
     }
-    // ---- XPBD joints (solve_joints 909-1399) ----
-    if constexpr (L == 1) {  // one after another in colour-sorted order (= colour by colour)
-      for (uint32_t it = 0; it < a.iterations; ++it)
-        for (uint32_t k = 0; k < a.K; ++k) solve_constraint(m, m.constraint(k), S);
-    } else {  // colour by colour, a colour's constraints (disjoint bodies) across the lanes
-      for (uint32_t it = 0; it < a.iterations; ++it)
-        for (uint32_t col = 0; col < f.num_colors; ++col) {
-          const uint32_t cr = m.color(col);
-          const uint32_t k0 = cr & 0xFFFFu, k1 = k0 + (cr >> 16);
-          for (uint32_t k = k0 + lane; k < k1; k += L) solve_constraint(m, m.constraint(k), S);
-          G.sync();
+    // slot impulses of the hit slots (narrow zeroes them, a match warm-starts them)
+    for (uint32_t v = lane; v < nh; v += L) {
+      const uint32_t i = aux[v * ne];
+      imp[i * ne] = nt[sw_hit(meta[i * ne]) * ne].w;
+    }
+    // ---- XPBD joints (solve_joints 909-1399): colour by colour, as runs of one type; a
+    //      run's constraints (one colour: disjoint bodies) split across the lanes.  With
+    //      one lane this is the colour-sorted order, which equals colour by colour.
+    for (uint32_t it = 0; it < a.iterations; ++it)
+      for (uint32_t r = 0; r < f.num_runs; ++r) {
+        const uint32_t rw = m.run(r);
+        const uint32_t k0 = (rw & 0xFFFu) + lane, k1 = (rw & 0xFFFu) + ((rw >> 12) & 0xFFFu);
+        switch (rw >> 24) {
+          case 2: for (uint32_t k = k0; k < k1; k += L) solve_typed<2>(m, m.constraint(k), S); break;
+          case 3: for (uint32_t k = k0; k < k1; k += L) solve_typed<3>(m, m.constraint(k), S); break;
+          case 4: for (uint32_t k = k0; k < k1; k += L) solve_typed<4>(m, m.constraint(k), S); break;
+          case 5: for (uint32_t k = k0; k < k1; k += L) solve_typed<5>(m, m.constraint(k), S); break;
+          case 7: for (uint32_t k = k0; k < k1; k += L) solve_typed<7>(m, m.constraint(k), S); break;
+          case 10: for (uint32_t k = k0; k < k1; k += L) solve_typed<10>(m, m.constraint(k), S); break;
+          default: break;
         }
-    }
+        G.sync();
+      }
     // ---- contacts (solve_contacts 1644-1793) ----
     auto contact = [&](uint32_t i) {
       const uint32_t hh = sw_hit(meta[i * ne]);
@@ -798,7 +811,7 @@ __global__ void __launch_bounds__(32 * L) fast_step_kernel(const __grid_constant
   __syncthreads();
   const ModelS m{hot, f};
   const Contact* gcb = a.contacts + size_t(e0) * M;
-  constexpr uint32_t kU = 4;  // slots per thread per round: their loads are in flight together
+  constexpr uint32_t kU = 8;  // slots per thread per round: their loads are in flight together
   // An environment is handed over (s_hdr[3] set) when a slot tuple of either list is not
   // a broad-phase candidate, when a list is not sorted by key, or when a valid previous
   // slot carries non-zero tangent impulses (a warm start would copy them; this kernel
