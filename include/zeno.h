@@ -200,8 +200,19 @@ typedef struct {
 } ZenoTaskConfig;
 int zeno_world_set_task(ZenoWorldHandle world, const ZenoTaskConfig* task);
 
-/* Launch shape of the step kernel: lanes per environment (4, 8, 16, 32) and
- * environments per thread block (lanes * envs <= 256, shared memory permitting). */
+/* Narrow phase (no counterpart export in the reference).  0 (default): the reference's
+ * GPU narrow phase (src/shaders/all_shaders.metal:751-894: sphere-sphere, sphere-plane,
+ * capsule-plane, geoms placed by unrotated offsets).  1: the reference's CPU collision
+ * routines (src/collision/narrow_phase.zig:28-512, detectCollision): also sphere-capsule,
+ * sphere-box, capsule-capsule, box-plane and box-box (SAT), geoms placed by their body's
+ * pose.  Returns 0, or -6 for another mode. */
+int zeno_world_set_narrow_phase(ZenoWorldHandle world, uint32_t mode);
+uint32_t zeno_world_get_narrow_phase(ZenoWorldHandle world);
+
+/* Launch shape of the step.  lanes 1, 2 or 4: the compressed-state kernel with that many
+ * lanes per environment and envs_per_block (1..32) environments per block; lanes 8, 16
+ * or 32: the general kernel (lanes * envs_per_block <= 256, shared memory permitting).
+ * Returns -6 when the shape does not fit the model. */
 int zeno_world_set_launch(ZenoWorldHandle world, int lanes, int envs_per_block);
 int zeno_world_get_launch(ZenoWorldHandle world, int* lanes, int* envs_per_block);
 

@@ -1,0 +1,321 @@
+// TEST INFRASTRUCTURE ONLY -- restatement of the reference's CPU collision routines
+// (src/collision/narrow_phase.zig, detectCollision and the primitive pairs it dispatches
+// to), used by the oracle when a world selects the extended narrow phase.
+//
+// Semantics kept from the reference code:
+//  * a geom is placed by its body transform: centre = R(q_body) * local_pos + body_pos
+//    (getWorldCenter, primitives.zig:413-415); capsule axes, box axes and plane normals
+//    come from the body quaternion only (the geom's own local quaternion is not applied);
+//  * boxes are centred on the body origin in sphereBox / boxPlane (they use the body
+//    transform, not the geom centre), but on the geom centre in boxBox;
+//  * box-capsule pairs, plane-plane pairs and every pair with a cylinder, mesh or
+//    heightfield report no contact (no primitive routine, or outside this build's scope).
+// Arithmetic follows the Zig source literally: plain IEEE-754 single-precision +, -, *,
+// / and sqrt, evaluated left to right as written (Zig's default float mode contracts
+// nothing); the oracle is compiled with -ffp-contract=off for the same reason.
+#include <cmath>
+#include <limits>
+
+#include "oracle_model.h"
+
+namespace zo {
+namespace {
+
+constexpr float kEps = 1e-6f;  // constants.EPSILON (src/physics/constants.zig:13)
+
+struct P3 {
+  float x, y, z;
+};
+inline P3 p3(const float* v) { return P3{v[0], v[1], v[2]}; }
+inline P3 add(P3 a, P3 b) { return P3{a.x + b.x, a.y + b.y, a.z + b.z}; }
+inline P3 sub(P3 a, P3 b) { return P3{a.x - b.x, a.y - b.y, a.z - b.z}; }
+inline P3 scl(P3 v, float s) { return P3{v.x * s, v.y * s, v.z * s}; }
+inline float dot(P3 a, P3 b) { return a.x * b.x + a.y * b.y + a.z * b.z; }
+inline P3 cross(P3 a, P3 b) { return P3{a.y * b.z - a.z * b.y, a.z * b.x - a.x * b.z, a.x * b.y - a.y * b.x}; }
+inline float clampf(float v, float lo, float hi) { return std::fmax(lo, std::fmin(v, hi)); }
+
+struct Quat {
+  float x, y, z, w;
+};
+// rotateByQuat (src/physics/body.zig:254-264): v + 2 (w (q x v) + q x (q x v))
+inline P3 rot(P3 v, Quat q) {
+  const P3 qv{q.x, q.y, q.z};
+  const P3 uv = cross(qv, v);
+  const P3 uuv = cross(qv, uv);
+  return P3{v.x + 2.0f * (q.w * uv.x + uuv.x), v.y + 2.0f * (q.w * uv.y + uuv.y), v.z + 2.0f * (q.w * uv.z + uuv.z)};
+}
+struct Xf {  // body.Transform
+  P3 p;
+  Quat q;
+  P3 point(P3 v) const { return add(rot(v, q), p); }  // transformPoint
+  P3 vec(P3 v) const { return rot(v, q); }            // transformVector
+  Xf inverse() const {                                 // inverse()
+    const Quat iq{-q.x, -q.y, -q.z, q.w};
+    return Xf{rot(P3{-p.x, -p.y, -p.z}, iq), iq};
+  }
+};
+
+struct Res {
+  P3 point, normal;
+  float pen;
+};
+
+// -------------------------------------------------------------- helpers (narrow_phase.zig)
+P3 closest_on_segment(P3 point, P3 s, P3 e) {
+  const P3 seg = sub(e, s);
+  const float len_sq = dot(seg, seg);
+  if (len_sq < kEps) return s;
+  const float t = clampf(dot(sub(point, s), seg) / len_sq, 0.0f, 1.0f);
+  return add(s, scl(seg, t));
+}
+
+void closest_between_segments(P3 a1, P3 a2, P3 b1, P3 b2, P3* pa, P3* pb) {
+  const P3 d1 = sub(a2, a1), d2 = sub(b2, b1), r = sub(a1, b1);
+  const float a = dot(d1, d1), e = dot(d2, d2), f = dot(d2, r);
+  float s = 0.0f, t = 0.0f;
+  if (a < kEps && e < kEps) {
+    *pa = a1, *pb = b1;
+    return;
+  }
+  if (a < kEps) {
+    t = clampf(f / e, 0.0f, 1.0f);
+  } else {
+    const float c = dot(d1, r);
+    if (e < kEps) {
+      s = clampf(-c / a, 0.0f, 1.0f);
+    } else {
+      const float b = dot(d1, d2);
+      const float denom = a * e - b * b;
+      if (denom != 0.0f) s = clampf((b * f - c * e) / denom, 0.0f, 1.0f);
+      t = (b * s + f) / e;
+      if (t < 0.0f) {
+        t = 0.0f;
+        s = clampf(-c / a, 0.0f, 1.0f);
+      } else if (t > 1.0f) {
+        t = 1.0f;
+        s = clampf((b - c) / a, 0.0f, 1.0f);
+      }
+    }
+  }
+  *pa = add(a1, scl(d1, s));
+  *pb = add(b1, scl(d2, t));
+}
+
+P3 box_face_normal(P3 p, P3 h) {  // the face with the largest distance, as written
+  const float pc[3] = {p.x, p.y, p.z}, hc[3] = {h.x, h.y, h.z};
+  float max_dist = -std::numeric_limits<float>::infinity();
+  float n[3] = {0.0f, 0.0f, 1.0f};
+  for (int i = 0; i < 3; ++i) {
+    const float d_pos = hc[i] - pc[i], d_neg = hc[i] + pc[i];
+    if (d_pos > max_dist) {
+      max_dist = d_pos;
+      n[0] = n[1] = n[2] = 0.0f;
+      n[i] = 1.0f;
+    }
+    if (d_neg > max_dist) {
+      max_dist = d_neg;
+      n[0] = n[1] = n[2] = 0.0f;
+      n[i] = -1.0f;
+    }
+  }
+  return P3{n[0], n[1], n[2]};
+}
+
+// testAxis: overlap on `axis`, or false when it separates
+bool test_axis(P3 axis, P3 d, const P3* axa, P3 ha, const P3* axb, P3 hb, float* overlap) {
+  const float proj_a = ha.x * std::fabs(dot(axis, axa[0])) + ha.y * std::fabs(dot(axis, axa[1])) +
+                       ha.z * std::fabs(dot(axis, axa[2]));
+  const float proj_b = hb.x * std::fabs(dot(axis, axb[0])) + hb.y * std::fabs(dot(axis, axb[1])) +
+                       hb.z * std::fabs(dot(axis, axb[2]));
+  const float dist = std::fabs(dot(d, axis));
+  if (dist > proj_a + proj_b) return false;
+  *overlap = proj_a + proj_b - dist;
+  return true;
+}
+
+// ------------------------------------------------------------------ primitive pairs
+bool sphere_sphere(P3 pa, float ra, P3 pb, float rb, Res* o) {
+  const P3 diff = sub(pb, pa);
+  const float dist_sq = dot(diff, diff), min_dist = ra + rb;
+  if (dist_sq >= min_dist * min_dist) return false;
+  const float dist = std::sqrt(dist_sq);
+  const P3 n = dist > kEps ? scl(diff, 1.0f / dist) : P3{0.0f, 0.0f, 1.0f};
+  const float pen = min_dist - dist;
+  *o = Res{add(pa, scl(n, ra - pen * 0.5f)), n, pen};
+  return true;
+}
+
+bool sphere_capsule(P3 sp, float sr, P3 cp, float cr, float hl, const Xf& ct, Res* o) {
+  const P3 axis = ct.vec(P3{0.0f, 0.0f, 1.0f});
+  const P3 p1 = sub(cp, scl(axis, hl)), p2 = add(cp, scl(axis, hl));
+  const P3 closest = closest_on_segment(sp, p1, p2);
+  const P3 diff = sub(sp, closest);
+  const float dist_sq = dot(diff, diff), min_dist = sr + cr;
+  if (dist_sq >= min_dist * min_dist) return false;
+  const float dist = std::sqrt(dist_sq);
+  const P3 n = dist > kEps ? scl(diff, 1.0f / dist) : P3{0.0f, 0.0f, 1.0f};
+  const float pen = min_dist - dist;
+  *o = Res{add(closest, scl(n, cr - pen * 0.5f)), n, pen};
+  return true;
+}
+
+bool sphere_plane(P3 sp, float sr, P3 plane_local, float plane_off, const Xf& pt, Res* o) {
+  const P3 n = pt.vec(P3{0.0f, 0.0f, 1.0f});
+  const P3 plane_point = pt.point(plane_local);
+  const float sd = dot(sub(sp, plane_point), n) - plane_off;
+  if (sd >= sr) return false;
+  const float pen = sr - sd;
+  *o = Res{sub(sp, scl(n, sd + pen * 0.5f)), n, pen};
+  return true;
+}
+
+bool sphere_box(P3 sp, float sr, P3 half, const Xf& bt, Res* o) {
+  const Xf inv = bt.inverse();
+  const P3 ls = inv.point(sp);
+  const P3 cl{clampf(ls.x, -half.x, half.x), clampf(ls.y, -half.y, half.y), clampf(ls.z, -half.z, half.z)};
+  const P3 diff = sub(ls, cl);
+  const float dist_sq = dot(diff, diff);
+  if (dist_sq >= sr * sr) return false;
+  const float dist = std::sqrt(dist_sq);
+  const P3 ln = dist > kEps ? scl(diff, 1.0f / dist) : box_face_normal(ls, half);
+  const P3 wc = bt.point(cl);
+  const P3 n = bt.vec(ln);
+  const float pen = sr - dist;
+  *o = Res{add(wc, scl(n, pen * 0.5f)), n, pen};
+  return true;
+}
+
+bool capsule_capsule(P3 pa, float ra, float hla, const Xf& ta, P3 pb, float rb, float hlb, const Xf& tb, Res* o) {
+  const P3 axa = ta.vec(P3{0.0f, 0.0f, 1.0f}), axb = tb.vec(P3{0.0f, 0.0f, 1.0f});
+  const P3 a1 = sub(pa, scl(axa, hla)), a2 = add(pa, scl(axa, hla));
+  const P3 b1 = sub(pb, scl(axb, hlb)), b2 = add(pb, scl(axb, hlb));
+  P3 ca, cb;
+  closest_between_segments(a1, a2, b1, b2, &ca, &cb);
+  const P3 diff = sub(cb, ca);
+  const float dist_sq = dot(diff, diff), min_dist = ra + rb;
+  if (dist_sq >= min_dist * min_dist) return false;
+  const float dist = std::sqrt(dist_sq);
+  const P3 n = dist > kEps ? scl(diff, 1.0f / dist) : P3{0.0f, 0.0f, 1.0f};
+  const float pen = min_dist - dist;
+  const P3 paw = add(ca, scl(n, ra)), pbw = sub(cb, scl(n, rb));
+  *o = Res{scl(add(paw, pbw), 0.5f), n, pen};
+  return true;
+}
+
+bool capsule_plane(P3 cp, float r, float hl, const Xf& ct, P3 plane_local, const Xf& pt, Res* o) {
+  const P3 axis = ct.vec(P3{0.0f, 0.0f, 1.0f});
+  const P3 pn = pt.vec(P3{0.0f, 0.0f, 1.0f});
+  const P3 pp = pt.point(plane_local);
+  const P3 p1 = sub(cp, scl(axis, hl)), p2 = add(cp, scl(axis, hl));
+  const float d1 = dot(sub(p1, pp), pn) - r, d2 = dot(sub(p2, pp), pn) - r;
+  if (d1 >= 0.0f && d2 >= 0.0f) return false;
+  const P3 deepest = d1 < d2 ? p1 : p2;
+  const float dist = std::fmin(d1, d2);
+  *o = Res{sub(deepest, scl(pn, dist * 0.5f + r)), pn, -dist};
+  return true;
+}
+
+bool box_plane(P3 half, const Xf& bt, P3 plane_local, const Xf& pt, Res* o) {
+  const P3 pn = pt.vec(P3{0.0f, 0.0f, 1.0f});
+  const P3 pp = pt.point(plane_local);
+  const float hx = half.x, hy = half.y, hz = half.z;
+  const P3 corners[8] = {{-hx, -hy, -hz}, {hx, -hy, -hz}, {-hx, hy, -hz}, {hx, hy, -hz},
+                         {-hx, -hy, hz},  {hx, -hy, hz},  {-hx, hy, hz},  {hx, hy, hz}};
+  float min_dist = std::numeric_limits<float>::infinity();
+  P3 deepest{0.0f, 0.0f, 0.0f};
+  for (const P3& c : corners) {
+    const P3 wc = bt.point(c);
+    const float dist = dot(sub(wc, pp), pn);
+    if (dist < min_dist) {
+      min_dist = dist;
+      deepest = wc;
+    }
+  }
+  if (min_dist >= 0.0f) return false;
+  *o = Res{deepest, pn, -min_dist};
+  return true;
+}
+
+bool box_box(P3 pa, P3 ha, const Xf& ta, P3 pb, P3 hb, const Xf& tb, Res* o) {
+  const P3 axa[3] = {ta.vec(P3{1.0f, 0.0f, 0.0f}), ta.vec(P3{0.0f, 1.0f, 0.0f}), ta.vec(P3{0.0f, 0.0f, 1.0f})};
+  const P3 axb[3] = {tb.vec(P3{1.0f, 0.0f, 0.0f}), tb.vec(P3{0.0f, 1.0f, 0.0f}), tb.vec(P3{0.0f, 0.0f, 1.0f})};
+  const P3 d = sub(pb, pa);
+  float min_overlap = std::numeric_limits<float>::infinity(), ov = 0.0f;
+  P3 best{0.0f, 0.0f, 1.0f};
+  for (int i = 0; i < 3; ++i) {
+    if (!test_axis(axa[i], d, axa, ha, axb, hb, &ov)) return false;
+    if (ov < min_overlap) min_overlap = ov, best = axa[i];
+  }
+  for (int i = 0; i < 3; ++i) {
+    if (!test_axis(axb[i], d, axa, ha, axb, hb, &ov)) return false;
+    if (ov < min_overlap) min_overlap = ov, best = axb[i];
+  }
+  for (int i = 0; i < 3; ++i)
+    for (int j = 0; j < 3; ++j) {
+      const P3 ea = cross(axa[i], axb[j]);
+      const float len = std::sqrt(dot(ea, ea));
+      if (len < kEps) continue;
+      const P3 nrm = scl(ea, 1.0f / len);
+      if (!test_axis(nrm, d, axa, ha, axb, hb, &ov)) return false;
+      if (ov < min_overlap) min_overlap = ov, best = nrm;
+    }
+  if (dot(best, d) < 0.0f) best = scl(best, -1.0f);
+  *o = Res{add(pa, scl(d, 0.5f)), best, min_overlap};
+  return true;
+}
+
+Res flip(Res r) { return Res{r.point, scl(r.normal, -1.0f), r.pen}; }
+
+}  // namespace
+
+// detectCollision (narrow_phase.zig:28-136) for the primitive geoms.  Geom types: 0 sphere,
+// 1 capsule, 2 box, 3 plane; anything else reports no contact.
+bool narrow_cpu(const GeomRec& ga, const float* bpa, const float* bqa, const GeomRec& gb, const float* bpb,
+                const float* bqb, float point[3], float normal[3], float* pen) {
+  const Xf ta{p3(bpa), Quat{bqa[0], bqa[1], bqa[2], bqa[3]}};
+  const Xf tb{p3(bpb), Quat{bqb[0], bqb[1], bqb[2], bqb[3]}};
+  const P3 la = p3(ga.pos_size0), lb = p3(gb.pos_size0);
+  const P3 pa = ta.point(la), pb = tb.point(lb);  // getWorldCenter
+  const float ra = ga.pos_size0[3], rb = gb.pos_size0[3];
+  const float hla = ga.params[0], hlb = gb.params[0];  // size[1]
+  const P3 sza{ga.pos_size0[3], ga.params[0], ga.params[1]}, szb{gb.pos_size0[3], gb.params[0], gb.params[1]};
+  const uint32_t ka = ga.type_body[0], kb = gb.type_body[0];
+  Res r{};
+  bool hit = false;
+  if (ka == 0) {
+    if (kb == 0) hit = sphere_sphere(pa, ra, pb, rb, &r);
+    else if (kb == 1) hit = sphere_capsule(pa, ra, pb, rb, hlb, tb, &r);
+    else if (kb == 2) hit = sphere_box(pa, ra, szb, tb, &r);
+    else if (kb == 3) hit = sphere_plane(pa, ra, lb, rb, tb, &r);
+  } else if (ka == 1) {
+    if (kb == 0) {
+      hit = sphere_capsule(pb, rb, pa, ra, hla, ta, &r);
+      if (hit) r = flip(r);
+    } else if (kb == 1) {
+      hit = capsule_capsule(pa, ra, hla, ta, pb, rb, hlb, tb, &r);
+    } else if (kb == 3) {
+      hit = capsule_plane(pa, ra, hla, ta, lb, tb, &r);
+    }
+  } else if (ka == 2) {
+    if (kb == 0) {
+      hit = sphere_box(pb, rb, sza, ta, &r);
+      if (hit) r = flip(r);
+    } else if (kb == 2) {
+      hit = box_box(pa, sza, ta, pb, szb, tb, &r);
+    } else if (kb == 3) {
+      hit = box_plane(sza, ta, lb, tb, &r);
+    }
+  } else if (ka == 3) {
+    if (kb == 0) hit = sphere_plane(pb, rb, la, ra, ta, &r);
+    else if (kb == 1) hit = capsule_plane(pb, rb, hlb, tb, la, ta, &r);
+    else if (kb == 2) hit = box_plane(szb, tb, la, ta, &r);
+    if (hit) r = flip(r);
+  }
+  if (!hit) return false;
+  point[0] = r.point.x, point[1] = r.point.y, point[2] = r.point.z;
+  normal[0] = r.normal.x, normal[1] = r.normal.y, normal[2] = r.normal.z;
+  *pen = r.pen;
+  return true;
+}
+
+}  // namespace zo

@@ -60,6 +60,8 @@ int zo_run_threads(void* h, const float* actions, uint32_t nsteps, uint32_t subs
 extern "C" {
 #endif
 float zo_atan2(float y, float x);
+int zo_set_narrow_mode(void* h, uint32_t mode);
+int zo_narrow_cpu(const float* geom_a, const float* body_a, const float* geom_b, const float* body_b, float* out);
 float zo_asin(float x);
 float zo_effective_mass(float ima, float imb, const float* Ia, const float* Ib, const float* ra, const float* rb,
                         const float* n);

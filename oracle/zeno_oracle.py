@@ -82,6 +82,8 @@ def lib() -> ctypes.CDLL:
         L.zo_dims.argtypes = [vp, ctypes.POINTER(ctypes.c_uint32)]
         L.zo_buffer.restype = vp
         L.zo_buffer.argtypes = [vp, ctypes.c_char_p, ctypes.POINTER(ctypes.c_size_t)]
+        L.zo_set_narrow_mode.argtypes = [vp, ctypes.c_uint32]
+        L.zo_narrow_cpu.argtypes = [f32p, f32p, f32p, f32p, f32p]
         _lib = L
     return _lib
 
@@ -183,5 +185,21 @@ class OracleWorld:
                    alive_bonus, ctrl_cost, seed, env_offset)
         return lib().zo_set_task(self._h, ctypes.byref(t))
 
+    def set_narrow_phase(self, mode: int) -> int:
+        """0: the reference's GPU narrow phase (default); 1: its CPU detectCollision."""
+        return lib().zo_set_narrow_mode(self._h, int(mode))
+
     def model_table(self, name: str) -> bytes:
         return self.raw(name, np.uint8).tobytes()
+
+
+def narrow_cpu(geom_a, body_a, geom_b, body_b):
+    """detectCollision of the restated CPU collision code for two geoms.
+    geom_*: (type, lx, ly, lz, size0, size1, size2); body_*: (px, py, pz, qx, qy, qz, qw).
+    Returns None or (point[3], normal[3], penetration)."""
+    ga, gb = (np.asarray(g, np.float32) for g in (geom_a, geom_b))
+    ba, bb = (np.asarray(b, np.float32) for b in (body_a, body_b))
+    out = np.zeros(7, np.float32)
+    if not lib().zo_narrow_cpu(_fptr(ga), _fptr(ba), _fptr(gb), _fptr(bb), _fptr(out)):
+        return None
+    return out[:3].copy(), out[3:6].copy(), float(out[6])

@@ -260,3 +260,61 @@ def test_hand_over_to_general_kernel(lanes):
             w.step(acts[s])
         runs.append(product_state(w))
     assert not diff_report(runs[0], runs[1])
+
+
+@pytest.mark.parametrize("name,lanes", [("ant", 1), ("ant", 2), ("ant", 4), ("ant", 8), ("cartpole", 1),
+                                        ("pendulum_asset", 1), ("humanoid", None)])
+def test_extended_narrow_phase_bit_exact(name, lanes):
+    """Narrow phase 1 (the reference's CPU detectCollision: sphere/capsule/box/plane pairs,
+    geoms placed by body pose) on both kernels against the oracle.  Humanoid has more
+    hittable candidates in this mode than the compressed-state kernel holds (64), so it
+    runs on the general kernel."""
+    E = 6
+    w, o, c = make_pair(name, E)
+    w.set_narrow_phase(1)
+    assert o.set_narrow_phase(1) == 0
+    if lanes is not None:
+        w.set_launch(lanes, 4)
+    elif name == "humanoid":
+        assert w.get_launch()[0] >= 8
+    rng = np.random.default_rng(21)
+    acts = actions(rng, 12, E, w.action_dim, c["act"])
+    for s in range(12):
+        w.step(acts[s])
+        o.step(acts[s])
+        bad = diff_report(product_state(w), o.state())
+        assert not bad, f"step {s}: {bad}"
+
+
+def test_extended_narrow_phase_drop_scene():
+    """The 64-body drop scene (spheres, capsules, boxes on a plane; general kernel) with
+    the extended narrow phase, where every pair type the reference CPU code handles occurs."""
+    xml = scenes.collision_stress(0)
+    kw = dict(num_envs=2, substeps=2, max_contacts_per_env=256)
+    w, o = ZenoWorld(mjcf_string=xml, **kw), OracleWorld(xml, **kw)
+    w.set_narrow_phase(1)
+    o.set_narrow_phase(1)
+    none = np.zeros((2, 0), np.float32)
+    for s in range(20):
+        w.step(none)
+        o.step(none)
+    st = product_state(w)
+    assert not diff_report(st, o.state())
+    assert (st["contacts"]["position_pen"][..., 3] >= 0).sum() > 0
+
+
+def test_narrow_phase_switch_mid_run():
+    """Switching the narrow phase between steps re-packs the compressed model; the oracle
+    switched at the same steps agrees."""
+    E = 5
+    w, o, c = make_pair("humanoid", E)
+    rng = np.random.default_rng(4)
+    acts = actions(rng, 15, E, w.action_dim, c["act"])
+    for s in range(15):
+        mode = 1 if 5 <= s < 10 else 0
+        w.set_narrow_phase(mode)
+        o.set_narrow_phase(mode)
+        assert w.get_narrow_phase() == mode
+        w.step(acts[s])
+        o.step(acts[s])
+    assert not diff_report(product_state(w), o.state())

@@ -90,6 +90,8 @@ ffi.cdef("""
     int zeno_world_set_stream(ZenoWorldHandle world, void* cuda_stream);
     int zeno_world_device(ZenoWorldHandle world);
     int zeno_world_set_task(ZenoWorldHandle world, const ZenoTaskConfig* task);
+    int zeno_world_set_narrow_phase(ZenoWorldHandle world, uint32_t mode);
+    uint32_t zeno_world_get_narrow_phase(ZenoWorldHandle world);
     int zeno_world_set_launch(ZenoWorldHandle world, int lanes, int envs_per_block);
     int zeno_world_get_launch(ZenoWorldHandle world, int* lanes, int* envs_per_block);
     const void* zeno_world_model_table(ZenoWorldHandle world, const char* name, uint64_t* nbytes);
@@ -415,6 +417,14 @@ class ZenoWorld:
         t.forward_weight, t.alive_bonus, t.ctrl_cost = forward_weight, alive_bonus, ctrl_cost
         t.seed, t.env_offset = seed, env_offset
         _check(_lib.zeno_world_set_task(self._handle, t), "Set task")
+
+    def set_narrow_phase(self, mode: int) -> None:
+        """0: the reference's GPU narrow phase (default); 1: its CPU collision routines
+        (detectCollision: sphere/capsule/box/plane pairs, geoms placed by body pose)."""
+        _check(_lib.zeno_world_set_narrow_phase(self._handle, int(mode)), "Set narrow phase")
+
+    def get_narrow_phase(self) -> int:
+        return int(_lib.zeno_world_get_narrow_phase(self._handle))
 
     def set_launch(self, lanes: int, envs_per_block: int) -> None:
         _check(_lib.zeno_world_set_launch(self._handle, lanes, envs_per_block), "Set launch")

@@ -11,15 +11,22 @@
 
 namespace zb {
 namespace {
-inline bool narrow_pair_supported(uint32_t ta, uint32_t tb) {  // narrow_core's type pairs
+// The type pairs the selected narrow phase can report a contact for: narrow_core (mode 0)
+// or narrow_cpu (mode 1), physics.cuh.
+inline bool narrow_pair_supported(uint32_t mode, uint32_t ta, uint32_t tb) {
+  if (mode == 1) {
+    if (ta > 3 || tb > 3) return false;
+    if ((ta == 1 && tb == 2) || (ta == 2 && tb == 1)) return false;
+    return !(ta == 3 && tb == 3);
+  }
   return (ta == 0 && tb == 0) || (ta == 0 && tb == 3) || (ta == 3 && tb == 0) || (ta == 1 && tb == 3) ||
          (ta == 3 && tb == 1);
 }
 inline float4 f4(const float* v) { return make_float4(v[0], v[1], v[2], v[3]); }
 }  // namespace
 
-bool pack_fast_model(const HostModel& h, uint32_t max_contacts, FModel* out, std::vector<uint8_t>* hot,
-                     std::string* why) {
+bool pack_fast_model(const HostModel& h, uint32_t max_contacts, uint32_t narrow_mode, FModel* out,
+                     std::vector<uint8_t>* hot, std::string* why) {
   auto fail = [&](const char* msg) {
     if (why) *why = msg;
     return false;
@@ -88,7 +95,7 @@ bool pack_fast_model(const HostModel& h, uint32_t max_contacts, FModel* out, std
     const DGeom &ga = h.geoms[pr.ga], &gb = h.geoms[pr.gb];
     const uint32_t rank = uint32_t(std::lower_bound(distinct.begin(), distinct.end(), keys[p]) - distinct.begin());
     uint32_t hidx = fm::kNoHit;
-    if (narrow_pair_supported(ga.type, gb.type)) {
+    if (narrow_pair_supported(narrow_mode, ga.type, gb.type)) {
       if (H >= fm::kH) return fail("more hittable candidates than the constant-bank model holds");
       hidx = H++;
       m.h_pair[hidx] = p;
@@ -98,6 +105,7 @@ bool pack_fast_model(const HostModel& h, uint32_t max_contacts, FModel* out, std
       const DGeom& cap = ga.type == 1 ? ga : gb;
       m.h_cq[hidx] = f4(cap.quat);
       m.h_hl[hidx] = cap.size12_fr_rest[0];
+      m.h_sz[hidx] = make_float4(ga.size12_fr_rest[0], ga.size12_fr_rest[1], gb.size12_fr_rest[0], gb.size12_fr_rest[1]);
       const float fp = ga.size12_fr_rest[2] * gb.size12_fr_rest[2];  // one IEEE product, then sqrt
       m.h_fr[hidx] = std::sqrt(fp);
     }
@@ -120,6 +128,7 @@ bool pack_fast_model(const HostModel& h, uint32_t max_contacts, FModel* out, std
     m.s_info[s] = (d.type & 0xFFu) | ((d.object & 0xFFu) << 8) | (d.offset << 16);
   }
   m.P = P, m.H = H, m.G = h.G;
+  m.narrow_mode = narrow_mode;
 
   // hot image
   std::vector<uint8_t>& img = *hot;
@@ -159,6 +168,7 @@ bool pack_fast_model(const HostModel& h, uint32_t max_contacts, FModel* out, std
   m.o_hhl = section(4 * H), put(m.o_hhl, m.h_hl, 4 * H);
   m.o_hfr = section(4 * H), put(m.o_hfr, m.h_fr, 4 * H);
   m.o_hpair = section(4 * H), put(m.o_hpair, m.h_pair, 4 * H);
+  m.o_hsz = section(16 * H), put(m.o_hsz, m.h_sz, 16 * H);
   m.o_gbody = section(4 * G), put(m.o_gbody, m.g_body, 4 * G);
   m.o_ggpair = section(G * G);
   for (uint32_t ga = 0; ga < G; ++ga) put(m.o_ggpair + ga * G, &m.gg_pair[ga * fm::kG], G);

@@ -47,6 +47,7 @@ struct FModel {
   float4 h_gb[fm::kH];      // geom b offset xyz, size[0]
   float4 h_cq[fm::kH];      // local quaternion of the capsule (when one geom is a capsule)
   float h_hl[fm::kH];       // capsule half length (size[1])
+  float4 h_sz[fm::kH];      // size[1], size[2] of geom a, size[1], size[2] of geom b
   float h_fr[fm::kH];       // combined friction sqrt(f_a * f_b)
   // geoms
   float4 g_ps[fm::kG];               // offset xyz, size[0]
@@ -58,13 +59,14 @@ struct FModel {
   // sensors
   uint32_t s_info[fm::kS];  // type | object << 8 | obs offset << 16
   uint32_t P, H, G;
+  uint32_t narrow_mode;  // 0: reference GPU narrow phase; 1: its CPU detectCollision
   // The tables read inside the substep loop, packed contiguously ("hot image"): the
   // kernel copies them into shared memory once per block, where warp-uniform reads are
   // broadcasts that never miss.  Byte offsets into the image (16-byte aligned sections):
   const uint4* hot;  // device copy of the image
   uint32_t hot_bytes;
   uint32_t o_imi, o_com, o_body, o_jf, o_jaxis, o_jinfo, o_caa, o_cab, o_cat, o_clim, o_cinfo;
-  uint32_t o_pbody, o_pinfo, o_pmd2, o_gps, o_hinfo, o_hga, o_hgb, o_hcq, o_hhl, o_hfr, o_hpair;
+  uint32_t o_pbody, o_pinfo, o_pmd2, o_gps, o_hinfo, o_hga, o_hgb, o_hcq, o_hhl, o_hfr, o_hpair, o_hsz;
   uint32_t o_gbody, o_ggpair;  // geom -> body (u32[G]), (ga, gb) -> candidate (u8[G * G])
   uint32_t o_gforce;           // float4[B], filled by each block: gravity * mass (zero when massless)
   uint32_t o_runs;             // u32[num_runs]: first constraint | count << 12 | type << 24
@@ -73,7 +75,7 @@ struct FModel {
 
 // Fills *out and the hot image *hot (to be uploaded and linked through out->hot); false
 // (with the reason in *why) when the model needs the general kernel.
-bool pack_fast_model(const HostModel& h, uint32_t max_contacts, FModel* out, std::vector<uint8_t>* hot,
-                     std::string* why);
+bool pack_fast_model(const HostModel& h, uint32_t max_contacts, uint32_t narrow_mode, FModel* out,
+                     std::vector<uint8_t>* hot, std::string* why);
 
 }  // namespace zb

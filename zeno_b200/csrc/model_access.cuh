@@ -41,6 +41,7 @@ struct ModelS {
   __device__ __forceinline__ float hhl(uint32_t x) const { return at<float>(f.o_hhl, x); }
   __device__ __forceinline__ float hfr(uint32_t x) const { return at<float>(f.o_hfr, x); }
   __device__ __forceinline__ uint32_t hpair(uint32_t x) const { return at<uint32_t>(f.o_hpair, x); }
+  __device__ __forceinline__ float4 hsz(uint32_t x) const { return at<float4>(f.o_hsz, x); }
   __device__ __forceinline__ uint32_t gbody(uint32_t g) const { return at<uint32_t>(f.o_gbody, g); }
   __device__ __forceinline__ uint32_t ggpair(uint32_t ga, uint32_t gb) const { return h[f.o_ggpair + ga * f.G + gb]; }
   __device__ __forceinline__ float4 gforce(uint32_t b) const { return at<float4>(f.o_gforce, b); }

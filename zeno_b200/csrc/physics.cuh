@@ -304,4 +304,308 @@ __host__ __device__ inline bool narrow_supported(uint32_t ta, uint32_t tb) {
          (ta == 3 && tb == 1);
 }
 
+// ------------------------------------------------------------------------------------
+// Extended narrow phase: the reference's CPU collision routines (src/collision/
+// narrow_phase.zig, detectCollision and the primitive pairs it dispatches to), selected
+// per world with zeno_world_set_narrow_phase(1).  Geoms are placed by their body's pose
+// (centre = R(q_body) local_pos + body_pos); capsule/box axes and plane normals come from
+// the body quaternion.  Box-capsule, plane-plane and cylinder/mesh/heightfield pairs report
+// no contact.  The arithmetic is the Zig source's: plain single-precision +, -, *, /,
+// sqrt, left to right as written, no fused multiply-adds (the file is compiled with
+// -fmad=false).
+// ------------------------------------------------------------------------------------
+namespace cpu_narrow {
+
+constexpr float kEps = 1e-6f;  // constants.EPSILON
+
+struct P3 {
+  float x, y, z;
+};
+__device__ __forceinline__ P3 add(P3 a, P3 b) { return P3{a.x + b.x, a.y + b.y, a.z + b.z}; }
+__device__ __forceinline__ P3 sub(P3 a, P3 b) { return P3{a.x - b.x, a.y - b.y, a.z - b.z}; }
+__device__ __forceinline__ P3 scl(P3 v, float s) { return P3{v.x * s, v.y * s, v.z * s}; }
+__device__ __forceinline__ float dot(P3 a, P3 b) { return __fadd_rn(__fadd_rn(__fmul_rn(a.x, b.x), __fmul_rn(a.y, b.y)), __fmul_rn(a.z, b.z)); }
+__device__ __forceinline__ P3 cross(P3 a, P3 b) {
+  return P3{__fsub_rn(__fmul_rn(a.y, b.z), __fmul_rn(a.z, b.y)), __fsub_rn(__fmul_rn(a.z, b.x), __fmul_rn(a.x, b.z)),
+            __fsub_rn(__fmul_rn(a.x, b.y), __fmul_rn(a.y, b.x))};
+}
+__device__ __forceinline__ float clampf(float v, float lo, float hi) { return fmaxf(lo, fminf(v, hi)); }
+// rotateByQuat (src/physics/body.zig:254-264)
+__device__ __forceinline__ P3 rot(P3 v, float4 q) {
+  const P3 qv{q.x, q.y, q.z};
+  const P3 uv = cross(qv, v);
+  const P3 uuv = cross(qv, uv);
+  return P3{__fadd_rn(v.x, __fmul_rn(2.0f, __fadd_rn(__fmul_rn(q.w, uv.x), uuv.x))),
+            __fadd_rn(v.y, __fmul_rn(2.0f, __fadd_rn(__fmul_rn(q.w, uv.y), uuv.y))),
+            __fadd_rn(v.z, __fmul_rn(2.0f, __fadd_rn(__fmul_rn(q.w, uv.z), uuv.z)))};
+}
+struct Xf {  // body.Transform
+  P3 p;
+  float4 q;
+  __device__ __forceinline__ P3 point(P3 v) const { return add(rot(v, q), p); }
+  __device__ __forceinline__ P3 vec(P3 v) const { return rot(v, q); }
+  __device__ __forceinline__ Xf inverse() const {
+    const float4 iq = make_float4(-q.x, -q.y, -q.z, q.w);
+    return Xf{rot(P3{-p.x, -p.y, -p.z}, iq), iq};
+  }
+};
+struct Res {
+  P3 point, normal;
+  float pen;
+};
+
+__device__ __forceinline__ P3 closest_on_segment(P3 point, P3 s, P3 e) {
+  const P3 seg = sub(e, s);
+  const float len_sq = dot(seg, seg);
+  if (len_sq < kEps) return s;
+  const float t = clampf(__fdiv_rn(dot(sub(point, s), seg), len_sq), 0.0f, 1.0f);
+  return add(s, scl(seg, t));
+}
+
+__device__ __forceinline__ void closest_between_segments(P3 a1, P3 a2, P3 b1, P3 b2, P3& pa, P3& pb) {
+  const P3 d1 = sub(a2, a1), d2 = sub(b2, b1), r = sub(a1, b1);
+  const float a = dot(d1, d1), e = dot(d2, d2), f = dot(d2, r);
+  float s = 0.0f, t = 0.0f;
+  if (a < kEps && e < kEps) {
+    pa = a1, pb = b1;
+    return;
+  }
+  if (a < kEps) {
+    t = clampf(__fdiv_rn(f, e), 0.0f, 1.0f);
+  } else {
+    const float c = dot(d1, r);
+    if (e < kEps) {
+      s = clampf(__fdiv_rn(-c, a), 0.0f, 1.0f);
+    } else {
+      const float b = dot(d1, d2);
+      const float denom = __fsub_rn(__fmul_rn(a, e), __fmul_rn(b, b));
+      if (denom != 0.0f) s = clampf(__fdiv_rn(__fsub_rn(__fmul_rn(b, f), __fmul_rn(c, e)), denom), 0.0f, 1.0f);
+      t = __fdiv_rn(__fadd_rn(__fmul_rn(b, s), f), e);
+      if (t < 0.0f) {
+        t = 0.0f;
+        s = clampf(__fdiv_rn(-c, a), 0.0f, 1.0f);
+      } else if (t > 1.0f) {
+        t = 1.0f;
+        s = clampf(__fdiv_rn(__fsub_rn(b, c), a), 0.0f, 1.0f);
+      }
+    }
+  }
+  pa = add(a1, scl(d1, s));
+  pb = add(b1, scl(d2, t));
+}
+
+__device__ __forceinline__ P3 box_face_normal(P3 p, P3 h) {  // the face with the largest distance, as written
+  const float pc[3] = {p.x, p.y, p.z}, hc[3] = {h.x, h.y, h.z};
+  float max_dist = -__int_as_float(0x7f800000);
+  float n[3] = {0.0f, 0.0f, 1.0f};
+#pragma unroll
+  for (int i = 0; i < 3; ++i) {
+    const float d_pos = __fsub_rn(hc[i], pc[i]), d_neg = __fadd_rn(hc[i], pc[i]);
+    if (d_pos > max_dist) {
+      max_dist = d_pos;
+      n[0] = n[1] = n[2] = 0.0f;
+      n[i] = 1.0f;
+    }
+    if (d_neg > max_dist) {
+      max_dist = d_neg;
+      n[0] = n[1] = n[2] = 0.0f;
+      n[i] = -1.0f;
+    }
+  }
+  return P3{n[0], n[1], n[2]};
+}
+
+__device__ __forceinline__ bool test_axis(P3 axis, P3 d, const P3* axa, P3 ha, const P3* axb, P3 hb, float& overlap) {
+  const float proj_a = __fadd_rn(__fadd_rn(__fmul_rn(ha.x, fabsf(dot(axis, axa[0]))), __fmul_rn(ha.y, fabsf(dot(axis, axa[1])))),
+                                 __fmul_rn(ha.z, fabsf(dot(axis, axa[2]))));
+  const float proj_b = __fadd_rn(__fadd_rn(__fmul_rn(hb.x, fabsf(dot(axis, axb[0]))), __fmul_rn(hb.y, fabsf(dot(axis, axb[1])))),
+                                 __fmul_rn(hb.z, fabsf(dot(axis, axb[2]))));
+  const float dist = fabsf(dot(d, axis));
+  const float sum = __fadd_rn(proj_a, proj_b);
+  if (dist > sum) return false;
+  overlap = __fsub_rn(sum, dist);
+  return true;
+}
+
+__device__ __forceinline__ bool sphere_sphere(P3 pa, float ra, P3 pb, float rb, Res& o) {
+  const P3 diff = sub(pb, pa);
+  const float dist_sq = dot(diff, diff), min_dist = __fadd_rn(ra, rb);
+  if (dist_sq >= __fmul_rn(min_dist, min_dist)) return false;
+  const float dist = __fsqrt_rn(dist_sq);
+  const P3 n = dist > kEps ? scl(diff, __fdiv_rn(1.0f, dist)) : P3{0.0f, 0.0f, 1.0f};
+  const float pen = __fsub_rn(min_dist, dist);
+  o = Res{add(pa, scl(n, __fsub_rn(ra, __fmul_rn(pen, 0.5f)))), n, pen};
+  return true;
+}
+
+__device__ __forceinline__ bool sphere_capsule(P3 sp, float sr, P3 cp, float cr, float hl, const Xf& ct, Res& o) {
+  const P3 axis = ct.vec(P3{0.0f, 0.0f, 1.0f});
+  const P3 p1 = sub(cp, scl(axis, hl)), p2 = add(cp, scl(axis, hl));
+  const P3 closest = closest_on_segment(sp, p1, p2);
+  const P3 diff = sub(sp, closest);
+  const float dist_sq = dot(diff, diff), min_dist = __fadd_rn(sr, cr);
+  if (dist_sq >= __fmul_rn(min_dist, min_dist)) return false;
+  const float dist = __fsqrt_rn(dist_sq);
+  const P3 n = dist > kEps ? scl(diff, __fdiv_rn(1.0f, dist)) : P3{0.0f, 0.0f, 1.0f};
+  const float pen = __fsub_rn(min_dist, dist);
+  o = Res{add(closest, scl(n, __fsub_rn(cr, __fmul_rn(pen, 0.5f)))), n, pen};
+  return true;
+}
+
+__device__ __forceinline__ bool sphere_plane(P3 sp, float sr, P3 plane_local, float plane_off, const Xf& pt, Res& o) {
+  const P3 n = pt.vec(P3{0.0f, 0.0f, 1.0f});
+  const P3 plane_point = pt.point(plane_local);
+  const float sd = __fsub_rn(dot(sub(sp, plane_point), n), plane_off);
+  if (sd >= sr) return false;
+  const float pen = __fsub_rn(sr, sd);
+  o = Res{sub(sp, scl(n, __fadd_rn(sd, __fmul_rn(pen, 0.5f)))), n, pen};
+  return true;
+}
+
+__device__ __forceinline__ bool sphere_box(P3 sp, float sr, P3 half, const Xf& bt, Res& o) {
+  const Xf inv = bt.inverse();
+  const P3 ls = inv.point(sp);
+  const P3 cl{clampf(ls.x, -half.x, half.x), clampf(ls.y, -half.y, half.y), clampf(ls.z, -half.z, half.z)};
+  const P3 diff = sub(ls, cl);
+  const float dist_sq = dot(diff, diff);
+  if (dist_sq >= __fmul_rn(sr, sr)) return false;
+  const float dist = __fsqrt_rn(dist_sq);
+  const P3 ln = dist > kEps ? scl(diff, __fdiv_rn(1.0f, dist)) : box_face_normal(ls, half);
+  const P3 wc = bt.point(cl);
+  const P3 n = bt.vec(ln);
+  const float pen = __fsub_rn(sr, dist);
+  o = Res{add(wc, scl(n, __fmul_rn(pen, 0.5f))), n, pen};
+  return true;
+}
+
+__device__ __forceinline__ bool capsule_capsule(P3 pa, float ra, float hla, const Xf& ta, P3 pb, float rb, float hlb,
+                                                const Xf& tb, Res& o) {
+  const P3 axa = ta.vec(P3{0.0f, 0.0f, 1.0f}), axb = tb.vec(P3{0.0f, 0.0f, 1.0f});
+  const P3 a1 = sub(pa, scl(axa, hla)), a2 = add(pa, scl(axa, hla));
+  const P3 b1 = sub(pb, scl(axb, hlb)), b2 = add(pb, scl(axb, hlb));
+  P3 ca, cb;
+  closest_between_segments(a1, a2, b1, b2, ca, cb);
+  const P3 diff = sub(cb, ca);
+  const float dist_sq = dot(diff, diff), min_dist = __fadd_rn(ra, rb);
+  if (dist_sq >= __fmul_rn(min_dist, min_dist)) return false;
+  const float dist = __fsqrt_rn(dist_sq);
+  const P3 n = dist > kEps ? scl(diff, __fdiv_rn(1.0f, dist)) : P3{0.0f, 0.0f, 1.0f};
+  const float pen = __fsub_rn(min_dist, dist);
+  const P3 paw = add(ca, scl(n, ra)), pbw = sub(cb, scl(n, rb));
+  o = Res{scl(add(paw, pbw), 0.5f), n, pen};
+  return true;
+}
+
+__device__ __forceinline__ bool capsule_plane(P3 cp, float r, float hl, const Xf& ct, P3 plane_local, const Xf& pt,
+                                              Res& o) {
+  const P3 axis = ct.vec(P3{0.0f, 0.0f, 1.0f});
+  const P3 pn = pt.vec(P3{0.0f, 0.0f, 1.0f});
+  const P3 pp = pt.point(plane_local);
+  const P3 p1 = sub(cp, scl(axis, hl)), p2 = add(cp, scl(axis, hl));
+  const float d1 = __fsub_rn(dot(sub(p1, pp), pn), r), d2 = __fsub_rn(dot(sub(p2, pp), pn), r);
+  if (d1 >= 0.0f && d2 >= 0.0f) return false;
+  const P3 deepest = d1 < d2 ? p1 : p2;
+  const float dist = fminf(d1, d2);
+  o = Res{sub(deepest, scl(pn, __fadd_rn(__fmul_rn(dist, 0.5f), r))), pn, -dist};
+  return true;
+}
+
+__device__ __forceinline__ bool box_plane(P3 half, const Xf& bt, P3 plane_local, const Xf& pt, Res& o) {
+  const P3 pn = pt.vec(P3{0.0f, 0.0f, 1.0f});
+  const P3 pp = pt.point(plane_local);
+  float min_dist = __int_as_float(0x7f800000);
+  P3 deepest{0.0f, 0.0f, 0.0f};
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {  // corner order of boxPlane: x fastest, then y, then z
+    const P3 corner{(c & 1) ? half.x : -half.x, (c & 2) ? half.y : -half.y, (c & 4) ? half.z : -half.z};
+    const P3 wc = bt.point(corner);
+    const float dist = dot(sub(wc, pp), pn);
+    if (dist < min_dist) {
+      min_dist = dist;
+      deepest = wc;
+    }
+  }
+  if (min_dist >= 0.0f) return false;
+  o = Res{deepest, pn, -min_dist};
+  return true;
+}
+
+__device__ __forceinline__ bool box_box(P3 pa, P3 ha, const Xf& ta, P3 pb, P3 hb, const Xf& tb, Res& o) {
+  const P3 axa[3] = {ta.vec(P3{1.0f, 0.0f, 0.0f}), ta.vec(P3{0.0f, 1.0f, 0.0f}), ta.vec(P3{0.0f, 0.0f, 1.0f})};
+  const P3 axb[3] = {tb.vec(P3{1.0f, 0.0f, 0.0f}), tb.vec(P3{0.0f, 1.0f, 0.0f}), tb.vec(P3{0.0f, 0.0f, 1.0f})};
+  const P3 d = sub(pb, pa);
+  float min_overlap = __int_as_float(0x7f800000), ov = 0.0f;
+  P3 best{0.0f, 0.0f, 1.0f};
+  for (int i = 0; i < 3; ++i) {
+    if (!test_axis(axa[i], d, axa, ha, axb, hb, ov)) return false;
+    if (ov < min_overlap) min_overlap = ov, best = axa[i];
+  }
+  for (int i = 0; i < 3; ++i) {
+    if (!test_axis(axb[i], d, axa, ha, axb, hb, ov)) return false;
+    if (ov < min_overlap) min_overlap = ov, best = axb[i];
+  }
+  for (int i = 0; i < 3; ++i)
+    for (int j = 0; j < 3; ++j) {
+      const P3 ea = cross(axa[i], axb[j]);
+      const float len = __fsqrt_rn(dot(ea, ea));
+      if (len < kEps) continue;
+      const P3 nrm = scl(ea, __fdiv_rn(1.0f, len));
+      if (!test_axis(nrm, d, axa, ha, axb, hb, ov)) return false;
+      if (ov < min_overlap) min_overlap = ov, best = nrm;
+    }
+  if (dot(best, d) < 0.0f) best = scl(best, -1.0f);
+  o = Res{add(pa, scl(d, 0.5f)), best, min_overlap};
+  return true;
+}
+
+}  // namespace cpu_narrow
+
+// True for the type pairs narrow_cpu can report a contact for (types 0 sphere, 1 capsule,
+// 2 box, 3 plane; no box-capsule, no plane-plane).
+__host__ __device__ inline bool narrow_cpu_supported(uint32_t ta, uint32_t tb) {
+  if (ta > 3 || tb > 3) return false;
+  if ((ta == 1 && tb == 2) || (ta == 2 && tb == 1)) return false;
+  return !(ta == 3 && tb == 3);
+}
+
+// detectCollision (narrow_phase.zig:28-136).  la/lb: geom local position, size[0]; sa/sb:
+// size[1], size[2]; bpa/bpb, bqa/bqb: body position and quaternion.
+__device__ __forceinline__ bool narrow_cpu(uint32_t ka, uint32_t kb, float4 la, float2 sa, float4 lb, float2 sb,
+                                           float4 bpa, float4 bqa, float4 bpb, float4 bqb, V3& point, V3& normal,
+                                           float& pen) {
+  using namespace cpu_narrow;
+  const Xf ta{P3{bpa.x, bpa.y, bpa.z}, bqa}, tb{P3{bpb.x, bpb.y, bpb.z}, bqb};
+  const P3 lpa{la.x, la.y, la.z}, lpb{lb.x, lb.y, lb.z};
+  const P3 pa = ta.point(lpa), pb = tb.point(lpb);
+  const float ra = la.w, rb = lb.w;
+  const P3 sza{la.w, sa.x, sa.y}, szb{lb.w, sb.x, sb.y};
+  Res r{};
+  bool hit = false, flip = false;
+  if (ka == 0) {
+    if (kb == 0) hit = sphere_sphere(pa, ra, pb, rb, r);
+    else if (kb == 1) hit = sphere_capsule(pa, ra, pb, rb, sb.x, tb, r);
+    else if (kb == 2) hit = sphere_box(pa, ra, szb, tb, r);
+    else if (kb == 3) hit = sphere_plane(pa, ra, lpb, rb, tb, r);
+  } else if (ka == 1) {
+    if (kb == 0) hit = sphere_capsule(pb, rb, pa, ra, sa.x, ta, r), flip = true;
+    else if (kb == 1) hit = capsule_capsule(pa, ra, sa.x, ta, pb, rb, sb.x, tb, r);
+    else if (kb == 3) hit = capsule_plane(pa, ra, sa.x, ta, lpb, tb, r);
+  } else if (ka == 2) {
+    if (kb == 0) hit = sphere_box(pb, rb, sza, ta, r), flip = true;
+    else if (kb == 2) hit = box_box(pa, sza, ta, pb, szb, tb, r);
+    else if (kb == 3) hit = box_plane(sza, ta, lpb, tb, r);
+  } else if (ka == 3) {
+    flip = true;
+    if (kb == 0) hit = sphere_plane(pb, rb, lpa, ra, ta, r);
+    else if (kb == 1) hit = capsule_plane(pb, rb, sb.x, tb, lpa, ta, r);
+    else if (kb == 2) hit = box_plane(szb, tb, lpa, ta, r);
+  }
+  if (!hit) return false;
+  if (flip) r.normal = scl(r.normal, -1.0f);
+  point = V3{r.point.x, r.point.y, r.point.z};
+  normal = V3{r.normal.x, r.normal.y, r.normal.z};
+  pen = r.pen;
+  return true;
+}
+
 }  // namespace zb

@@ -122,20 +122,29 @@ struct ArrBodies {
   __device__ __forceinline__ float4& ang(uint32_t b) { return w[b]; }
 };
 
-// Narrow phase for one slot (narrow_phase, all_shaders.metal:751-894)
-__device__ __forceinline__ void narrow(uint32_t pk, const DGeom* geoms, const float4* pos, float restitution,
-                                       float4& cpp, float4& cnf, float4& cim) {
+// Narrow phase for one slot (narrow_phase, all_shaders.metal:751-894; mode 1: the
+// reference's CPU detectCollision, src/collision/narrow_phase.zig:28-136)
+__device__ __forceinline__ void narrow(uint32_t pk, const DGeom* geoms, const float4* pos, const float4* quat,
+                                       uint32_t mode, float restitution, float4& cpp, float4& cnf, float4& cim) {
   const DGeom& gA = geoms[pk_ga(pk)];
   const DGeom& gB = geoms[pk_gb(pk)];
   const float4 ga0 = __ldg(reinterpret_cast<const float4*>(gA.pos_size0));
   const float4 gb0 = __ldg(reinterpret_cast<const float4*>(gB.pos_size0));
-  const V3 pa = v3(pos[pk_a(pk)]) + v3(ga0), pb = v3(pos[pk_b(pk)]) + v3(gb0);
   const uint32_t ta = __ldg(&gA.type), tb = __ldg(&gB.type);
-  const DGeom& cg = ta == 1 ? gA : gB;
   V3 normal{0, 0, 0}, point{0, 0, 0};
   float pen = 0.0f;
-  const bool hit = narrow_core(ta, tb, pa, pb, ga0.w, gb0.w, __ldg(&cg.size12_fr_rest[0]),
-                               __ldg(reinterpret_cast<const float4*>(cg.quat)), point, normal, pen);
+  bool hit;
+  if (mode == 1) {
+    const float2 sa = make_float2(__ldg(&gA.size12_fr_rest[0]), __ldg(&gA.size12_fr_rest[1]));
+    const float2 sb = make_float2(__ldg(&gB.size12_fr_rest[0]), __ldg(&gB.size12_fr_rest[1]));
+    hit = narrow_cpu(ta, tb, ga0, sa, gb0, sb, pos[pk_a(pk)], quat[pk_a(pk)], pos[pk_b(pk)], quat[pk_b(pk)], point,
+                     normal, pen);
+  } else {
+    const V3 pa = v3(pos[pk_a(pk)]) + v3(ga0), pb = v3(pos[pk_b(pk)]) + v3(gb0);
+    const DGeom& cg = ta == 1 ? gA : gB;
+    hit = narrow_core(ta, tb, pa, pb, ga0.w, gb0.w, __ldg(&cg.size12_fr_rest[0]),
+                      __ldg(reinterpret_cast<const float4*>(cg.quat)), point, normal, pen);
+  }
   if (hit) {
     const float fr = __fsqrt_rn(__ldg(&gA.size12_fr_rest[2]) * __ldg(&gB.size12_fr_rest[2]));
     cpp = with_w(point, pen);
@@ -399,7 +408,7 @@ __device__ __forceinline__ void step_env(const StepArgs& a, uint32_t e, unsigned
     // ---- narrow phase ----
     for (uint32_t i = l; i < n; i += L) {
       const uint32_t st = ord[i];
-      narrow(cpk[st], a.geoms, pos, a.restitution, cpp[st], cnf[st], cim[st]);
+      narrow(cpk[st], a.geoms, pos, quat, a.narrow_mode, a.restitution, cpp[st], cnf[st], cim[st]);
     }
     __syncwarp(gmask);
     // ---- warm start: best previous contact of the same pair within 0.2 ----

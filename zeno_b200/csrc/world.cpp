@@ -81,7 +81,7 @@ World* World::create(const Scene& sc, const WorldConfig& cfg, std::string* err) 
   w->envs_per_block_ = int(std::min<uint32_t>(4u, uint32_t(smem_cap) / env_bytes));
   // environment-per-lane kernel when the model packs into its fixed-capacity tables
   std::string why;
-  w->fast_ok_ = pack_fast_model(m, M, &w->fmodel_, &w->hot_image_, &why);
+  w->fast_ok_ = pack_fast_model(m, M, w->narrow_mode_, &w->fmodel_, &w->hot_image_, &why);
 
   if (cudaStreamCreateWithFlags(&w->own_stream_, cudaStreamNonBlocking) != cudaSuccess) return fail("stream", w);
   w->stream_ = w->own_stream_;
@@ -126,6 +126,7 @@ World* World::create(const Scene& sc, const WorldConfig& cfg, std::string* err) 
   upload(&w->d_init_, m.init_state);
   if (w->fast_ok_) {
     upload(&w->d_hot_, w->hot_image_);
+    w->hot_capacity_ = w->hot_image_.size();
     w->fmodel_.hot = reinterpret_cast<const uint4*>(w->d_hot_);
     e = e ? e : w->device_buf(&w->pose_scratch_, size_t(2) * B * E);
   }
@@ -193,6 +194,7 @@ StepArgs World::args(uint32_t substeps, const float* actions, const uint8_t* mas
   a.iterations = cfg_.contact_iterations;
   a.substeps = substeps;
   a.actuators_unique = m.actuators_unique ? 1u : 0u;
+  a.narrow_mode = narrow_mode_;
   a.dt = timestep_ / float(substeps > 1 ? substeps : 1u);  // world.zig:699-702
   a.inv_dt = 1.0f / a.dt;
   a.inv_step = timestep_ > 0 ? 1.0f / timestep_ : 0.0f;  // world.zig:736
@@ -397,6 +399,7 @@ int World::set_launch(int lanes, int envs_per_block) {
     fast_lanes_ = lanes;
     fast_epb_ = envs_per_block;
     use_fast_ = true;
+    prefer_general_ = false;
     return 0;
   }
   if (lanes != 8 && lanes != 16 && lanes != 32) return -6;
@@ -407,6 +410,42 @@ int World::set_launch(int lanes, int envs_per_block) {
   lanes_ = lanes;
   envs_per_block_ = envs_per_block;
   use_fast_ = false;
+  prefer_general_ = true;
+  return 0;
+}
+
+// Selects the narrow phase and re-packs the compressed-state model (its hittable pairs
+// depend on it); a model that no longer fits runs on the general kernel.
+int World::set_narrow_phase(uint32_t mode) {
+  if (mode > 1) return -6;
+  if (mode == narrow_mode_) return 0;
+  if (cudaStreamSynchronize(stream_) != cudaSuccess) return -4;
+  narrow_mode_ = mode;
+  std::string why;
+  std::vector<uint8_t> img;
+  FModel fm{};
+  const bool ok = pack_fast_model(model_, cfg_.max_contacts_per_env, mode, &fm, &img, &why);
+  if (ok && img.size() > hot_capacity_) {
+    uint8_t* p = nullptr;
+    if (device_buf(&p, img.size()) != cudaSuccess) return -5;
+    d_hot_ = p;
+    hot_capacity_ = img.size();
+  }
+  if (ok && !pose_scratch_ &&
+      device_buf(&pose_scratch_, size_t(2) * model_.B * cfg_.num_envs) != cudaSuccess)
+    return -5;
+  if (ok && cudaMemcpy(d_hot_, img.data(), img.size(), cudaMemcpyHostToDevice) != cudaSuccess) return -4;
+  const bool was_fast = use_fast_;
+  fast_ok_ = ok;
+  fmodel_ = fm;
+  hot_image_ = std::move(img);
+  fmodel_.hot = reinterpret_cast<const uint4*>(d_hot_);
+  use_fast_ = false;
+  if (fast_ok_ && !prefer_general_) {  // keep a caller's shape when it still fits
+    const int lanes = fast_lanes_, epb = fast_epb_;
+    choose_fast_shape();
+    if (was_fast && set_launch(lanes, epb) != 0) choose_fast_shape();
+  }
   return 0;
 }
 

@@ -51,6 +51,9 @@ class World {
   void set_gravity(float gx, float gy, float gz);
   int set_timestep(float ts);
   int set_task(const DTask& t);
+  // 0: the reference's GPU narrow phase (default); 1: its CPU detectCollision routines.
+  int set_narrow_phase(uint32_t mode);
+  uint32_t narrow_phase() const { return narrow_mode_; }
   // lanes 1, 2, 4: compressed-state kernel with that many lanes per environment and
   // envs_per_block (1..32) environments per block; lanes 8, 16, 32: general kernel only.
   // -6 when the shape is invalid or unsupported.
@@ -105,11 +108,14 @@ class World {
   int envs_per_block_ = 4;
   bool fast_ok_ = false;     // the model packs into FModel
   bool use_fast_ = false;
+  bool prefer_general_ = false;  // the caller selected the general kernel
   int fast_lanes_ = 2;
   int fast_epb_ = 32;
   FModel fmodel_{};
   std::vector<uint8_t> hot_image_;
   uint8_t* d_hot_ = nullptr;
+  size_t hot_capacity_ = 0;
+  uint32_t narrow_mode_ = 0;
   float4* pose_scratch_ = nullptr;
   uint64_t bytes_ = 0;
   cudaStream_t own_stream_ = nullptr;

@@ -100,6 +100,7 @@ struct StepArgs {
   uint32_t num_envs, B, J, A, G, S, M, K, obs_dim, num_colors, num_pairs, iterations;
   uint32_t substeps;
   uint32_t actuators_unique;  // 1: no two actuators drive the same joint
+  uint32_t narrow_mode;       // 0: reference GPU narrow phase; 1: its CPU detectCollision
   float dt, inv_dt, inv_step;  // dt = timestep/substeps, inv_dt = 1/dt, inv_step = 1/timestep
   float gravity[3];
   float baumgarte, slop, restitution;
