@@ -209,7 +209,7 @@ int zeno_world_set_task(ZenoWorldHandle world, const ZenoTaskConfig* task);
 int zeno_world_set_narrow_phase(ZenoWorldHandle world, uint32_t mode);
 uint32_t zeno_world_get_narrow_phase(ZenoWorldHandle world);
 
-/* Launch shape of the step.  lanes 1, 2 or 4: the compressed-state kernel with that many
+/* Launch shape of the step.  lanes 1 or 2: the compressed-state kernel with that many
  * lanes per environment and envs_per_block (1..32) environments per block; lanes 8, 16
  * or 32: the general kernel (lanes * envs_per_block <= 256, shared memory permitting).
  * Returns -6 when the shape does not fit the model. */

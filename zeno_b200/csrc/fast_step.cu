@@ -1,7 +1,7 @@
 // Step kernel with compressed per-environment state, for sm_100a.
 //
 // One launch runs every substep of one World.step (src/world/world.zig:694-792).  Each
-// environment is owned by a group of L lanes (L = 1, 2 or 4) that runs the whole step for
+// environment is owned by a group of L lanes (L = 1 or 2) that runs the whole step for
 // it in the order the reference's dispatch sequence defines (world.zig:934-1293).  All
 // environments of a launch share one model, so a warp executes one coherent instruction
 // stream, and the model is read from a per-block shared-memory copy with warp-uniform
@@ -927,7 +927,7 @@ static cudaError_t launch_l(const StepArgs& args, const FModel& model, int envs_
   return cudaGetLastError();
 }
 
-bool fast_lanes_supported(int lanes) { return lanes == 1 || lanes == 2 || lanes == 4; }
+bool fast_lanes_supported(int lanes) { return lanes == 1 || lanes == 2; }
 
 cudaError_t launch_fast_step(const StepArgs& args, const FModel& model, int lanes, int envs_per_block,
                              cudaStream_t stream) {
@@ -936,7 +936,6 @@ cudaError_t launch_fast_step(const StepArgs& args, const FModel& model, int lane
   switch (lanes) {
     case 1: return launch_l<1>(args, model, envs_per_block, stream);
     case 2: return launch_l<2>(args, model, envs_per_block, stream);
-    case 4: return launch_l<4>(args, model, envs_per_block, stream);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -963,7 +962,6 @@ int fast_max_active_blocks(const StepArgs& args, const FModel& model, int lanes,
   switch (lanes) {
     case 1: return max_active_l<1>(args, model, envs_per_block);
     case 2: return max_active_l<2>(args, model, envs_per_block);
-    case 4: return max_active_l<4>(args, model, envs_per_block);
     default: return 0;
   }
 }

@@ -21,7 +21,7 @@ cudaError_t launch_step(const StepArgs& args, int lanes, int envs_per_block, cud
 // Shared memory one environment needs in the compressed-state kernel with L lanes per env.
 uint32_t fast_env_smem_bytes(uint32_t B, uint32_t J, uint32_t M, uint32_t H, uint32_t L);
 
-// Compressed-state kernel: `lanes` (1, 2 or 4) lanes per environment, envs_per_block
+// Compressed-state kernel: `lanes` (1 or 2) lanes per environment, envs_per_block
 // (1..32) environments per block.  Environments it cannot
 // represent are appended to args.odd_list / odd_count untouched, for a following
 // list-mode launch_step.

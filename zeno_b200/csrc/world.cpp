@@ -106,7 +106,6 @@ World* World::create(const Scene& sc, const WorldConfig& cfg, std::string* err) 
   e = e ? e : w->device_buf(&w->episode_, E);
   e = e ? e : w->device_buf(&w->d_actions_, size_t(E) * (m.A ? m.A : 1));
   e = e ? e : w->device_buf(&w->d_mask_, E);
-  e = e ? e : w->device_buf(&w->d_status_, 4);
   e = e ? e : w->device_buf(&w->d_odd_, size_t(E) + 2);
   auto upload = [&](auto** dst, const auto& v) {
     if (e != cudaSuccess) return;
@@ -208,7 +207,6 @@ StepArgs World::args(uint32_t substeps, const float* actions, const uint8_t* mas
   a.contacts = contacts, a.counts = counts, a.prev_counts = prev_counts_, a.prev_contacts = prev_contacts_;
   a.prev_sep = prev_sep_, a.episode = episode_, a.actions = actions, a.step_mask = mask;
   a.task = task_;
-  a.status = d_status_;
   a.odd_count = d_odd_;
   a.odd_list = d_odd_ + 2;
   a.pose_scratch = pose_scratch_;

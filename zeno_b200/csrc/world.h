@@ -54,7 +54,7 @@ class World {
   // 0: the reference's GPU narrow phase (default); 1: its CPU detectCollision routines.
   int set_narrow_phase(uint32_t mode);
   uint32_t narrow_phase() const { return narrow_mode_; }
-  // lanes 1, 2, 4: compressed-state kernel with that many lanes per environment and
+  // lanes 1, 2: compressed-state kernel with that many lanes per environment and
   // envs_per_block (1..32) environments per block; lanes 8, 16, 32: general kernel only.
   // -6 when the shape is invalid or unsupported.
   int set_launch(int lanes, int envs_per_block);
@@ -141,7 +141,6 @@ class World {
   uint32_t* episode_ = nullptr;
   float* d_actions_ = nullptr;
   uint8_t* d_mask_ = nullptr;
-  uint32_t* d_status_ = nullptr;
   uint32_t* d_odd_ = nullptr;  // [0] hand-over count, [1] blocks done, [2..] env indices
   std::vector<void*> allocations_;
 };

@@ -137,7 +137,6 @@ struct StepArgs {
   const float* actions;      // E*A
   const uint8_t* step_mask;  // null, or per-env: 0 = compute but publish only the caches
   DTask task;
-  uint32_t* status;          // device status word (bit 0: shared-memory plan exceeded)
   // hand-over from the environment-per-lane kernel to the general kernel
   uint32_t* odd_list;        // environments the fast kernel left untouched
   uint32_t* odd_count;
