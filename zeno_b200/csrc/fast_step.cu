@@ -215,7 +215,6 @@ __device__ __forceinline__ void run_env(const StepArgs& a, const FModel& f, cons
   Contact* gc = a.contacts + size_t(e) * M;
   const Contact* gprev = sep ? a.prev_contacts + size_t(e) * M : gc;
   const uint32_t n_prev0 = prev_count0 < M ? prev_count0 : M;
-  (void)n0;
   for (uint32_t h = lane; h < H; h += L) nlh[h * ne] = 0;
 
   const float dt = a.dt, inv_dt = a.inv_dt;
@@ -641,7 +640,7 @@ __device__ __forceinline__ void run_env(const StepArgs& a, const FModel& f, cons
           out[3] = *reinterpret_cast<const uint4*>(&im);
         } else if (inplace && o == j) {
           reinterpret_cast<float*>(out)[3] = -1.0f;
-          out[2] = idx;
+          if (o >= n0) out[2] = idx;  // a slot loaded at this position keeps its stored tuple
         } else {
           uint4 r[4];
           if (cycle && o == i) {
@@ -820,39 +819,39 @@ __global__ void __launch_bounds__(32 * L) fast_step_kernel(const __grid_constant
   const Contact* gcb = a.contacts + size_t(e0) * M;
   constexpr uint32_t kU = 8;  // slots per thread per round: their loads are in flight together
   // An environment is handed over (s_hdr[3] set) when a slot tuple of either list is not
-  // a broad-phase candidate, when a list is not sorted by key, or when a valid previous
-  // slot carries non-zero tangent impulses (a warm start would copy them; this kernel
-  // keeps only normal impulses).  This library never writes any of these.
+  // a broad-phase candidate, when a list is not sorted by key, or when a slot of the
+  // previous list carries non-zero tangent impulses (a warm start would copy them; this
+  // kernel keeps only normal impulses).  This library never writes any of these.  Only
+  // the second half of each 64-byte record (indices, impulses) is read.
   for (uint32_t t0 = tid; t0 < nb * M; t0 += kU * nt) {
-    uint4 ix[kU], px[kU], pim[kU];
-    float im[kU], ppen[kU];
+    uint4 ix[kU], iq[kU];
 #pragma unroll
     for (uint32_t u = 0; u < kU; ++u) {
       const uint32_t t = t0 + u * nt;
       if (t >= nb * M) continue;
-      const uint32_t el = t / M, i = t - el * M;
       ix[u] = *reinterpret_cast<const uint4*>(gcb[t].indices);
-      im[u] = gcb[t].impulses[0];
-      const Contact* pr = (s_hdr[2 * ne + el] != 0 && i < s_hdr[ne + el]) ? a.prev_contacts + size_t(e0 + el) * M + i
-                                                                          : gcb + t;
-      px[u] = *reinterpret_cast<const uint4*>(pr->indices);
-      pim[u] = *reinterpret_cast<const uint4*>(pr->impulses);
-      ppen[u] = pr->position_pen[3];
+      iq[u] = *reinterpret_cast<const uint4*>(gcb[t].impulses);
     }
 #pragma unroll
     for (uint32_t u = 0; u < kU; ++u) {
       const uint32_t t = t0 + u * nt;
       if (t >= nb * M) continue;
       const uint32_t el = t / M, i = t - el * M;
-      s_imp[i * ne + el] = im[u];
+      s_imp[i * ne + el] = __uint_as_float(iq[u].x);
       if (i < s_hdr[el]) {  // i < min(count, M)
         const uint32_t p = lookup_pair(m, ix[u]);
         if (p == fm::kNoPair) s_hdr[3 * ne + el] = 1;
         else s_meta[i * ne + el] = slot_word(m, p, i);
       }
-      if (i < s_hdr[ne + el]) {  // previous list
-        const uint32_t p = lookup_pair(m, px[u]);
-        if (p == fm::kNoPair || (!(ppen[u] < 0.0f) && (pim[u].y | pim[u].z) != 0u)) s_hdr[3 * ne + el] = 1;
+      if (i < s_hdr[ne + el]) {  // previous list: the same records unless a subset step separated it
+        uint4 px = ix[u], pq = iq[u];
+        if (s_hdr[2 * ne + el] != 0) {
+          const Contact& pr = a.prev_contacts[size_t(e0 + el) * M + i];
+          px = *reinterpret_cast<const uint4*>(pr.indices);
+          pq = *reinterpret_cast<const uint4*>(pr.impulses);
+        }
+        const uint32_t p = lookup_pair(m, px);
+        if (p == fm::kNoPair || (pq.y | pq.z) != 0u) s_hdr[3 * ne + el] = 1;
         else s_aux[i * ne + el] = uint8_t(m.pinfo(p) >> 24);
       }
     }
