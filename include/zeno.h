@@ -205,7 +205,9 @@ int zeno_world_set_task(ZenoWorldHandle world, const ZenoTaskConfig* task);
  * capsule-plane, geoms placed by unrotated offsets).  1: the reference's CPU collision
  * routines (src/collision/narrow_phase.zig:28-512, detectCollision): also sphere-capsule,
  * sphere-box, capsule-capsule, box-plane and box-box (SAT), geoms placed by their body's
- * pose.  Returns 0, or -6 for another mode. */
+ * pose.  2: as 1, plus box-capsule through the reference's GJK + EPA
+ * (src/collision/gjk.zig:152-574, which the reference runs only for meshes).  Returns 0,
+ * or -6 for another mode. */
 int zeno_world_set_narrow_phase(ZenoWorldHandle world, uint32_t mode);
 uint32_t zeno_world_get_narrow_phase(ZenoWorldHandle world);
 

@@ -166,21 +166,31 @@ extern "C" {
 float zo_atan2(float y, float x) { return zo::atan2_r(y, x); }
 
 int zo_set_narrow_mode(void* h, uint32_t mode) {
-  if (!h || mode > 1) return -6;
+  if (!h || mode > 2) return -6;
   static_cast<World*>(h)->narrow_mode = mode;
   return 0;
 }
 
 // One detectCollision call on two free-standing geoms (known-answer tests).  geom_*:
 // type, local pos xyz, size xyz; body_*: pos xyz, quat xyzw.  out: point xyz, normal
-// xyz, penetration.  Returns 1 on contact.
-int zo_narrow_cpu(const float* geom_a, const float* body_a, const float* geom_b, const float* body_b, float* out) {
+// xyz, penetration.  mode 2 adds GJK + EPA for box-capsule pairs.  Returns 1 on contact.
+int zo_narrow_cpu(const float* geom_a, const float* body_a, const float* geom_b, const float* body_b, float* out,
+                  uint32_t mode) {
   GeomRec ga{}, gb{};
   ga.type_body[0] = uint32_t(geom_a[0]), gb.type_body[0] = uint32_t(geom_b[0]);
   for (int k = 0; k < 3; ++k) ga.pos_size0[k] = geom_a[1 + k], gb.pos_size0[k] = geom_b[1 + k];
   ga.pos_size0[3] = geom_a[4], ga.params[0] = geom_a[5], ga.params[1] = geom_a[6];
   gb.pos_size0[3] = geom_b[4], gb.params[0] = geom_b[5], gb.params[1] = geom_b[6];
-  return narrow_cpu(ga, body_a, body_a + 3, gb, body_b, body_b + 3, out, out + 3, out + 6) ? 1 : 0;
+  return narrow_cpu(ga, body_a, body_a + 3, gb, body_b, body_b + 3, out, out + 3, out + 6, mode == 2) ? 1 : 0;
+}
+// gjk + epa on two free-standing shapes (same argument layout as zo_narrow_cpu).
+int zo_gjk_epa(const float* geom_a, const float* body_a, const float* geom_b, const float* body_b, float* out) {
+  GeomRec ga{}, gb{};
+  ga.type_body[0] = uint32_t(geom_a[0]), gb.type_body[0] = uint32_t(geom_b[0]);
+  for (int k = 0; k < 3; ++k) ga.pos_size0[k] = geom_a[1 + k], gb.pos_size0[k] = geom_b[1 + k];
+  ga.pos_size0[3] = geom_a[4], ga.params[0] = geom_a[5], ga.params[1] = geom_a[6];
+  gb.pos_size0[3] = geom_b[4], gb.params[0] = geom_b[5], gb.params[1] = geom_b[6];
+  return gjk_epa_query(ga, body_a, body_a + 3, gb, body_b, body_b + 3, out);
 }
 float zo_asin(float x) { return zo::asin_r(x); }
 // Generalised inverse mass of a contact or positional constraint, the expression the

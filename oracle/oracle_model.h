@@ -179,7 +179,8 @@ struct World {
   uint32_t adaptive_substeps = 1;
   Task task;
   uint64_t task_env_offset = 0;     // global index of env 0 (multi-GPU sharding)
-  uint32_t narrow_mode = 0;         // 0: reference GPU narrow phase; 1: CPU detectCollision
+  uint32_t narrow_mode = 0;         // 0: reference GPU narrow phase; 1: CPU detectCollision;
+                                    // 2: as 1, plus GJK + EPA for box-capsule pairs
   std::vector<uint32_t> episode;    // per-env reset counter (task extension RNG stream)
   std::vector<uint32_t> subtree;    // per-body subtree size (depth-first body order)
 };
@@ -193,6 +194,10 @@ void world_reset_env_noise(World* w, uint32_t e);
 // detectCollision of the reference CPU collision code for one geom pair placed by its
 // bodies' poses (oracle_narrow.cpp).
 bool narrow_cpu(const GeomRec& ga, const float* body_pos_a, const float* body_quat_a, const GeomRec& gb,
-                const float* body_pos_b, const float* body_quat_b, float point[3], float normal[3], float* pen);
+                const float* body_pos_b, const float* body_quat_b, float point[3], float normal[3], float* pen,
+                bool gjk_pairs);
+// GJK + EPA of the reference (src/collision/gjk.zig) on two free-standing shapes.
+int gjk_epa_query(const GeomRec& ga, const float* body_pos_a, const float* body_quat_a, const GeomRec& gb,
+                  const float* body_pos_b, const float* body_quat_b, float out[10]);
 
 }  // namespace zo

@@ -9,12 +9,17 @@
 //  * boxes are centred on the body origin in sphereBox / boxPlane (they use the body
 //    transform, not the geom centre), but on the geom centre in boxBox;
 //  * box-capsule pairs, plane-plane pairs and every pair with a cylinder, mesh or
-//    heightfield report no contact (no primitive routine, or outside this build's scope).
+//    heightfield report no contact (no primitive routine, or outside this build's scope);
+//  * narrow-phase mode 2 adds one extension: box-capsule pairs go through the reference's
+//    GJK + EPA (src/collision/gjk.zig, which the reference itself runs only for meshes),
+//    on the sphere / capsule / box support maps of that file, and the contact is built as
+//    meshPrimitiveCollision builds it.
 // Arithmetic follows the Zig source literally: plain IEEE-754 single-precision +, -, *,
 // / and sqrt, evaluated left to right as written (Zig's default float mode contracts
 // nothing); the oracle is compiled with -ffp-contract=off for the same reason.
 #include <cmath>
 #include <limits>
+#include <utility>
 
 #include "oracle_model.h"
 
@@ -266,12 +271,323 @@ bool box_box(P3 pa, P3 ha, const Xf& ta, P3 pb, P3 hb, const Xf& tb, Res* o) {
 
 Res flip(Res r) { return Res{r.point, scl(r.normal, -1.0f), r.pen}; }
 
+// ---- GJK + EPA (src/collision/gjk.zig) on the sphere, capsule and box support maps ----
+constexpr float kGjkTol = 1e-6f;  // GJK_TOLERANCE (gjk.zig:17)
+constexpr float kEpaTol = 1e-4f;  // EPA_TOLERANCE (gjk.zig:19)
+constexpr int kGjkIters = 64;     // GJK_MAX_ITERATIONS
+constexpr int kEpaIters = 64;     // EPA_MAX_ITERATIONS
+constexpr int kEpaFaces = 128;    // EPA_MAX_FACES
+constexpr int kEpaEdges = 256;    // horizon edge list (addEdge)
+// EPA starts from 4 vertices and adds at most one per iteration, so its 256-entry vertex
+// array never holds more than 4 + 64.
+constexpr int kEpaVerts = 4 + kEpaIters;
+
+struct Shape {  // ConvexShape: geom type 0 sphere, 1 capsule, 2 box; body transform
+  uint32_t type;
+  P3 local;  // geom local position
+  P3 size;   // size[0..2]: radius / half length, or box half extents
+  Xf xf;
+};
+
+inline P3 neg(P3 v) { return P3{-v.x, -v.y, -v.z}; }
+// safeNormalize (gjk.zig:661-665)
+inline P3 safe_normalize(P3 v) {
+  const float len = std::sqrt(dot(v, v));
+  if (len < kGjkTol) return P3{0.0f, 0.0f, 1.0f};
+  return scl(v, 1.0f / len);
+}
+inline P3 triple(P3 a, P3 b, P3 c) { return cross(cross(a, b), c); }  // tripleProduct
+// perpendicular (gjk.zig:673-679)
+inline P3 perpendicular(P3 v) {
+  if (std::fabs(v.x) < std::fabs(v.y)) return safe_normalize(cross(v, P3{1.0f, 0.0f, 0.0f}));
+  return safe_normalize(cross(v, P3{0.0f, 1.0f, 0.0f}));
+}
+
+// sphereSupport / capsuleSupport / boxSupport (gjk.zig:70-120).  The box support point is
+// taken about the body origin (transformPoint of the corner), as written.
+P3 support(const Shape& s, P3 dir) {
+  if (s.type == 0) {
+    const P3 c = s.xf.point(s.local);
+    return add(c, scl(safe_normalize(dir), s.size.x));
+  }
+  if (s.type == 1) {
+    const P3 c = s.xf.point(s.local);
+    const P3 axis = s.xf.vec(P3{0.0f, 0.0f, 1.0f});
+    const P3 n = safe_normalize(dir);
+    const float d = dot(axis, dir);
+    const P3 e = d >= 0.0f ? add(c, scl(axis, s.size.y)) : sub(c, scl(axis, s.size.y));
+    return add(e, scl(n, s.size.x));
+  }
+  const P3 ld = s.xf.inverse().vec(dir);
+  const P3 corner{ld.x >= 0.0f ? s.size.x : -s.size.x, ld.y >= 0.0f ? s.size.y : -s.size.y,
+                  ld.z >= 0.0f ? s.size.z : -s.size.z};
+  return s.xf.point(corner);
+}
+
+struct MinkPoint {
+  P3 p, sa, sb;
+};
+// minkowskiSupport (gjk.zig:137-149): support of A - B
+inline MinkPoint mink(const Shape& A, const Shape& B, P3 dir) {
+  const P3 sa = support(A, dir), sb = support(B, neg(dir));
+  return MinkPoint{sub(sa, sb), sa, sb};
+}
+
+struct Simplex {
+  P3 s[4], sa[4], sb[4];
+  uint32_t n;
+};
+
+// doSimplex2 (gjk.zig:226-253); the support points are left as they are, as written.
+void simplex2(Simplex& x, P3& dir) {
+  const P3 a = x.s[1], b = x.s[0];
+  const P3 ab = sub(b, a), ao = neg(a);
+  if (dot(ab, ao) > 0.0f) {
+    dir = triple(ab, ao, ab);
+    if (dot(dir, dir) < kGjkTol) dir = perpendicular(ab);
+  } else {
+    x.s[0] = a;
+    x.n = 1;
+    dir = ao;
+  }
+}
+
+// doSimplex3 (gjk.zig:256-339)
+void simplex3(Simplex& x, P3& dir) {
+  const P3 a = x.s[2], b = x.s[1], c = x.s[0];
+  const P3 ab = sub(b, a), ac = sub(c, a), ao = neg(a);
+  const P3 abc = cross(ab, ac);
+  if (dot(cross(ab, abc), ao) > 0.0f) {
+    if (dot(ab, ao) > 0.0f) {
+      x.s[0] = b, x.s[1] = a;
+      x.sa[0] = x.sa[1], x.sb[0] = x.sb[1];
+      x.sa[1] = x.sa[2], x.sb[1] = x.sb[2];
+      x.n = 2;
+      dir = triple(ab, ao, ab);
+      if (dot(dir, dir) < kGjkTol) dir = perpendicular(ab);
+    } else {
+      x.s[0] = a;
+      x.sa[0] = x.sa[2], x.sb[0] = x.sb[2];
+      x.n = 1;
+      dir = ao;
+    }
+    return;
+  }
+  if (dot(cross(abc, ac), ao) > 0.0f) {
+    if (dot(ac, ao) > 0.0f) {
+      x.s[0] = c, x.s[1] = a;
+      x.sa[1] = x.sa[2], x.sb[1] = x.sb[2];
+      x.n = 2;
+      dir = triple(ac, ao, ac);
+      if (dot(dir, dir) < kGjkTol) dir = perpendicular(ac);
+    } else {
+      x.s[0] = a;
+      x.sa[0] = x.sa[2], x.sb[0] = x.sb[2];
+      x.n = 1;
+      dir = ao;
+    }
+    return;
+  }
+  if (dot(abc, ao) > 0.0f) {
+    dir = abc;
+  } else {
+    std::swap(x.s[0], x.s[1]);
+    std::swap(x.sa[0], x.sa[1]);
+    std::swap(x.sb[0], x.sb[1]);
+    dir = neg(abc);
+  }
+}
+
+// doSimplex4 (gjk.zig:342-413).  The support copies run in the written order: in the ADB
+// case slot 1 receives the already overwritten slot 0 (b), as in the reference.
+bool simplex4(Simplex& x, P3& dir) {
+  const P3 a = x.s[3], b = x.s[2], c = x.s[1], d = x.s[0];
+  const P3 ab = sub(b, a), ac = sub(c, a), ad = sub(d, a), ao = neg(a);
+  const P3 abc = cross(ab, ac), acd = cross(ac, ad), adb = cross(ad, ab);
+  if (dot(abc, ao) > 0.0f) {
+    x.s[0] = c, x.s[1] = b, x.s[2] = a;
+    x.sa[0] = x.sa[1], x.sb[0] = x.sb[1];
+    x.sa[1] = x.sa[2], x.sb[1] = x.sb[2];
+    x.sa[2] = x.sa[3], x.sb[2] = x.sb[3];
+    x.n = 3;
+    dir = abc;
+    return false;
+  }
+  if (dot(acd, ao) > 0.0f) {
+    x.s[0] = d, x.s[1] = c, x.s[2] = a;
+    x.sa[2] = x.sa[3], x.sb[2] = x.sb[3];
+    x.n = 3;
+    dir = acd;
+    return false;
+  }
+  if (dot(adb, ao) > 0.0f) {
+    x.s[0] = b, x.s[1] = d, x.s[2] = a;
+    x.sa[0] = x.sa[2], x.sb[0] = x.sb[2];
+    x.sa[1] = x.sa[0], x.sb[1] = x.sb[0];
+    x.sa[2] = x.sa[3], x.sb[2] = x.sb[3];
+    x.n = 3;
+    dir = adb;
+    return false;
+  }
+  return true;
+}
+
+// gjk (gjk.zig:152-223)
+bool gjk(const Shape& A, const Shape& B, Simplex& x) {
+  P3 dir = sub(B.xf.point(B.local), A.xf.point(A.local));
+  if (dot(dir, dir) < kGjkTol) dir = P3{1.0f, 0.0f, 0.0f};
+  const MinkPoint first = mink(A, B, dir);
+  x.s[0] = first.p, x.sa[0] = first.sa, x.sb[0] = first.sb;
+  x.n = 1;
+  dir = neg(first.p);
+  for (int it = 0; it < kGjkIters; ++it) {
+    const MinkPoint m = mink(A, B, dir);
+    if (dot(m.p, dir) < -kGjkTol) return false;
+    const uint32_t i = x.n;
+    x.s[i] = m.p, x.sa[i] = m.sa, x.sb[i] = m.sb;
+    x.n += 1;
+    if (x.n == 2) simplex2(x, dir);
+    else if (x.n == 3) simplex3(x, dir);
+    else if (simplex4(x, dir)) return true;
+  }
+  return false;
+}
+
+struct Face {
+  uint32_t i0, i1, i2;
+  P3 n;
+  float d;
+};
+
+// faceNormal (gjk.zig:600-604)
+inline P3 face_normal(P3 a, P3 b, P3 c) { return safe_normalize(cross(sub(b, a), sub(c, a))); }
+
+// barycentricOriginProjection (gjk.zig:607-638)
+void barycentric(P3 a, P3 b, P3 c, float out[3]) {
+  const float third = 1.0f / 3.0f;
+  const P3 ab = sub(b, a), ac = sub(c, a), ao = neg(a);
+  const float d00 = dot(ab, ab), d01 = dot(ab, ac), d11 = dot(ac, ac), d20 = dot(ao, ab), d21 = dot(ao, ac);
+  const float denom = d00 * d11 - d01 * d01;
+  if (std::fabs(denom) < kGjkTol) {
+    out[0] = out[1] = out[2] = third;
+    return;
+  }
+  const float v = (d11 * d20 - d01 * d21) / denom;
+  const float w = (d00 * d21 - d01 * d20) / denom;
+  const float u = 1.0f - v - w;
+  const float cu = clampf(u, 0.0f, 1.0f), cv = clampf(v, 0.0f, 1.0f), cw = clampf(w, 0.0f, 1.0f);
+  const float total = cu + cv + cw;
+  if (total < kGjkTol) {
+    out[0] = out[1] = out[2] = third;
+    return;
+  }
+  out[0] = cu / total, out[1] = cv / total, out[2] = cw / total;
+}
+
+// addEdge (gjk.zig:577-597): a reversed duplicate cancels, else append while room remains.
+void add_edge(uint32_t (*edges)[2], uint32_t& ne, uint32_t a, uint32_t b) {
+  for (uint32_t i = 0; i < ne; ++i)
+    if (edges[i][0] == b && edges[i][1] == a) {
+      edges[i][0] = edges[ne - 1][0], edges[i][1] = edges[ne - 1][1];
+      ne -= 1;
+      return;
+    }
+  if (ne < uint32_t(kEpaEdges)) edges[ne][0] = a, edges[ne][1] = b, ne += 1;
+}
+
+// epa (gjk.zig:424-574): contact normal (A to B), depth and the witness points on A and B.
+bool epa(const Shape& A, const Shape& B, const Simplex& x, P3* normal, float* depth, P3* pa, P3* pb) {
+  if (x.n < 4) return false;
+  P3 v[kEpaVerts], va[kEpaVerts], vb[kEpaVerts];
+  uint32_t nv = 4;
+  for (int i = 0; i < 4; ++i) v[i] = x.s[i], va[i] = x.sa[i], vb[i] = x.sb[i];
+  Face f[kEpaFaces];
+  uint32_t nf = 0;
+  static const uint32_t tet[4][3] = {{0, 1, 2}, {0, 3, 1}, {0, 2, 3}, {1, 3, 2}};
+  for (const auto& t : tet) {
+    const P3 n = face_normal(v[t[0]], v[t[1]], v[t[2]]);
+    const float d = dot(n, v[t[0]]);
+    if (d < 0.0f) f[nf++] = Face{t[0], t[2], t[1], neg(n), -d};
+    else f[nf++] = Face{t[0], t[1], t[2], n, d};
+  }
+  auto finish = [&](uint32_t k, float dist) {
+    const Face& fc = f[k];
+    float w[3];
+    barycentric(v[fc.i0], v[fc.i1], v[fc.i2], w);
+    *pa = add(add(scl(va[fc.i0], w[0]), scl(va[fc.i1], w[1])), scl(va[fc.i2], w[2]));
+    *pb = add(add(scl(vb[fc.i0], w[0]), scl(vb[fc.i1], w[1])), scl(vb[fc.i2], w[2]));
+    *normal = fc.n;
+    *depth = dist;
+  };
+  auto closest = [&](float* dist) {
+    uint32_t k = 0;
+    float best = std::numeric_limits<float>::infinity();
+    for (uint32_t i = 0; i < nf; ++i)
+      if (f[i].d < best) best = f[i].d, k = i;
+    *dist = best;
+    return k;
+  };
+  for (int it = 0; it < kEpaIters; ++it) {
+    float cd;
+    const uint32_t k = closest(&cd);
+    const P3 dir = f[k].n;
+    const MinkPoint m = mink(A, B, dir);
+    if (dot(m.p, dir) - cd < kEpaTol) {
+      finish(k, cd);
+      return true;
+    }
+    const uint32_t ni = nv;
+    v[nv] = m.p, va[nv] = m.sa, vb[nv] = m.sb;
+    nv += 1;
+    uint32_t edges[kEpaEdges][2];
+    uint32_t ne = 0;
+    for (uint32_t i = 0; i < nf;) {
+      if (dot(f[i].n, sub(m.p, v[f[i].i0])) > 0.0f) {
+        add_edge(edges, ne, f[i].i0, f[i].i1);
+        add_edge(edges, ne, f[i].i1, f[i].i2);
+        add_edge(edges, ne, f[i].i2, f[i].i0);
+        f[i] = f[nf - 1];
+        nf -= 1;
+      } else {
+        i += 1;
+      }
+    }
+    for (uint32_t e = 0; e < ne; ++e) {
+      if (nf >= uint32_t(kEpaFaces)) break;
+      const uint32_t e0 = edges[e][0], e1 = edges[e][1];
+      const P3 n = face_normal(v[e0], v[e1], v[ni]);
+      const float d = dot(n, v[e0]);
+      if (d < 0.0f) f[nf++] = Face{e1, e0, ni, neg(n), -d};
+      else f[nf++] = Face{e0, e1, ni, n, d};
+    }
+    if (nf == 0) break;
+  }
+  if (nf == 0) return false;
+  float cd;
+  const uint32_t k = closest(&cd);
+  finish(k, cd);
+  return true;
+}
+
+// The contact the reference builds from GJK + EPA (meshPrimitiveCollision,
+// narrow_phase.zig:693-747): point = midpoint of the witness points, normal = EPA normal
+// (A to B), penetration = EPA depth.
+bool gjk_contact(const Shape& A, const Shape& B, Res* o) {
+  Simplex x{};
+  if (!gjk(A, B, x)) return false;
+  P3 n, pa, pb;
+  float depth;
+  if (!epa(A, B, x, &n, &depth, &pa, &pb)) return false;
+  *o = Res{scl(add(pa, pb), 0.5f), n, depth};
+  return true;
+}
+
 }  // namespace
 
 // detectCollision (narrow_phase.zig:28-136) for the primitive geoms.  Geom types: 0 sphere,
 // 1 capsule, 2 box, 3 plane; anything else reports no contact.
 bool narrow_cpu(const GeomRec& ga, const float* bpa, const float* bqa, const GeomRec& gb, const float* bpb,
-                const float* bqb, float point[3], float normal[3], float* pen) {
+                const float* bqb, float point[3], float normal[3], float* pen, bool gjk_pairs) {
   const Xf ta{p3(bpa), Quat{bqa[0], bqa[1], bqa[2], bqa[3]}};
   const Xf tb{p3(bpb), Quat{bqb[0], bqb[1], bqb[2], bqb[3]}};
   const P3 la = p3(ga.pos_size0), lb = p3(gb.pos_size0);
@@ -287,6 +603,9 @@ bool narrow_cpu(const GeomRec& ga, const float* bpa, const float* bqa, const Geo
     else if (kb == 1) hit = sphere_capsule(pa, ra, pb, rb, hlb, tb, &r);
     else if (kb == 2) hit = sphere_box(pa, ra, szb, tb, &r);
     else if (kb == 3) hit = sphere_plane(pa, ra, lb, rb, tb, &r);
+  } else if (gjk_pairs && ((ka == 1 && kb == 2) || (ka == 2 && kb == 1))) {
+    const Shape A{ka, la, sza, ta}, B{kb, lb, szb, tb};
+    hit = gjk_contact(A, B, &r);
   } else if (ka == 1) {
     if (kb == 0) {
       hit = sphere_capsule(pb, rb, pa, ra, hla, ta, &r);
@@ -316,6 +635,26 @@ bool narrow_cpu(const GeomRec& ga, const float* bpa, const float* bqa, const Geo
   normal[0] = r.normal.x, normal[1] = r.normal.y, normal[2] = r.normal.z;
   *pen = r.pen;
   return true;
+}
+
+// gjk then epa on two free-standing shapes (types 0 sphere, 1 capsule, 2 box), for the
+// reference's own GJK / EPA unit tests (gjk.zig:712-826).  Returns 0 when GJK finds no
+// intersection, 1 when it does but EPA gives no result, 2 with out = EPA normal xyz,
+// depth, witness point on A xyz, witness point on B xyz.
+int gjk_epa_query(const GeomRec& ga, const float* bpa, const float* bqa, const GeomRec& gb, const float* bpb,
+                  const float* bqb, float out[10]) {
+  const Xf ta{p3(bpa), Quat{bqa[0], bqa[1], bqa[2], bqa[3]}};
+  const Xf tb{p3(bpb), Quat{bqb[0], bqb[1], bqb[2], bqb[3]}};
+  const Shape A{ga.type_body[0], p3(ga.pos_size0), P3{ga.pos_size0[3], ga.params[0], ga.params[1]}, ta};
+  const Shape B{gb.type_body[0], p3(gb.pos_size0), P3{gb.pos_size0[3], gb.params[0], gb.params[1]}, tb};
+  Simplex x{};
+  if (!gjk(A, B, x)) return 0;
+  P3 n, pa, pb;
+  float depth;
+  if (!epa(A, B, x, &n, &depth, &pa, &pb)) return 1;
+  const float v[10] = {n.x, n.y, n.z, depth, pa.x, pa.y, pa.z, pb.x, pb.y, pb.z};
+  for (int i = 0; i < 10; ++i) out[i] = v[i];
+  return 2;
 }
 
 }  // namespace zo

@@ -415,16 +415,18 @@ void substep_env(World* w, uint32_t e) {
     con[j + 1] = key;
   }
 
-  // narrow_phase (all_shaders.metal:751-894); extended mode: the reference's CPU
-  // detectCollision (src/collision/narrow_phase.zig:28-136) on the same slots
+  // narrow_phase (all_shaders.metal:751-894); extended modes: the reference's CPU
+  // detectCollision (src/collision/narrow_phase.zig:28-136) on the same slots, mode 2
+  // with GJK + EPA (src/collision/gjk.zig) for box-capsule pairs
   for (uint32_t i = 0; i < n; i++) {
     ContactRec& c = con[i];
     uint32_t ba = c.indices[0], bb = c.indices[1];
     const GeomRec& gA = w->geoms[c.indices[2]];
     const GeomRec& gB = w->geoms[c.indices[3]];
-    if (w->narrow_mode == 1) {
+    if (w->narrow_mode >= 1) {
       float pt[3], nm[3], pen = 0.0f;
-      if (narrow_cpu(gA, &pos[ba * 4], &quat[ba * 4], gB, &pos[bb * 4], &quat[bb * 4], pt, nm, &pen)) {
+      if (narrow_cpu(gA, &pos[ba * 4], &quat[ba * 4], gB, &pos[bb * 4], &quat[bb * 4], pt, nm, &pen,
+                     w->narrow_mode == 2)) {
         const float fr = std::sqrt(gA.params[2] * gB.params[2]);
         st4(c.position_pen, F4{pt[0], pt[1], pt[2], pen});
         st4(c.normal_friction, F4{nm[0], nm[1], nm[2], fr});

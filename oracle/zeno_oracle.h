@@ -61,7 +61,9 @@ extern "C" {
 #endif
 float zo_atan2(float y, float x);
 int zo_set_narrow_mode(void* h, uint32_t mode);
-int zo_narrow_cpu(const float* geom_a, const float* body_a, const float* geom_b, const float* body_b, float* out);
+int zo_gjk_epa(const float* geom_a, const float* body_a, const float* geom_b, const float* body_b, float* out);
+int zo_narrow_cpu(const float* geom_a, const float* body_a, const float* geom_b, const float* body_b, float* out,
+                  uint32_t mode);
 float zo_asin(float x);
 float zo_effective_mass(float ima, float imb, const float* Ia, const float* Ib, const float* ra, const float* rb,
                         const float* n);

@@ -83,7 +83,8 @@ def lib() -> ctypes.CDLL:
         L.zo_buffer.restype = vp
         L.zo_buffer.argtypes = [vp, ctypes.c_char_p, ctypes.POINTER(ctypes.c_size_t)]
         L.zo_set_narrow_mode.argtypes = [vp, ctypes.c_uint32]
-        L.zo_narrow_cpu.argtypes = [f32p, f32p, f32p, f32p, f32p]
+        L.zo_narrow_cpu.argtypes = [f32p, f32p, f32p, f32p, f32p, ctypes.c_uint32]
+        L.zo_gjk_epa.argtypes = [f32p, f32p, f32p, f32p, f32p]
         _lib = L
     return _lib
 
@@ -186,20 +187,34 @@ class OracleWorld:
         return lib().zo_set_task(self._h, ctypes.byref(t))
 
     def set_narrow_phase(self, mode: int) -> int:
-        """0: the reference's GPU narrow phase (default); 1: its CPU detectCollision."""
+        """0: the reference's GPU narrow phase (default); 1: its CPU detectCollision; 2: as 1,
+        plus GJK + EPA for box-capsule pairs."""
         return lib().zo_set_narrow_mode(self._h, int(mode))
 
     def model_table(self, name: str) -> bytes:
         return self.raw(name, np.uint8).tobytes()
 
 
-def narrow_cpu(geom_a, body_a, geom_b, body_b):
-    """detectCollision of the restated CPU collision code for two geoms.
-    geom_*: (type, lx, ly, lz, size0, size1, size2); body_*: (px, py, pz, qx, qy, qz, qw).
-    Returns None or (point[3], normal[3], penetration)."""
+def narrow_cpu(geom_a, body_a, geom_b, body_b, mode=1):
+    """detectCollision of the restated CPU collision code for two geoms (mode 2: with GJK +
+    EPA for box-capsule pairs).  geom_*: (type, lx, ly, lz, size0, size1, size2); body_*:
+    (px, py, pz, qx, qy, qz, qw).  Returns None or (point[3], normal[3], penetration)."""
     ga, gb = (np.asarray(g, np.float32) for g in (geom_a, geom_b))
     ba, bb = (np.asarray(b, np.float32) for b in (body_a, body_b))
     out = np.zeros(7, np.float32)
-    if not lib().zo_narrow_cpu(_fptr(ga), _fptr(ba), _fptr(gb), _fptr(bb), _fptr(out)):
+    if not lib().zo_narrow_cpu(_fptr(ga), _fptr(ba), _fptr(gb), _fptr(bb), _fptr(out), int(mode)):
         return None
     return out[:3].copy(), out[3:6].copy(), float(out[6])
+
+
+def gjk_epa(geom_a, body_a, geom_b, body_b):
+    """The reference's GJK then EPA (src/collision/gjk.zig) on two shapes (types 0 sphere,
+    1 capsule, 2 box; arguments as narrow_cpu).  Returns (intersect, epa) with epa None or
+    (normal[3], depth, point_a[3], point_b[3])."""
+    ga, gb = (np.asarray(g, np.float32) for g in (geom_a, geom_b))
+    ba, bb = (np.asarray(b, np.float32) for b in (body_a, body_b))
+    out = np.zeros(10, np.float32)
+    r = lib().zo_gjk_epa(_fptr(ga), _fptr(ba), _fptr(gb), _fptr(bb), _fptr(out))
+    if r < 2:
+        return bool(r), None
+    return True, (out[:3].copy(), float(out[3]), out[4:7].copy(), out[7:10].copy())

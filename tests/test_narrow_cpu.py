@@ -1,11 +1,11 @@
 """The extended narrow phase (the reference's CPU detectCollision, restated in
 oracle/oracle_narrow.cpp) against the known answers of the reference's own tests
-(tests/test_collision.zig:55-81, 173-199, 219-232) and hand-derived contacts for the
-pairs those tests do not cover."""
+(tests/test_collision.zig:55-81, 173-199, 219-232; src/collision/gjk.zig:712-826 for GJK
+and EPA) and hand-derived contacts for the pairs those tests do not cover."""
 import numpy as np
 import pytest
 
-from oracle.zeno_oracle import OracleWorld, narrow_cpu
+from oracle.zeno_oracle import OracleWorld, gjk_epa, narrow_cpu
 from zeno_b200 import scenes
 
 I = (0, 0, 0, 0, 0, 0, 1)  # body at the origin, identity quaternion
@@ -111,3 +111,70 @@ def test_extended_mode_adds_pair_types_in_a_rollout():
             cc += int((valid & (types[ga] == 1) & (types[gb] == 1)).sum())
         seen[mode] = cc
     assert seen[0] == 0 and seen[1] > 0
+
+
+# ---- GJK + EPA (narrow-phase mode 2) ----
+
+def test_reference_gjk_sphere_sphere_overlap():  # gjk.zig:712-725
+    hit, _ = gjk_epa(sphere(1.0), I, sphere(1.0), body(1.0))
+    assert hit
+
+
+def test_reference_gjk_sphere_sphere_apart():  # gjk.zig:727-740
+    assert gjk_epa(sphere(1.0), I, sphere(1.0), body(5.0)) == (False, None)
+
+
+def test_reference_epa_sphere_sphere_depth():  # gjk.zig:742-762
+    hit, res = gjk_epa(sphere(1.0), I, sphere(1.0), body(1.0))
+    assert hit and res is not None
+    normal, depth = res[0], res[1]
+    assert abs(depth - 1.0) <= 0.1
+    assert abs(normal[0]) > 0.8
+
+
+def test_reference_gjk_box_sphere_overlap():  # gjk.zig:764-777
+    hit, _ = gjk_epa(box(1.0, 1.0, 1.0), I, sphere(0.5), body(1.2))
+    assert hit
+
+
+def test_reference_gjk_box_sphere_apart():  # gjk.zig:779-792
+    hit, _ = gjk_epa(box(1.0, 1.0, 1.0), I, sphere(0.5), body(3.0))
+    assert not hit
+
+
+S45 = float(np.sin(np.pi / 4))
+
+
+@pytest.mark.parametrize("case,expect", [
+    # box half 1 at the origin, upright capsule r .5 beside it at x = 1.3: depth .2 along x
+    ((box(1, 1, 1), I, capsule(0.5, 1.0), body(1.3)), ((0.9, 0, 0.5), (1, 0, 0), 0.2)),
+    ((capsule(0.5, 1.0), body(1.3), box(1, 1, 1), I), ((0.9, 0, 0.5), (-1, 0, 0), 0.2)),
+    # capsule lying along y (90 degrees about x) on top of the box: depth .1 along z
+    ((box(1, 1, 1), I, capsule(0.5, 0.8), body(0.2, 0, 1.4, (S45, 0, 0, S45))), ((0.2, 0, 0.95), (0, 0, 1), 0.1)),
+])
+def test_gjk_box_capsule(case, expect):
+    """Mode 2 resolves box-capsule pairs through GJK + EPA: normal from A to B, depth, and
+    the midpoint of the witness points, to EPA's tolerance (1e-4)."""
+    r = narrow_cpu(*case, mode=2)
+    assert r is not None
+    np.testing.assert_allclose(r[1], expect[1], atol=1e-4)
+    assert abs(r[2] - expect[2]) < 1e-4
+    # the contact point lies on the contact normal's line through the overlap; check the
+    # coordinate along the normal (the tangential position of EPA's witness is not unique)
+    n = np.asarray(expect[1], np.float32)
+    assert abs(float(np.dot(r[0], n)) - float(np.dot(expect[0], n))) < 1e-3
+
+
+def test_gjk_box_capsule_apart():
+    assert narrow_cpu(box(1, 1, 1), I, capsule(0.5, 1.0), body(1.6), mode=2) is None
+
+
+def test_mode2_leaves_other_pairs_as_mode1():
+    """Mode 2 changes only box-capsule pairs."""
+    cases = [(sphere(0.5), I, sphere(0.5), body(0.8)), (capsule(0.1, 0.5), body(z=0.55), PLANE, I),
+             (box(0.5, 0.5, 0.5), I, box(0.5, 0.5, 0.5), body(0.9))]
+    for c in cases:
+        r1, r2 = narrow_cpu(*c, mode=1), narrow_cpu(*c, mode=2)
+        for a, b in zip(r1, r2):
+            np.testing.assert_array_equal(a, b)
+

@@ -261,17 +261,19 @@ def test_hand_over_to_general_kernel(lanes):
     assert not diff_report(runs[0], runs[1])
 
 
-@pytest.mark.parametrize("name,lanes", [("ant", 1), ("ant", 2), ("ant", 8), ("cartpole", 1),
-                                        ("pendulum_asset", 1), ("humanoid", None)])
-def test_extended_narrow_phase_bit_exact(name, lanes):
-    """Narrow phase 1 (the reference's CPU detectCollision: sphere/capsule/box/plane pairs,
-    geoms placed by body pose) on both kernels against the oracle.  Humanoid has more
-    hittable candidates in this mode than the compressed-state kernel holds (64), so it
-    runs on the general kernel."""
+@pytest.mark.parametrize("name,lanes,mode", [("ant", 1, 1), ("ant", 2, 1), ("ant", 8, 1), ("cartpole", 1, 1),
+                                             ("pendulum_asset", 1, 1), ("humanoid", None, 1), ("ant", 1, 2),
+                                             ("humanoid", None, 2)])
+def test_extended_narrow_phase_bit_exact(name, lanes, mode):
+    """Narrow phases 1 (the reference's CPU detectCollision: sphere/capsule/box/plane pairs,
+    geoms placed by body pose) and 2 (the same plus GJK + EPA for box-capsule pairs) on
+    both kernels against the oracle.  Humanoid has more hittable candidates in these modes
+    than the compressed-state kernel holds (64), so it runs on the general kernel; Ant has
+    no box, so mode 2 keeps it on the compressed-state kernel."""
     E = 6
     w, o, c = make_pair(name, E)
-    w.set_narrow_phase(1)
-    assert o.set_narrow_phase(1) == 0
+    w.set_narrow_phase(mode)
+    assert o.set_narrow_phase(mode) == 0
     if lanes is not None:
         w.set_launch(lanes, 4)
     elif name == "humanoid":
@@ -300,6 +302,78 @@ def test_extended_narrow_phase_drop_scene():
     st = product_state(w)
     assert not diff_report(st, o.state())
     assert (st["contacts"]["position_pen"][..., 3] >= 0).sum() > 0
+
+
+BOX_CAPSULE = """<mujoco model="box_capsule">
+  <option timestep="0.005" gravity="0 0 -9.81"/>
+  <worldbody>
+    <geom type="plane" size="5 5 0.1" friction="0.8 0.005 0.0001"/>
+    <body name="crate" pos="0 0 0.1">
+      <joint type="free"/>
+      <geom type="box" size="0.3 0.3 0.1" density="500"/>
+    </body>
+    <body name="log" pos="0.05 0.02 0.24" quat="0.7071068 0.7071068 0 0">
+      <joint type="free"/>
+      <geom type="capsule" size="0.05 0.2" density="800"/>
+    </body>
+    <body name="post" pos="-0.15 0.1 0.45" quat="0.9961947 0 0.0871557 0">
+      <joint type="free"/>
+      <geom type="capsule" size="0.04 0.2" density="800"/>
+    </body>
+    <body name="crate2" pos="0.9 0 0.35" quat="0.9659258 0.2588190 0 0">
+      <joint type="free"/>
+      <geom type="box" size="0.1 0.2 0.1" density="500"/>
+    </body>
+    <body name="rod" pos="0.9 0.05 0.08" quat="0.7071068 0 0.7071068 0">
+      <joint type="free"/>
+      <geom type="capsule" size="0.06 0.25" density="800"/>
+    </body>
+  </worldbody>
+</mujoco>
+"""
+
+
+@pytest.mark.parametrize("lanes", [8, 32])
+def test_gjk_box_capsule_scene(lanes):
+    """Capsules resting on and under boxes: with narrow phase 2 the box-capsule pairs go
+    through GJK + EPA on the GPU and agree with the oracle bit for bit; mode 1 reports no
+    contact for them (no routine), mode 2 does."""
+    E = 4
+    kw = dict(num_envs=E, substeps=4, max_contacts_per_env=32)
+    w, o = ZenoWorld(mjcf_string=BOX_CAPSULE, **kw), OracleWorld(BOX_CAPSULE, **kw)
+    w.set_narrow_phase(2)
+    assert o.set_narrow_phase(2) == 0
+    w.set_launch(lanes, 1)
+    geoms = np.frombuffer(o.model_table("geoms"), np.uint32).reshape(-1, 16)
+    types = geoms[:, 0]
+    none = np.zeros((E, 0), np.float32)
+    gjk_hits = 0
+    for s in range(40):
+        w.step(none)
+        o.step(none)
+        st = product_state(w)
+        bad = diff_report(st, o.state())
+        assert not bad, f"step {s}: {bad}"
+        c = st["contacts"]
+        valid = c["position_pen"][..., 3] >= 0
+        ta, tb = types[c["indices"][..., 2]], types[c["indices"][..., 3]]
+        gjk_hits += int((valid & (((ta == 1) & (tb == 2)) | ((ta == 2) & (tb == 1)))).sum())
+    assert gjk_hits > 0
+
+
+def test_extended_narrow_phase_drop_scene_gjk():
+    """The 64-body drop scene with narrow phase 2 (box-capsule through GJK + EPA)."""
+    xml = scenes.collision_stress(0)
+    kw = dict(num_envs=2, substeps=2, max_contacts_per_env=256)
+    w, o = ZenoWorld(mjcf_string=xml, **kw), OracleWorld(xml, **kw)
+    w.set_narrow_phase(2)
+    o.set_narrow_phase(2)
+    none = np.zeros((2, 0), np.float32)
+    for s in range(20):
+        w.step(none)
+        o.step(none)
+        bad = diff_report(product_state(w), o.state())
+        assert not bad, f"step {s}: {bad}"
 
 
 def test_narrow_phase_switch_mid_run():

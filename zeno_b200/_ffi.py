@@ -420,7 +420,8 @@ class ZenoWorld:
 
     def set_narrow_phase(self, mode: int) -> None:
         """0: the reference's GPU narrow phase (default); 1: its CPU collision routines
-        (detectCollision: sphere/capsule/box/plane pairs, geoms placed by body pose)."""
+        (detectCollision: sphere/capsule/box/plane pairs, geoms placed by body pose); 2: as
+        1, plus box-capsule pairs through its GJK + EPA."""
         _check(_lib.zeno_world_set_narrow_phase(self._handle, int(mode)), "Set narrow phase")
 
     def get_narrow_phase(self) -> int:

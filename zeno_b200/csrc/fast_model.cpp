@@ -12,9 +12,10 @@
 namespace zb {
 namespace {
 // The type pairs the selected narrow phase can report a contact for: narrow_core (mode 0)
-// or narrow_cpu (mode 1), physics.cuh.
+// or narrow_cpu (modes 1 and 2; box-capsule pairs of mode 2 are rejected before this),
+// physics.cuh.
 inline bool narrow_pair_supported(uint32_t mode, uint32_t ta, uint32_t tb) {
-  if (mode == 1) {
+  if (mode >= 1) {
     if (ta > 3 || tb > 3) return false;
     if ((ta == 1 && tb == 2) || (ta == 2 && tb == 1)) return false;
     return !(ta == 3 && tb == 3);
@@ -82,6 +83,9 @@ bool pack_fast_model(const HostModel& h, uint32_t max_contacts, uint32_t narrow_
   // used, so the kernel carries the dense rank of each candidate's key.
   std::vector<uint32_t> keys(P);
   for (uint32_t p = 0; p < P; ++p) {
+    const uint32_t ta = h.geoms[h.pairs[p].ga].type, tb = h.geoms[h.pairs[p].gb].type;
+    if (narrow_mode == 2 && ((ta == 1 && tb == 2) || (ta == 2 && tb == 1)))
+      return fail("box-capsule candidates need GJK + EPA (general kernel)");
     const uint32_t ba = h.geoms[h.pairs[p].ga].body, bb = h.geoms[h.pairs[p].gb].body;
     keys[p] = (std::min(ba, bb) << 16) | std::max(ba, bb);
   }

@@ -154,13 +154,14 @@ struct Group {
 };
 
 // Narrow phase of hittable pair h on the current poses (the world's narrow-phase mode is
-// uniform across the launch).
+// uniform across the launch; models with GJK pairs, mode 2, never reach this kernel, so
+// mode 2 is mode 1 here).
 __device__ __forceinline__ bool narrow_h(const ModelS& m, uint32_t h, EnvBodies& S, V3& point, V3& normal,
                                          float& pen) {
   const uint32_t hi = m.hinfo(h);
   const float4 ga = m.hga(h), gb = m.hgb(h);
   const uint32_t ba = (hi >> 16) & 0xFFu, bb = hi >> 24;
-  if (m.f.narrow_mode == 1) {
+  if (m.f.narrow_mode >= 1) {
     const float4 sz = m.hsz(h);
     return narrow_cpu(hi & 0xFFu, (hi >> 8) & 0xFFu, ga, make_float2(sz.x, sz.y), gb, make_float2(sz.z, sz.w),
                       S.pos(ba), S.quat(ba), S.pos(bb), S.quat(bb), point, normal, pen);

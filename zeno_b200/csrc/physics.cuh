@@ -558,13 +558,288 @@ __device__ __forceinline__ bool box_box(P3 pa, P3 ha, const Xf& ta, P3 pb, P3 hb
   return true;
 }
 
+// ---- GJK + EPA (src/collision/gjk.zig) on the sphere, capsule and box support maps ----
+// Used by narrow-phase mode 2 for box-capsule pairs; the reference runs this code only for
+// meshes.  Arithmetic as in the rest of this namespace: IEEE operations in written order.
+constexpr float kGjkTol = 1e-6f;  // GJK_TOLERANCE
+constexpr float kEpaTol = 1e-4f;  // EPA_TOLERANCE
+constexpr int kGjkIters = 64, kEpaIters = 64, kEpaFaces = 128, kEpaEdges = 256;
+constexpr int kEpaVerts = 4 + kEpaIters;  // 4 start vertices + at most one per iteration
+
+struct Shape {  // ConvexShape: type 0 sphere, 1 capsule, 2 box; body transform
+  uint32_t type;
+  P3 local, size;
+  Xf xf;
+};
+__device__ __forceinline__ P3 neg(P3 v) { return P3{-v.x, -v.y, -v.z}; }
+__device__ __forceinline__ P3 safe_normalize(P3 v) {  // safeNormalize
+  const float len = __fsqrt_rn(dot(v, v));
+  if (len < kGjkTol) return P3{0.0f, 0.0f, 1.0f};
+  return scl(v, __fdiv_rn(1.0f, len));
+}
+__device__ __forceinline__ P3 triple(P3 a, P3 b, P3 c) { return cross(cross(a, b), c); }
+__device__ __forceinline__ P3 perpendicular(P3 v) {
+  if (fabsf(v.x) < fabsf(v.y)) return safe_normalize(cross(v, P3{1.0f, 0.0f, 0.0f}));
+  return safe_normalize(cross(v, P3{0.0f, 1.0f, 0.0f}));
+}
+// sphereSupport / capsuleSupport / boxSupport (box corner about the body origin, as written)
+__device__ __forceinline__ P3 support(const Shape& s, P3 dir) {
+  if (s.type == 0) return add(s.xf.point(s.local), scl(safe_normalize(dir), s.size.x));
+  if (s.type == 1) {
+    const P3 c = s.xf.point(s.local);
+    const P3 axis = s.xf.vec(P3{0.0f, 0.0f, 1.0f});
+    const P3 n = safe_normalize(dir);
+    const float d = dot(axis, dir);
+    const P3 e = d >= 0.0f ? add(c, scl(axis, s.size.y)) : sub(c, scl(axis, s.size.y));
+    return add(e, scl(n, s.size.x));
+  }
+  const P3 ld = s.xf.inverse().vec(dir);
+  const P3 corner{ld.x >= 0.0f ? s.size.x : -s.size.x, ld.y >= 0.0f ? s.size.y : -s.size.y,
+                  ld.z >= 0.0f ? s.size.z : -s.size.z};
+  return s.xf.point(corner);
+}
+struct MinkPoint {
+  P3 p, sa, sb;
+};
+__device__ __forceinline__ MinkPoint mink(const Shape& A, const Shape& B, P3 dir) {
+  const P3 sa = support(A, dir), sb = support(B, neg(dir));
+  return MinkPoint{sub(sa, sb), sa, sb};
+}
+struct Simplex {
+  P3 s[4], sa[4], sb[4];
+  uint32_t n;
+};
+// doSimplex2: support points left as they are, as written
+__device__ __forceinline__ void simplex2(Simplex& x, P3& dir) {
+  const P3 a = x.s[1], b = x.s[0];
+  const P3 ab = sub(b, a), ao = neg(a);
+  if (dot(ab, ao) > 0.0f) {
+    dir = triple(ab, ao, ab);
+    if (dot(dir, dir) < kGjkTol) dir = perpendicular(ab);
+  } else {
+    x.s[0] = a;
+    x.n = 1;
+    dir = ao;
+  }
+}
+__device__ __forceinline__ void simplex3(Simplex& x, P3& dir) {
+  const P3 a = x.s[2], b = x.s[1], c = x.s[0];
+  const P3 ab = sub(b, a), ac = sub(c, a), ao = neg(a);
+  const P3 abc = cross(ab, ac);
+  if (dot(cross(ab, abc), ao) > 0.0f) {
+    if (dot(ab, ao) > 0.0f) {
+      x.s[0] = b, x.s[1] = a;
+      x.sa[0] = x.sa[1], x.sb[0] = x.sb[1];
+      x.sa[1] = x.sa[2], x.sb[1] = x.sb[2];
+      x.n = 2;
+      dir = triple(ab, ao, ab);
+      if (dot(dir, dir) < kGjkTol) dir = perpendicular(ab);
+    } else {
+      x.s[0] = a;
+      x.sa[0] = x.sa[2], x.sb[0] = x.sb[2];
+      x.n = 1;
+      dir = ao;
+    }
+    return;
+  }
+  if (dot(cross(abc, ac), ao) > 0.0f) {
+    if (dot(ac, ao) > 0.0f) {
+      x.s[0] = c, x.s[1] = a;
+      x.sa[1] = x.sa[2], x.sb[1] = x.sb[2];
+      x.n = 2;
+      dir = triple(ac, ao, ac);
+      if (dot(dir, dir) < kGjkTol) dir = perpendicular(ac);
+    } else {
+      x.s[0] = a;
+      x.sa[0] = x.sa[2], x.sb[0] = x.sb[2];
+      x.n = 1;
+      dir = ao;
+    }
+    return;
+  }
+  if (dot(abc, ao) > 0.0f) {
+    dir = abc;
+  } else {
+    P3 t = x.s[0];
+    x.s[0] = x.s[1], x.s[1] = t;
+    t = x.sa[0], x.sa[0] = x.sa[1], x.sa[1] = t;
+    t = x.sb[0], x.sb[0] = x.sb[1], x.sb[1] = t;
+    dir = neg(abc);
+  }
+}
+// doSimplex4: support copies in the written order (the ADB case copies slot 0 after it was
+// overwritten, as in the reference)
+__device__ __forceinline__ bool simplex4(Simplex& x, P3& dir) {
+  const P3 a = x.s[3], b = x.s[2], c = x.s[1], d = x.s[0];
+  const P3 ab = sub(b, a), ac = sub(c, a), ad = sub(d, a), ao = neg(a);
+  const P3 abc = cross(ab, ac), acd = cross(ac, ad), adb = cross(ad, ab);
+  if (dot(abc, ao) > 0.0f) {
+    x.s[0] = c, x.s[1] = b, x.s[2] = a;
+    x.sa[0] = x.sa[1], x.sb[0] = x.sb[1];
+    x.sa[1] = x.sa[2], x.sb[1] = x.sb[2];
+    x.sa[2] = x.sa[3], x.sb[2] = x.sb[3];
+    x.n = 3;
+    dir = abc;
+    return false;
+  }
+  if (dot(acd, ao) > 0.0f) {
+    x.s[0] = d, x.s[1] = c, x.s[2] = a;
+    x.sa[2] = x.sa[3], x.sb[2] = x.sb[3];
+    x.n = 3;
+    dir = acd;
+    return false;
+  }
+  if (dot(adb, ao) > 0.0f) {
+    x.s[0] = b, x.s[1] = d, x.s[2] = a;
+    x.sa[0] = x.sa[2], x.sb[0] = x.sb[2];
+    x.sa[1] = x.sa[0], x.sb[1] = x.sb[0];
+    x.sa[2] = x.sa[3], x.sb[2] = x.sb[3];
+    x.n = 3;
+    dir = adb;
+    return false;
+  }
+  return true;
+}
+__device__ __forceinline__ bool gjk(const Shape& A, const Shape& B, Simplex& x) {
+  P3 dir = sub(B.xf.point(B.local), A.xf.point(A.local));
+  if (dot(dir, dir) < kGjkTol) dir = P3{1.0f, 0.0f, 0.0f};
+  const MinkPoint first = mink(A, B, dir);
+  x.s[0] = first.p, x.sa[0] = first.sa, x.sb[0] = first.sb;
+  x.n = 1;
+  dir = neg(first.p);
+  for (int it = 0; it < kGjkIters; ++it) {
+    const MinkPoint m = mink(A, B, dir);
+    if (dot(m.p, dir) < -kGjkTol) return false;
+    const uint32_t i = x.n;
+    x.s[i] = m.p, x.sa[i] = m.sa, x.sb[i] = m.sb;
+    x.n += 1;
+    if (x.n == 2) simplex2(x, dir);
+    else if (x.n == 3) simplex3(x, dir);
+    else if (simplex4(x, dir)) return true;
+  }
+  return false;
+}
+struct Face {
+  uint32_t idx;  // vertex indices i0 | i1 << 8 | i2 << 16
+  P3 n;
+  float d;
+};
+__device__ __forceinline__ uint32_t fidx(uint32_t i0, uint32_t i1, uint32_t i2) { return i0 | (i1 << 8) | (i2 << 16); }
+__device__ __forceinline__ P3 face_normal(P3 a, P3 b, P3 c) { return safe_normalize(cross(sub(b, a), sub(c, a))); }
+__device__ __forceinline__ void barycentric(P3 a, P3 b, P3 c, float& w0, float& w1, float& w2) {
+  const float third = 1.0f / 3.0f;
+  const P3 ab = sub(b, a), ac = sub(c, a), ao = neg(a);
+  const float d00 = dot(ab, ab), d01 = dot(ab, ac), d11 = dot(ac, ac), d20 = dot(ao, ab), d21 = dot(ao, ac);
+  const float denom = __fsub_rn(__fmul_rn(d00, d11), __fmul_rn(d01, d01));
+  if (fabsf(denom) < kGjkTol) {
+    w0 = w1 = w2 = third;
+    return;
+  }
+  const float v = __fdiv_rn(__fsub_rn(__fmul_rn(d11, d20), __fmul_rn(d01, d21)), denom);
+  const float w = __fdiv_rn(__fsub_rn(__fmul_rn(d00, d21), __fmul_rn(d01, d20)), denom);
+  const float u = __fsub_rn(__fsub_rn(1.0f, v), w);
+  const float cu = clampf(u, 0.0f, 1.0f), cv = clampf(v, 0.0f, 1.0f), cw = clampf(w, 0.0f, 1.0f);
+  const float total = __fadd_rn(__fadd_rn(cu, cv), cw);
+  if (total < kGjkTol) {
+    w0 = w1 = w2 = third;
+    return;
+  }
+  w0 = __fdiv_rn(cu, total), w1 = __fdiv_rn(cv, total), w2 = __fdiv_rn(cw, total);
+}
+// addEdge: a reversed duplicate cancels, else append while room remains (edge = a | b << 8)
+__device__ __forceinline__ void add_edge(uint16_t* edges, uint32_t& ne, uint32_t a, uint32_t b) {
+  const uint16_t rev = uint16_t(b | (a << 8));
+  for (uint32_t i = 0; i < ne; ++i)
+    if (edges[i] == rev) {
+      edges[i] = edges[ne - 1];
+      ne -= 1;
+      return;
+    }
+  if (ne < uint32_t(kEpaEdges)) edges[ne++] = uint16_t(a | (b << 8));
+}
+// gjk, then epa, then the contact as meshPrimitiveCollision builds it (narrow_phase.zig:
+// 693-747): midpoint of the witness points, EPA normal (A to B), EPA depth.
+static __device__ __noinline__ bool gjk_contact(const Shape& A, const Shape& B, Res& o) {
+  Simplex x;
+  if (!gjk(A, B, x)) return false;
+  if (x.n < 4) return false;
+  P3 v[kEpaVerts], va[kEpaVerts], vb[kEpaVerts];
+  Face f[kEpaFaces];
+  uint16_t edges[kEpaEdges];
+  uint32_t nv = 4, nf = 0;
+  for (int i = 0; i < 4; ++i) v[i] = x.s[i], va[i] = x.sa[i], vb[i] = x.sb[i];
+  const uint8_t tf[4][3] = {{0, 1, 2}, {0, 3, 1}, {0, 2, 3}, {1, 3, 2}};
+#pragma unroll
+  for (int t = 0; t < 4; ++t) {
+    const uint32_t i0 = tf[t][0], i1 = tf[t][1], i2 = tf[t][2];
+    const P3 n = face_normal(v[i0], v[i1], v[i2]);
+    const float d = dot(n, v[i0]);
+    if (d < 0.0f) f[nf++] = Face{fidx(i0, i2, i1), neg(n), -d};
+    else f[nf++] = Face{fidx(i0, i1, i2), n, d};
+  }
+  bool done = false;
+  uint32_t k = 0;
+  float cd = 0.0f;
+  for (int it = 0; it < kEpaIters; ++it) {
+    k = 0;
+    cd = __int_as_float(0x7f800000);
+    for (uint32_t i = 0; i < nf; ++i)
+      if (f[i].d < cd) cd = f[i].d, k = i;
+    const P3 dir = f[k].n;
+    const MinkPoint m = mink(A, B, dir);
+    if (__fsub_rn(dot(m.p, dir), cd) < kEpaTol) {
+      done = true;
+      break;
+    }
+    const uint32_t ni = nv;
+    v[nv] = m.p, va[nv] = m.sa, vb[nv] = m.sb;
+    nv += 1;
+    uint32_t ne = 0;
+    for (uint32_t i = 0; i < nf;) {
+      const uint32_t fi = f[i].idx;
+      if (dot(f[i].n, sub(m.p, v[fi & 0xFFu])) > 0.0f) {
+        add_edge(edges, ne, fi & 0xFFu, (fi >> 8) & 0xFFu);
+        add_edge(edges, ne, (fi >> 8) & 0xFFu, fi >> 16);
+        add_edge(edges, ne, fi >> 16, fi & 0xFFu);
+        f[i] = f[nf - 1];
+        nf -= 1;
+      } else {
+        i += 1;
+      }
+    }
+    for (uint32_t e = 0; e < ne; ++e) {
+      if (nf >= uint32_t(kEpaFaces)) break;
+      const uint32_t e0 = edges[e] & 0xFFu, e1 = edges[e] >> 8;
+      const P3 n = face_normal(v[e0], v[e1], v[ni]);
+      const float d = dot(n, v[e0]);
+      if (d < 0.0f) f[nf++] = Face{fidx(e1, e0, ni), neg(n), -d};
+      else f[nf++] = Face{fidx(e0, e1, ni), n, d};
+    }
+    if (nf == 0) break;
+  }
+  if (!done) {  // fallback: the closest face of the current polytope
+    if (nf == 0) return false;
+    k = 0;
+    cd = __int_as_float(0x7f800000);
+    for (uint32_t i = 0; i < nf; ++i)
+      if (f[i].d < cd) cd = f[i].d, k = i;
+  }
+  const uint32_t fi = f[k].idx, i0 = fi & 0xFFu, i1 = (fi >> 8) & 0xFFu, i2 = fi >> 16;
+  float w0, w1, w2;
+  barycentric(v[i0], v[i1], v[i2], w0, w1, w2);
+  const P3 pa = add(add(scl(va[i0], w0), scl(va[i1], w1)), scl(va[i2], w2));
+  const P3 pb = add(add(scl(vb[i0], w0), scl(vb[i1], w1)), scl(vb[i2], w2));
+  o = Res{scl(add(pa, pb), 0.5f), f[k].n, cd};
+  return true;
+}
+
 }  // namespace cpu_narrow
 
 // True for the type pairs narrow_cpu can report a contact for (types 0 sphere, 1 capsule,
-// 2 box, 3 plane; no box-capsule, no plane-plane).
-__host__ __device__ inline bool narrow_cpu_supported(uint32_t ta, uint32_t tb) {
+// 2 box, 3 plane; no plane-plane; box-capsule only with GJK + EPA, mode 2).
+__host__ __device__ inline bool narrow_cpu_supported(uint32_t ta, uint32_t tb, bool gjk_pairs = false) {
   if (ta > 3 || tb > 3) return false;
-  if ((ta == 1 && tb == 2) || (ta == 2 && tb == 1)) return false;
+  if ((ta == 1 && tb == 2) || (ta == 2 && tb == 1)) return gjk_pairs;
   return !(ta == 3 && tb == 3);
 }
 
@@ -572,7 +847,7 @@ __host__ __device__ inline bool narrow_cpu_supported(uint32_t ta, uint32_t tb) {
 // size[1], size[2]; bpa/bpb, bqa/bqb: body position and quaternion.
 __device__ __forceinline__ bool narrow_cpu(uint32_t ka, uint32_t kb, float4 la, float2 sa, float4 lb, float2 sb,
                                            float4 bpa, float4 bqa, float4 bpb, float4 bqb, V3& point, V3& normal,
-                                           float& pen) {
+                                           float& pen, bool gjk_pairs = false) {
   using namespace cpu_narrow;
   const Xf ta{P3{bpa.x, bpa.y, bpa.z}, bqa}, tb{P3{bpb.x, bpb.y, bpb.z}, bqb};
   const P3 lpa{la.x, la.y, la.z}, lpb{lb.x, lb.y, lb.z};
@@ -581,7 +856,9 @@ __device__ __forceinline__ bool narrow_cpu(uint32_t ka, uint32_t kb, float4 la, 
   const P3 sza{la.w, sa.x, sa.y}, szb{lb.w, sb.x, sb.y};
   Res r{};
   bool hit = false, flip = false;
-  if (ka == 0) {
+  if (gjk_pairs && ((ka == 1 && kb == 2) || (ka == 2 && kb == 1))) {
+    hit = gjk_contact(Shape{ka, lpa, sza, ta}, Shape{kb, lpb, szb, tb}, r);
+  } else if (ka == 0) {
     if (kb == 0) hit = sphere_sphere(pa, ra, pb, rb, r);
     else if (kb == 1) hit = sphere_capsule(pa, ra, pb, rb, sb.x, tb, r);
     else if (kb == 2) hit = sphere_box(pa, ra, szb, tb, r);

@@ -123,7 +123,8 @@ struct ArrBodies {
 };
 
 // Narrow phase for one slot (narrow_phase, all_shaders.metal:751-894; mode 1: the
-// reference's CPU detectCollision, src/collision/narrow_phase.zig:28-136)
+// reference's CPU detectCollision, src/collision/narrow_phase.zig:28-136; mode 2: as 1,
+// with GJK + EPA, src/collision/gjk.zig, for box-capsule pairs)
 __device__ __forceinline__ void narrow(uint32_t pk, const DGeom* geoms, const float4* pos, const float4* quat,
                                        uint32_t mode, float restitution, float4& cpp, float4& cnf, float4& cim) {
   const DGeom& gA = geoms[pk_ga(pk)];
@@ -134,11 +135,11 @@ __device__ __forceinline__ void narrow(uint32_t pk, const DGeom* geoms, const fl
   V3 normal{0, 0, 0}, point{0, 0, 0};
   float pen = 0.0f;
   bool hit;
-  if (mode == 1) {
+  if (mode >= 1) {
     const float2 sa = make_float2(__ldg(&gA.size12_fr_rest[0]), __ldg(&gA.size12_fr_rest[1]));
     const float2 sb = make_float2(__ldg(&gB.size12_fr_rest[0]), __ldg(&gB.size12_fr_rest[1]));
     hit = narrow_cpu(ta, tb, ga0, sa, gb0, sb, pos[pk_a(pk)], quat[pk_a(pk)], pos[pk_b(pk)], quat[pk_b(pk)], point,
-                     normal, pen);
+                     normal, pen, mode == 2);
   } else {
     const V3 pa = v3(pos[pk_a(pk)]) + v3(ga0), pb = v3(pos[pk_b(pk)]) + v3(gb0);
     const DGeom& cg = ta == 1 ? gA : gB;

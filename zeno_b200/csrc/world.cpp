@@ -415,7 +415,7 @@ int World::set_launch(int lanes, int envs_per_block) {
 // Selects the narrow phase and re-packs the compressed-state model (its hittable pairs
 // depend on it); a model that no longer fits runs on the general kernel.
 int World::set_narrow_phase(uint32_t mode) {
-  if (mode > 1) return -6;
+  if (mode > 2) return -6;
   if (mode == narrow_mode_) return 0;
   if (cudaStreamSynchronize(stream_) != cudaSuccess) return -4;
   narrow_mode_ = mode;
