@@ -242,9 +242,28 @@ int zeno_world_reset_to_state_noalloc(ZenoWorldHandle world, const float* positi
                                       const float* velocities, const float* angular_velocities,
                                       const uint8_t* env_mask);
 
+/* Model semantics (no counterpart in the reference).  ZENO_SEMANTICS_REFERENCE: the
+ * reference's loader and step, quirks included (what zeno_world_create builds).
+ * ZENO_SEMANTICS_CORRECTED: the MJCF compiler rules the reference loader skips (compiler
+ * angle units and euler sequence; parent-rotation composition of body frames; child-frame
+ * joint anchors and normalised axes; geom orientation, including fromto capsules; rotated
+ * geom inertia, diagonal kept; frame/site sensors resolved to their body), and in the
+ * step: geom offsets rotated with their body in the broad phase with whole-geom bounding
+ * radii, the contact list rebuilt every substep (the reference's counter never resets,
+ * so its list freezes with duplicate slots), each geom placed by its own world frame in
+ * the narrow phase, and every contact normal pointing from B to A as the contact solver
+ * expects.  Corrected worlds use narrow
+ * phase 2 (mode 0 is refused) and run on the general kernel. */
+#define ZENO_SEMANTICS_REFERENCE 0u
+#define ZENO_SEMANTICS_CORRECTED 1u
+ZenoWorldHandle zeno_world_create_ex(const char* mjcf_path, const ZenoConfig* config, uint32_t semantics);
+ZenoWorldHandle zeno_world_create_from_string_ex(const char* mjcf_string, const ZenoConfig* config,
+                                                 uint32_t semantics);
+
 /* Host-only model build (no GPU needed): parse MJCF text and build the model tables;
  * zeno_model_table takes the same names as zeno_world_model_table. */
 void* zeno_model_create_from_string(const char* mjcf_string);
+void* zeno_model_create_from_string_ex(const char* mjcf_string, uint32_t semantics);
 void zeno_model_destroy(void* model);
 const void* zeno_model_table(void* model, const char* name, uint64_t* nbytes);
 

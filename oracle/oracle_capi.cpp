@@ -10,10 +10,10 @@ using namespace zo;
 
 extern "C" {
 
-void* zo_create(const char* xml, const ZoConfig* c) {
-  if (!xml || !c) return nullptr;
+void* zo_create_ex(const char* xml, const ZoConfig* c, uint32_t semantics) {
+  if (!xml || !c || semantics > 1) return nullptr;
   Scene sc;
-  if (!parse_mjcf(std::string(xml), &sc)) return nullptr;
+  if (!parse_mjcf(std::string(xml), &sc, semantics == 1)) return nullptr;
   Config cfg;
   cfg.num_envs = c->num_envs;
   cfg.timestep = c->timestep;
@@ -29,6 +29,8 @@ void* zo_create(const char* xml, const ZoConfig* c) {
   }
   return w;
 }
+
+void* zo_create(const char* xml, const ZoConfig* c) { return zo_create_ex(xml, c, 0); }
 
 void zo_destroy(void* h) { delete static_cast<World*>(h); }
 
@@ -166,7 +168,7 @@ extern "C" {
 float zo_atan2(float y, float x) { return zo::atan2_r(y, x); }
 
 int zo_set_narrow_mode(void* h, uint32_t mode) {
-  if (!h || mode > 2) return -6;
+  if (!h || mode > 2 || (static_cast<World*>(h)->scene.corrected && mode == 0)) return -6;
   static_cast<World*>(h)->narrow_mode = mode;
   return 0;
 }

@@ -193,6 +193,8 @@ struct MGeom {
   float size[3] = {0.05f, 0, 0};
   bool has_fromto = false;
   float fromto[6] = {0, 0, 0, 0, 0, 0};
+  bool has_euler = false;  // corrected loader only
+  float euler[3] = {0, 0, 0};
   bool has_mass = false;
   float mass = 0;
   float density = 1000;
@@ -216,6 +218,7 @@ struct MBody {
   std::vector<MJoint> joints;
   std::vector<MGeom> geoms;
   std::vector<MBody> children;
+  std::vector<std::string> sites;  // corrected loader only
 };
 struct MActuator {
   std::string joint;
@@ -229,6 +232,7 @@ enum MSensType { SJointPos, SJointVel, SAccel, SGyro, STouch, SForce, STorque, S
 struct MSensor {
   MSensType type = SJointPos;
   std::string joint;
+  std::string objtype, objname, site;  // corrected loader only
   float noise = 0;
 };
 struct MDefault {
@@ -238,6 +242,8 @@ struct MDefault {
 struct MModel {
   float timestep = 0.002f;
   float gravity[3] = {0, 0, -9.81f};
+  bool degree = true;            // <compiler angle> (corrected loader only)
+  std::string eulerseq = "xyz";  // <compiler eulerseq> (corrected loader only)
   std::map<std::string, MDefault> defaults;
   MBody world;
   std::vector<MActuator> actuators;
@@ -320,6 +326,7 @@ void apply_geom_attrs(MGeom* g, const std::string& a) {
   if (get_attr(a, "contype", &v) && parse_u32(v, &u)) g->contype = u;
   if (get_attr(a, "conaffinity", &v) && parse_u32(v, &u)) g->conaffinity = u;
   if (get_attr(a, "mesh", &v)) g->type = GMesh;
+  if (get_attr(a, "euler", &v)) g->has_euler = parse_vecn(v, 3, g->euler);
 }
 
 MJoint joint_with_defaults(const std::string& a, const MModel& m, const std::string& cls) {
@@ -366,6 +373,8 @@ void parse_body_content(Tokenizer& tk, MModel& m, MBody* body, const std::string
       body->joints.push_back(joint_with_defaults(t.attrs, m, cls));
     } else if (t.name == "geom") {
       body->geoms.push_back(geom_with_defaults(t.attrs, m, cls));
+    } else if (t.name == "site") {
+      body->sites.push_back(get_attr(t.attrs, "name", &v) ? v : std::string());
     } else if (t.name == "inertial") {
       MInertial in;
       float f;
@@ -433,6 +442,9 @@ void parse_sensors(Tokenizer& tk, MModel& m) {
     if (!sensor_type_from(t.name, &s.type)) s.type = SJointPos;
     std::string v;
     if (get_attr(t.attrs, "joint", &v)) s.joint = v;
+    if (get_attr(t.attrs, "objtype", &v)) s.objtype = v;
+    if (get_attr(t.attrs, "objname", &v)) s.objname = v;
+    if (get_attr(t.attrs, "site", &v)) s.site = v;
     float f;
     if (get_attr(t.attrs, "noise", &v)) s.noise = parse_float(v, &f) ? f : 0.0f;
     m.sensors.push_back(s);
@@ -466,6 +478,9 @@ void parse_mujoco(Tokenizer& tk, MModel& m) {
         m.gravity[1] = 0;
         m.gravity[2] = -9.81f;
       }
+    } else if (t.name == "compiler") {
+      if (get_attr(t.attrs, "angle", &v)) m.degree = !(v == "radian");
+      if (get_attr(t.attrs, "eulerseq", &v) && v.size() == 3) m.eulerseq = v;
     } else if (t.name == "default") {
       parse_defaults(tk, m);
     } else if (t.name == "asset") {
@@ -748,6 +763,196 @@ void process_body(Scene* sc, const MBody& mb, int32_t parent_id, const float ppo
   }
 }
 
+// ----- corrected semantics (not the reference's behaviour) -----
+// The MJCF compiler rules of MuJoCo's documentation that the reference loader skips:
+// angle units (<compiler angle>, default degree) for hinge/ball ranges and euler angles;
+// euler sequences (<compiler eulerseq>, default "xyz", lower case = moving axes); body
+// frames composed with the parent's rotation; joint pos/axis given in the child frame
+// (moved into the parent frame, where the constraints read them; axes normalised); geom
+// orientation (quat, euler, fromto segment for capsules and cylinders) and fromto centres;
+// body inertia from rotated geom inertia (the diagonal is kept); frame/site sensors
+// resolved to their body; automatic sensors on the world's first child.  Plain IEEE
+// single precision in written order.
+constexpr float kDegF = 0.017453292519943295f;  // pi / 180
+
+struct Qt {
+  float x, y, z, w;
+};
+Qt qt_mul(Qt a, Qt b) {  // quatMultiply (body.zig:238-245)
+  Qt r;
+  r.x = a.w * b.x + a.x * b.w + a.y * b.z - a.z * b.y;
+  r.y = a.w * b.y - a.x * b.z + a.y * b.w + a.z * b.x;
+  r.z = a.w * b.z + a.x * b.y - a.y * b.x + a.z * b.w;
+  r.w = a.w * b.w - a.x * b.x - a.y * b.y - a.z * b.z;
+  return r;
+}
+void qt_rot(const float v[3], Qt q, float o[3]) {  // rotateByQuat (body.zig:254-264)
+  float uv[3] = {q.y * v[2] - q.z * v[1], q.z * v[0] - q.x * v[2], q.x * v[1] - q.y * v[0]};
+  float uuv[3] = {q.y * uv[2] - q.z * uv[1], q.z * uv[0] - q.x * uv[2], q.x * uv[1] - q.y * uv[0]};
+  for (int k = 0; k < 3; k++) o[k] = v[k] + 2.0f * (q.w * uv[k] + uuv[k]);
+}
+Qt qt_unit(Qt q) {
+  float n = std::sqrt(q.x * q.x + q.y * q.y + q.z * q.z + q.w * q.w);
+  if (!(n > 0.0f)) return Qt{0, 0, 0, 1};
+  return Qt{q.x / n, q.y / n, q.z / n, q.w / n};
+}
+Qt qt_from_wxyz(const float* q) { return Qt{q[1], q[2], q[3], q[0]}; }
+Qt euler_rotation(const float e[3], bool degree, const std::string& seq) {
+  Qt q{0, 0, 0, 1};
+  for (int i = 0; i < 3; i++) {
+    char c = seq[size_t(i)];
+    int axis = (c | 0x20) - 'x';
+    if (axis < 0 || axis > 2) continue;
+    float ang = degree ? e[i] * kDegF : e[i];
+    float half = ang * 0.5f;
+    Qt r{0, 0, 0, std::cos(half)};
+    float s = std::sin(half);
+    if (axis == 0) r.x = s;
+    else if (axis == 1) r.y = s;
+    else r.z = s;
+    bool moving_axes = c >= 'a';
+    q = moving_axes ? qt_mul(q, r) : qt_mul(r, q);
+  }
+  return q;
+}
+Qt z_to_dir(const float d[3]) {  // shortest arc from local +z onto d
+  float len = std::sqrt(d[0] * d[0] + d[1] * d[1] + d[2] * d[2]);
+  if (!(len > 1e-12f)) return Qt{0, 0, 0, 1};
+  float ux = d[0] / len, uy = d[1] / len, uz = d[2] / len;
+  if (uz < -1.0f + 1e-6f) return Qt{1, 0, 0, 0};
+  return qt_unit(Qt{-uy, ux, 0.0f, 1.0f + uz});
+}
+bool oriented_by_fromto(const MGeom& g) { return g.has_fromto && (g.type == GCapsule || g.type == GCylinder); }
+Qt geom_local_quat(const MGeom& g, const MModel& m) {
+  if (oriented_by_fromto(g)) {
+    float d[3] = {g.fromto[3] - g.fromto[0], g.fromto[4] - g.fromto[1], g.fromto[5] - g.fromto[2]};
+    return z_to_dir(d);
+  }
+  if (g.has_euler) return euler_rotation(g.euler, m.degree, m.eulerseq);
+  return qt_unit(qt_from_wxyz(g.quat));
+}
+void geom_local_centre(const MGeom& g, float c[3]) {
+  for (int k = 0; k < 3; k++) c[k] = oriented_by_fromto(g) ? (g.fromto[k] + g.fromto[k + 3]) * 0.5f : g.pos[k];
+}
+
+GeomDef convert_geom_corrected(const MGeom& mg, const MModel& m) {
+  GeomDef g = convert_geom(mg);
+  geom_local_centre(mg, g.pos);
+  if (mg.type == GCylinder && mg.has_fromto) {
+    const float* f = mg.fromto;
+    float dx = f[3] - f[0], dy = f[4] - f[1], dz = f[5] - f[2];
+    g.size[1] = std::sqrt(dx * dx + dy * dy + dz * dz) * 0.5f;
+  }
+  Qt q = geom_local_quat(mg, m);
+  g.quat[0] = q.x;
+  g.quat[1] = q.y;
+  g.quat[2] = q.z;
+  g.quat[3] = q.w;
+  return g;
+}
+
+void body_mass_inertia_corrected(const MBody& b, const MModel& m, float* mass, float inertia[3], float com[3]) {
+  if (b.has_inertial || b.geoms.empty()) {
+    body_mass_inertia(b, mass, inertia, com);
+    return;
+  }
+  float tm = 0, ti[3] = {0, 0, 0}, c[3] = {0, 0, 0};
+  for (const MGeom& g : b.geoms) {
+    float gm = geom_mass(g);
+    float gi[3] = {0, 0, 0};
+    geom_inertia(g, gm, gi);
+    Qt q = geom_local_quat(g, m);
+    const float ex[3] = {1, 0, 0}, ey[3] = {0, 1, 0}, ez[3] = {0, 0, 1};
+    float rx[3], ry[3], rz[3];  // rotated geom axes = columns of the rotation
+    qt_rot(ex, q, rx);
+    qt_rot(ey, q, ry);
+    qt_rot(ez, q, rz);
+    float d[3];
+    geom_local_centre(g, d);
+    float dsq[3] = {d[0] * d[0], d[1] * d[1], d[2] * d[2]};
+    for (int k = 0; k < 3; k++) {
+      float diag = rx[k] * rx[k] * gi[0] + ry[k] * ry[k] * gi[1] + rz[k] * rz[k] * gi[2];
+      float perp = k == 0 ? dsq[1] + dsq[2] : (k == 1 ? dsq[0] + dsq[2] : dsq[0] + dsq[1]);
+      ti[k] += diag + gm * perp;
+    }
+    for (int k = 0; k < 3; k++) c[k] += gm * d[k];
+    tm += gm;
+  }
+  if (tm <= 0) tm = 1.0f;
+  *mass = tm;
+  std::memcpy(inertia, ti, 12);
+  for (int k = 0; k < 3; k++) com[k] = c[k] / tm;
+}
+
+void process_body_corrected(Scene* sc, const MBody& mb, int32_t parent_id, const float ppos[3], Qt pq,
+                            const MModel& m, std::map<std::string, uint32_t>* site_body) {
+  for (const MBody& ch : mb.children) {
+    Qt ql = ch.has_euler ? euler_rotation(ch.euler, m.degree, m.eulerseq) : qt_unit(qt_from_wxyz(ch.quat));
+    float off[3];
+    qt_rot(ch.pos, pq, off);
+    float pos[3] = {ppos[0] + off[0], ppos[1] + off[1], ppos[2] + off[2]};
+    Qt qw = qt_mul(pq, ql);
+    BodyDef bd;
+    bd.name = ch.name;
+    bd.parent = parent_id;
+    bd.type = kDynamic;
+    std::memcpy(bd.pos, pos, 12);
+    bd.quat[0] = qw.x;
+    bd.quat[1] = qw.y;
+    bd.quat[2] = qw.z;
+    bd.quat[3] = qw.w;
+    body_mass_inertia_corrected(ch, m, &bd.mass, bd.inertia, bd.com);
+    uint32_t bid = uint32_t(sc->bodies.size());
+    sc->bodies.push_back(bd);
+    if (!ch.name.empty()) sc->body_names[ch.name] = bid;
+    if (ch.joints.empty() && parent_id >= 0) {
+      JointDef jd;
+      jd.type = kFixed;
+      jd.parent = uint32_t(parent_id);
+      jd.child = bid;
+      std::memcpy(jd.anchor_parent, ch.pos, 12);
+      sc->joints.push_back(jd);
+    }
+    for (const MJoint& mj : ch.joints) {
+      JointDef jd;
+      jd.name = mj.name;
+      jd.parent = parent_id >= 0 ? uint32_t(parent_id) : 0u;
+      jd.child = bid;
+      float jp[3], ax[3];
+      qt_rot(mj.pos, ql, jp);
+      qt_rot(mj.axis, ql, ax);
+      float n = std::sqrt(ax[0] * ax[0] + ax[1] * ax[1] + ax[2] * ax[2]);
+      for (int k = 0; k < 3; k++) {
+        jd.anchor_parent[k] = ch.pos[k] + jp[k];
+        jd.anchor_child[k] = mj.pos[k];
+        jd.axis[k] = n > 0.0f ? ax[k] / n : mj.axis[k];
+      }
+      jd.damping = mj.damping;
+      jd.stiffness = mj.stiffness;
+      jd.armature = mj.armature;
+      jd.ref = mj.ref;
+      jd.type = mj.type == JFree ? kFree : mj.type == JBall ? kBall : mj.type == JSlide ? kPrismatic : kRevolute;
+      if (mj.has_range) {
+        bool angular = mj.type == JHinge || mj.type == JBall;
+        jd.lower = (angular && m.degree) ? mj.range[0] * kDegF : mj.range[0];
+        jd.upper = (angular && m.degree) ? mj.range[1] * kDegF : mj.range[1];
+        jd.limited = true;
+      }
+      uint32_t jid = uint32_t(sc->joints.size());
+      sc->joints.push_back(jd);
+      if (!mj.name.empty()) sc->joint_names[mj.name] = jid;
+    }
+    for (const MGeom& mg : ch.geoms) {
+      GeomDef g = convert_geom_corrected(mg, m);
+      g.body = bid;
+      sc->geoms.push_back(g);
+    }
+    for (const std::string& s : ch.sites)
+      if (!s.empty()) site_body->emplace(s, bid);
+    process_body_corrected(sc, ch, int32_t(bid), pos, qw, m, site_body);
+  }
+}
+
 }  // namespace
 
 float BodyDef::inv_mass() const {
@@ -762,7 +967,7 @@ void BodyDef::inv_inertia(float o[3]) const {
   for (int i = 0; i < 3; i++) o[i] = inertia[i] > 1e-6f ? 1.0f / inertia[i] : 0.0f;
 }
 
-bool parse_mjcf(const std::string& xml, Scene* sc) {
+bool parse_mjcf(const std::string& xml, Scene* sc, bool corrected) {
   MModel m;
   Tokenizer tk(xml);
   Token t;
@@ -773,6 +978,7 @@ bool parse_mjcf(const std::string& xml, Scene* sc) {
     }
   }
   *sc = Scene{};
+  sc->corrected = corrected;
   sc->timestep = m.timestep;
   std::memcpy(sc->gravity, m.gravity, 12);
   BodyDef world;
@@ -780,13 +986,20 @@ bool parse_mjcf(const std::string& xml, Scene* sc) {
   world.type = kStatic;
   sc->bodies.push_back(world);
   sc->body_names["world"] = 0;
+  std::map<std::string, uint32_t> site_body;
   for (const MGeom& mg : m.world.geoms) {
-    GeomDef g = convert_geom(mg);
+    GeomDef g = corrected ? convert_geom_corrected(mg, m) : convert_geom(mg);
     g.body = 0;
     sc->geoms.push_back(g);
   }
   float zero[3] = {0, 0, 0};
-  process_body(sc, m.world, 0, zero);
+  if (corrected) {
+    for (const std::string& s : m.world.sites)
+      if (!s.empty()) site_body.emplace(s, 0u);
+    process_body_corrected(sc, m.world, 0, zero, Qt{0, 0, 0, 1}, m, &site_body);
+  } else {
+    process_body(sc, m.world, 0, zero);
+  }
   for (const MActuator& ma : m.actuators) {
     auto it = sc->joint_names.find(ma.joint);
     if (ma.joint.empty() || it == sc->joint_names.end()) continue;
@@ -812,6 +1025,21 @@ bool parse_mjcf(const std::string& xml, Scene* sc) {
       auto it = sc->joint_names.find(ms.joint);
       return (ms.joint.empty() || it == sc->joint_names.end()) ? 0u : it->second;
     };
+    // corrected: non-joint sensors observe the body named by objname (objtype body /
+    // xbody), else the body holding the site
+    auto body_id = [&]() -> uint32_t {
+      if (!corrected) return 0u;
+      bool body_obj = ms.objtype.empty() || ms.objtype == "body" || ms.objtype == "xbody";
+      if (body_obj && !ms.objname.empty()) {
+        for (uint32_t i = 0; i < sc->bodies.size(); i++)
+          if (sc->bodies[i].name == ms.objname) return i;
+        return 0u;
+      }
+      const std::string& site = ms.objtype == "site" ? ms.objname : ms.site;
+      auto it = site.empty() ? site_body.end() : site_body.find(site);
+      return it == site_body.end() ? 0u : it->second;
+    };
+    s.object = body_id();
     switch (ms.type) {
       case SJointPos: s.type = kJointPos; s.object = joint_id(); s.dim = 1; break;
       case SJointVel: s.type = kJointVel; s.object = joint_id(); s.dim = 1; break;
@@ -831,7 +1059,7 @@ bool parse_mjcf(const std::string& xml, Scene* sc) {
   if (sc->sensors.empty()) {  // scene.zig:211-226 autoAddSensors -> sensors.zig:191-207
     uint32_t root = 0;
     for (size_t i = 0; i < sc->bodies.size(); i++) {
-      if (sc->bodies[i].type == kDynamic && sc->bodies[i].parent < 0) {
+      if (sc->bodies[i].type == kDynamic && (corrected ? sc->bodies[i].parent == 0 : sc->bodies[i].parent < 0)) {
         root = uint32_t(i);
         break;
       }

@@ -90,6 +90,7 @@ struct Scene {
   float timestep = 0.002f;
   float gravity[3] = {0, 0, -9.81f};
   float friction = 1.0f, restitution = 0.0f, baumgarte = 0.2f, slop = 0.005f;  // constants.zig
+  bool corrected = false;  // loaded with corrected semantics
   uint32_t obs_dim() const {
     uint32_t d = 0;
     for (auto& s : sensors) d += s.dim;
@@ -99,7 +100,8 @@ struct Scene {
 
 // Parse MJCF text (parser.zig semantics).  Returns false on failure (file errors only;
 // the reference parser accepts almost any text).
-bool parse_mjcf(const std::string& xml, Scene* out);
+// corrected = true applies the MJCF compiler rules the reference skips (oracle_mjcf.cpp).
+bool parse_mjcf(const std::string& xml, Scene* out, bool corrected = false);
 
 // ----- GPU-layout records -----
 struct BodyRec { float position[4], quaternion[4], inv_mass_inertia[4], params[4], com_offset[4]; };
@@ -196,6 +198,9 @@ void world_reset_env_noise(World* w, uint32_t e);
 bool narrow_cpu(const GeomRec& ga, const float* body_pos_a, const float* body_quat_a, const GeomRec& gb,
                 const float* body_pos_b, const float* body_quat_b, float point[3], float normal[3], float* pen,
                 bool gjk_pairs);
+// Corrected semantics helpers (oracle_narrow.cpp).
+void geom_world_pose(const GeomRec& g, const float* body_pos, const float* body_quat, float wp[3], float wq[4]);
+bool normal_a_to_b(uint32_t ta, uint32_t tb);
 // GJK + EPA of the reference (src/collision/gjk.zig) on two free-standing shapes.
 int gjk_epa_query(const GeomRec& ga, const float* body_pos_a, const float* body_quat_a, const GeomRec& gb,
                   const float* body_pos_b, const float* body_quat_b, float out[10]);

@@ -637,6 +637,27 @@ bool narrow_cpu(const GeomRec& ga, const float* bpa, const float* bqa, const Geo
   return true;
 }
 
+// Corrected semantics: a geom's world frame, body pose (x) geom local pose: centre =
+// transformPoint(local position), orientation = quatMultiply(body quat, geom quat), both
+// in written order with plain IEEE operations.
+void geom_world_pose(const GeomRec& g, const float* bp, const float* bq, float wp[3], float wq[4]) {
+  const Xf t{p3(bp), Quat{bq[0], bq[1], bq[2], bq[3]}};
+  const P3 c = t.point(p3(g.pos_size0));
+  wp[0] = c.x, wp[1] = c.y, wp[2] = c.z;
+  const float* b = g.quat;
+  wq[0] = bq[3] * b[0] + bq[0] * b[3] + bq[1] * b[2] - bq[2] * b[1];
+  wq[1] = bq[3] * b[1] - bq[0] * b[2] + bq[1] * b[3] + bq[2] * b[0];
+  wq[2] = bq[3] * b[2] + bq[0] * b[1] - bq[1] * b[0] + bq[2] * b[3];
+  wq[3] = bq[3] * b[3] - bq[0] * b[0] - bq[1] * b[1] - bq[2] * b[2];
+}
+
+// The type pairs whose routines return the normal from A to B (sphere-sphere,
+// capsule-capsule, box-box; GJK's box-capsule).  The others, and all plane pairs, return
+// it from B to A, the direction solve_contacts pushes body A along.
+bool normal_a_to_b(uint32_t ta, uint32_t tb) {
+  return (ta == tb && ta <= 2) || (ta == 1 && tb == 2) || (ta == 2 && tb == 1);
+}
+
 // gjk then epa on two free-standing shapes (types 0 sphere, 1 capsule, 2 box), for the
 // reference's own GJK / EPA unit tests (gjk.zig:712-826).  Returns 0 when GJK finds no
 // intersection, 1 when it does but EPA gives no result, 2 with out = EPA normal xyz,

@@ -369,11 +369,32 @@ void substep_env(World* w, uint32_t e) {
   // the reference (world.zig:534), whose pair set for non-plane pairs is the subset of
   // this one within the 27-cell neighbourhood; the oracle only restates the O(n^2) path.
   uint32_t& count = w->counts[e];
+  // corrected semantics: geom offsets rotate with the body; bounding radius of the whole
+  // geom (sphere r, capsule r + half length, box |half extents|, cylinder
+  // sqrt(r^2 + half length^2))
+  const bool corr = w->scene.corrected;
+  if (corr) count = 0;  // corrected: the list is rebuilt every substep
+  auto centre = [&](const GeomRec& g, uint32_t b) -> F3 {
+    if (!corr) return add(ld3(&pos[b * 4]), ld3(g.pos_size0));
+    float wp[3], wq[4];
+    geom_world_pose(g, &pos[b * 4], &quat[b * 4], wp, wq);
+    return F3{wp[0], wp[1], wp[2]};
+  };
+  auto bound = [&](const GeomRec& g) -> float {
+    const float s0 = g.pos_size0[3], s1 = g.params[0], s2 = g.params[1];
+    if (!corr) return s0;
+    switch (g.type_body[0]) {
+      case 1: return s0 + s1;
+      case 2: return std::sqrt(s0 * s0 + s1 * s1 + s2 * s2);
+      case 4: return std::sqrt(s0 * s0 + s1 * s1);
+      default: return s0;
+    }
+  };
   for (uint32_t ga = 0; ga < G; ga++) {
     const GeomRec& A_ = w->geoms[ga];
     uint32_t ba = A_.type_body[1];
-    F3 pa = add(ld3(&pos[ba * 4]), ld3(A_.pos_size0));
-    float ra = A_.pos_size0[3];
+    F3 pa = centre(A_, ba);
+    float ra = bound(A_);
     uint32_t ta = A_.type_body[0], grp_a = A_.type_body[3], msk_a = A_.type_body[2];
     for (uint32_t gb = ga + 1; gb < G; gb++) {
       const GeomRec& B_ = w->geoms[gb];
@@ -381,8 +402,8 @@ void substep_env(World* w, uint32_t e) {
       if (ba == bb) continue;
       uint32_t tb = B_.type_body[0], grp_b = B_.type_body[3], msk_b = B_.type_body[2];
       if ((grp_a & msk_b) == 0 && (grp_b & msk_a) == 0) continue;
-      F3 pb = add(ld3(&pos[bb * 4]), ld3(B_.pos_size0));
-      float rb = B_.pos_size0[3];
+      F3 pb = centre(B_, bb);
+      float rb = bound(B_);
       bool plane = ta == 3 || tb == 3;
       if (!plane) {
         F3 d = sub(pb, pa);
@@ -425,8 +446,21 @@ void substep_env(World* w, uint32_t e) {
     const GeomRec& gB = w->geoms[c.indices[3]];
     if (w->narrow_mode >= 1) {
       float pt[3], nm[3], pen = 0.0f;
-      if (narrow_cpu(gA, &pos[ba * 4], &quat[ba * 4], gB, &pos[bb * 4], &quat[bb * 4], pt, nm, &pen,
-                     w->narrow_mode == 2)) {
+      bool hit;
+      if (corr) {  // each geom placed by its own world frame; normals from B to A
+        GeomRec ca = gA, cb = gB;
+        float wpa[3], wqa[4], wpb[3], wqb[4];
+        geom_world_pose(gA, &pos[ba * 4], &quat[ba * 4], wpa, wqa);
+        geom_world_pose(gB, &pos[bb * 4], &quat[bb * 4], wpb, wqb);
+        ca.pos_size0[0] = ca.pos_size0[1] = ca.pos_size0[2] = 0.0f;
+        cb.pos_size0[0] = cb.pos_size0[1] = cb.pos_size0[2] = 0.0f;
+        hit = narrow_cpu(ca, wpa, wqa, cb, wpb, wqb, pt, nm, &pen, w->narrow_mode == 2);
+        if (hit && normal_a_to_b(gA.type_body[0], gB.type_body[0])) nm[0] = -nm[0], nm[1] = -nm[1], nm[2] = -nm[2];
+      } else {
+        hit = narrow_cpu(gA, &pos[ba * 4], &quat[ba * 4], gB, &pos[bb * 4], &quat[bb * 4], pt, nm, &pen,
+                         w->narrow_mode == 2);
+      }
+      if (hit) {
         const float fr = std::sqrt(gA.params[2] * gB.params[2]);
         st4(c.position_pen, F4{pt[0], pt[1], pt[2], pen});
         st4(c.normal_friction, F4{nm[0], nm[1], nm[2], fr});
@@ -908,6 +942,7 @@ void substep_env(World* w, uint32_t e) {
 bool world_init(World* w, const Scene& scene, const Config& cfg) {
   w->scene = scene;
   w->cfg = cfg;
+  w->narrow_mode = scene.corrected ? 2u : 0u;  // corrected semantics: CPU routines + GJK
   w->timestep = cfg.timestep > 0 ? cfg.timestep : scene.timestep;  // main.zig:153
   const uint32_t E = cfg.num_envs;
   w->E = E;

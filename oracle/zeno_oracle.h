@@ -30,6 +30,8 @@ typedef struct {
 } ZoTask;
 
 void* zo_create(const char* mjcf_xml, const ZoConfig* cfg);
+/* semantics 0: the reference; 1: corrected (MJCF compiler rules, geom frames, B->A normals) */
+void* zo_create_ex(const char* mjcf_xml, const ZoConfig* cfg, uint32_t semantics);
 void zo_destroy(void* h);
 int zo_step(void* h, const float* actions, uint32_t substeps);
 int zo_step_subset(void* h, const float* actions, const uint8_t* mask, uint32_t substeps);

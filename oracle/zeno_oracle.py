@@ -69,6 +69,8 @@ def lib() -> ctypes.CDLL:
         vp, f32p, u8p = ctypes.c_void_p, ctypes.POINTER(ctypes.c_float), ctypes.POINTER(ctypes.c_uint8)
         L.zo_create.restype = vp
         L.zo_create.argtypes = [ctypes.c_char_p, ctypes.POINTER(ZoConfig)]
+        L.zo_create_ex.restype = vp
+        L.zo_create_ex.argtypes = [ctypes.c_char_p, ctypes.POINTER(ZoConfig), ctypes.c_uint32]
         L.zo_destroy.argtypes = [vp]
         L.zo_step.argtypes = [vp, f32p, ctypes.c_uint32]
         L.zo_run.argtypes = [vp, f32p, ctypes.c_uint32, ctypes.c_uint32]
@@ -106,10 +108,11 @@ class OracleWorld:
     """A world stepped by the CPU oracle; buffers are numpy views into oracle memory."""
 
     def __init__(self, xml: str, num_envs=1, timestep=0.0, contact_iterations=4,
-                 max_contacts_per_env=64, seed=42, substeps=1):
+                 max_contacts_per_env=64, seed=42, substeps=1, semantics="reference"):
         cfg = ZoConfig(num_envs, timestep, contact_iterations, max_contacts_per_env, seed, substeps,
                        False, 0, 0, 0)
-        self._h = lib().zo_create(xml.encode(), ctypes.byref(cfg))
+        sem = {"reference": 0, "corrected": 1}[semantics]
+        self._h = lib().zo_create_ex(xml.encode(), ctypes.byref(cfg), sem)
         if not self._h:
             raise RuntimeError("oracle world creation failed")
         d = (ctypes.c_uint32 * 10)()

@@ -21,12 +21,12 @@ FIELDS = ["positions", "quaternions", "velocities", "angular_velocities", "accel
           "joint_velocities", "joint_torques", "observations", "rewards", "dones", "contacts", "contact_counts"]
 
 
-def make_pair(name: str, num_envs: int, **over):
+def make_pair(name: str, num_envs: int, semantics: str = "reference", **over):
     c = dict(CONFIGS[name])
     c.update(over)
     xml = c["xml"]() if callable(c["xml"]) else c["xml"]
     kw = dict(num_envs=num_envs, timestep=c.get("timestep", 0.0), contact_iterations=c["iters"],
-              max_contacts_per_env=c["max_contacts"], substeps=c["substeps"])
+              max_contacts_per_env=c["max_contacts"], substeps=c["substeps"], semantics=semantics)
     return ZenoWorld(mjcf_string=xml, **kw), OracleWorld(xml, **kw), c
 
 

@@ -44,6 +44,9 @@ ffi.cdef("""
 
     ZenoWorldHandle zeno_world_create(const char* mjcf_path, const ZenoConfig* config);
     ZenoWorldHandle zeno_world_create_from_string(const char* mjcf_string, const ZenoConfig* config);
+    ZenoWorldHandle zeno_world_create_ex(const char* mjcf_path, const ZenoConfig* config, uint32_t semantics);
+    ZenoWorldHandle zeno_world_create_from_string_ex(const char* mjcf_string, const ZenoConfig* config,
+                                                     uint32_t semantics);
     void zeno_world_destroy(ZenoWorldHandle world);
     int zeno_world_step(ZenoWorldHandle world, const float* actions, uint32_t substeps);
     int zeno_world_step_subset(ZenoWorldHandle world, const float* actions, const uint8_t* env_mask, uint32_t substeps);
@@ -97,6 +100,7 @@ ffi.cdef("""
     const void* zeno_world_model_table(ZenoWorldHandle world, const char* name, uint64_t* nbytes);
     const char* zeno_last_error(void);
     void* zeno_model_create_from_string(const char* mjcf_string);
+    void* zeno_model_create_from_string_ex(const char* mjcf_string, uint32_t semantics);
     void zeno_model_destroy(void* model);
     const void* zeno_model_table(void* model, const char* name, uint64_t* nbytes);
 """)
@@ -177,9 +181,12 @@ class CudaArray:
                                          "version": 3, "strides": None, "stream": None}
 
 
-def model_tables(mjcf_string: str) -> Dict[str, bytes]:
+SEMANTICS = {"reference": 0, "corrected": 1}
+
+
+def model_tables(mjcf_string: str, semantics: str = "reference") -> Dict[str, bytes]:
     """Build the model on the host only (no GPU) and return its reference-layout tables."""
-    h = _lib.zeno_model_create_from_string(mjcf_string.encode())
+    h = _lib.zeno_model_create_from_string_ex(mjcf_string.encode(), SEMANTICS[semantics])
     if h == ffi.NULL:
         raise RuntimeError("model build failed: " + ffi.string(_lib.zeno_last_error()).decode())
     try:
@@ -212,12 +219,16 @@ class ZenoWorld:
     Parameters follow the reference ``ZenoWorld`` (mjcf_path or mjcf_string, num_envs,
     timestep (0: MJCF value), contact_iterations, max_contacts_per_env, seed, substeps,
     enable_profiling, max_*_per_env).  The world binds to the current CUDA device.
+    ``semantics="corrected"`` (no counterpart in the reference) loads and steps the model
+    with the MJCF compiler rules and contact conventions the reference skips; the default
+    "reference" reproduces the reference, quirks included.
     """
 
     def __init__(self, mjcf_path: Optional[str] = None, mjcf_string: Optional[str] = None, num_envs: int = 1,
                  timestep: float = 0, contact_iterations: int = 4, max_contacts_per_env: int = 64,
                  seed: int = 42, substeps: int = 1, enable_profiling: bool = False,
-                 max_bodies_per_env: int = 64, max_joints_per_env: int = 64, max_geoms_per_env: int = 128):
+                 max_bodies_per_env: int = 64, max_joints_per_env: int = 64, max_geoms_per_env: int = 128,
+                 semantics: str = "reference"):
         if mjcf_path is None and mjcf_string is None:
             raise ValueError("Either mjcf_path or mjcf_string must be provided")
         cfg = ffi.new("ZenoConfig*")
@@ -226,10 +237,12 @@ class ZenoWorld:
         cfg.enable_profiling = enable_profiling
         cfg.max_bodies_per_env, cfg.max_joints_per_env, cfg.max_geoms_per_env = (
             max_bodies_per_env, max_joints_per_env, max_geoms_per_env)
+        if semantics not in SEMANTICS:
+            raise ValueError(f"semantics must be one of {sorted(SEMANTICS)}")
         if mjcf_path is not None:
-            self._handle = _lib.zeno_world_create(str(mjcf_path).encode(), cfg)
+            self._handle = _lib.zeno_world_create_ex(str(mjcf_path).encode(), cfg, SEMANTICS[semantics])
         else:
-            self._handle = _lib.zeno_world_create_from_string(mjcf_string.encode(), cfg)
+            self._handle = _lib.zeno_world_create_from_string_ex(mjcf_string.encode(), cfg, SEMANTICS[semantics])
         if self._handle == ffi.NULL:
             msg = ffi.string(_lib.zeno_last_error()).decode()
             raise RuntimeError("Failed to create Zeno world" + (f": {msg}" if msg else ""))

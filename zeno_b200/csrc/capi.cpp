@@ -43,11 +43,15 @@ void set_last_error(const std::string& msg) { g_last_error = msg; }
 
 extern "C" {
 
-ZenoWorldHandle zeno_world_create(const char* mjcf_path, const ZenoConfig* config) {
+ZenoWorldHandle zeno_world_create_ex(const char* mjcf_path, const ZenoConfig* config, uint32_t semantics) {
   if (!mjcf_path || !config) return nullptr;
+  if (semantics > ZENO_SEMANTICS_CORRECTED) {
+    g_last_error = "unknown semantics";
+    return nullptr;
+  }
   zb::Scene sc;
   std::string err;
-  if (!zb::load_mjcf_file(mjcf_path, &sc, &err)) {
+  if (!zb::load_mjcf_file(mjcf_path, &sc, &err, semantics == ZENO_SEMANTICS_CORRECTED)) {
     g_last_error = err;
     std::fprintf(stderr, "zeno: failed to parse MJCF: %s\n", err.c_str());
     return nullptr;
@@ -55,15 +59,28 @@ ZenoWorldHandle zeno_world_create(const char* mjcf_path, const ZenoConfig* confi
   return create_world(sc, config);
 }
 
-ZenoWorldHandle zeno_world_create_from_string(const char* mjcf_string, const ZenoConfig* config) {
+ZenoWorldHandle zeno_world_create_from_string_ex(const char* mjcf_string, const ZenoConfig* config,
+                                                 uint32_t semantics) {
   if (!mjcf_string || !config) return nullptr;
+  if (semantics > ZENO_SEMANTICS_CORRECTED) {
+    g_last_error = "unknown semantics";
+    return nullptr;
+  }
   zb::Scene sc;
   std::string err;
-  if (!zb::load_mjcf(mjcf_string, ".", &sc, &err)) {
+  if (!zb::load_mjcf(mjcf_string, ".", &sc, &err, semantics == ZENO_SEMANTICS_CORRECTED)) {
     g_last_error = err;
     return nullptr;
   }
   return create_world(sc, config);
+}
+
+ZenoWorldHandle zeno_world_create(const char* mjcf_path, const ZenoConfig* config) {
+  return zeno_world_create_ex(mjcf_path, config, ZENO_SEMANTICS_REFERENCE);
+}
+
+ZenoWorldHandle zeno_world_create_from_string(const char* mjcf_string, const ZenoConfig* config) {
+  return zeno_world_create_from_string_ex(mjcf_string, config, ZENO_SEMANTICS_REFERENCE);
 }
 
 void zeno_world_destroy(ZenoWorldHandle world) { delete W(world); }
@@ -297,17 +314,22 @@ const void* zeno_world_model_table(ZenoWorldHandle world, const char* name, uint
 
 const char* zeno_last_error(void) { return g_last_error.c_str(); }
 
-void* zeno_model_create_from_string(const char* mjcf_string) {
-  if (!mjcf_string) return nullptr;
+void* zeno_model_create_from_string_ex(const char* mjcf_string, uint32_t semantics) {
+  if (!mjcf_string || semantics > ZENO_SEMANTICS_CORRECTED) return nullptr;
   zb::Scene sc;
   std::string err;
   auto* m = new zb::HostModel();
-  if (!zb::load_mjcf(mjcf_string, ".", &sc, &err) || !zb::build_model(sc, m, &err)) {
+  if (!zb::load_mjcf(mjcf_string, ".", &sc, &err, semantics == ZENO_SEMANTICS_CORRECTED) ||
+      !zb::build_model(sc, m, &err)) {
     g_last_error = err;
     delete m;
     return nullptr;
   }
   return m;
+}
+
+void* zeno_model_create_from_string(const char* mjcf_string) {
+  return zeno_model_create_from_string_ex(mjcf_string, ZENO_SEMANTICS_REFERENCE);
 }
 
 void zeno_model_destroy(void* model) { delete static_cast<zb::HostModel*>(model); }

@@ -81,6 +81,7 @@ bool pack_fast_model(const HostModel& h, uint32_t max_contacts, uint32_t narrow_
 
   // sort_contacts key (min body << 16 | max body in the reference); only its order is
   // used, so the kernel carries the dense rank of each candidate's key.
+  if (h.corrected) return fail("corrected semantics run on the general kernel");
   std::vector<uint32_t> keys(P);
   for (uint32_t p = 0; p < P; ++p) {
     const uint32_t ta = h.geoms[h.pairs[p].ga].type, tb = h.geoms[h.pairs[p].gb].type;

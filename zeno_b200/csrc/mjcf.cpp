@@ -166,6 +166,8 @@ struct XGeom {
   std::string name;
   int type = 1;  // schema GeomType: 0 plane 1 sphere 2 capsule 3 cylinder 4 box 5 mesh 6 hfield
   float pos[3] = {0, 0, 0}, quat_wxyz[4] = {1, 0, 0, 0}, size[3] = {0.05f, 0, 0};
+  bool has_euler = false;  // read only by the corrected loader
+  float euler[3] = {0, 0, 0};
   bool has_fromto = false, has_mass = false;
   float fromto[6] = {0, 0, 0, 0, 0, 0}, mass = 0, density = 1000;
   float friction[3] = {1, 0.005f, 0.0001f};
@@ -183,6 +185,7 @@ struct XBody {
   std::vector<XJoint> joints;
   std::vector<XGeom> geoms;
   std::vector<XBody> kids;
+  std::vector<std::string> sites;  // site names (corrected sensor resolution)
 };
 struct XActuator {
   std::string joint;
@@ -191,7 +194,7 @@ struct XActuator {
 };
 struct XSensor {
   int type = 0;  // jointpos .. subtreecom in schema order
-  std::string joint;
+  std::string joint, objtype, objname, site;
   float noise = 0;
 };
 struct XDefaults {
@@ -200,6 +203,8 @@ struct XDefaults {
 };
 struct XModel {
   float timestep = 0.002f, gravity[3] = {0, 0, -9.81f};
+  bool angle_degree = true;       // <compiler angle>, read only by the corrected loader
+  std::string eulerseq = "xyz";   // <compiler eulerseq>
   std::map<std::string, XDefaults> defaults;
   XBody world;
   std::vector<XActuator> actuators;
@@ -247,6 +252,7 @@ void geom_attrs(XGeom& g, const std::string& a) {
   }
   if (attr(a, "pos", v)) vec(v, 3, g.pos);
   if (attr(a, "quat", v)) vec(v, 4, g.quat_wxyz);
+  if (attr(a, "euler", v)) g.has_euler = vec(v, 3, g.euler);
   if (attr(a, "size", v)) {  // up to three fields, unparsable ones read as 0
     std::vector<std::string> fs = fields(v);
     for (int i = 0; i < 3; ++i) g.size[i] = (i < int(fs.size()) && num(fs[i], f)) ? f : 0.0f;
@@ -297,6 +303,10 @@ class Reader {
         m.gravity[0] = 0.0f, m.gravity[1] = 0.0f, m.gravity[2] = -9.81f;
         if (attr(t.attrs, "timestep", v)) m.timestep = num(v, f) ? f : 0.002f;
         if (attr(t.attrs, "gravity", v)) vec(v, 3, m.gravity);
+      } else if (t.name == "compiler") {
+        std::string v;
+        if (attr(t.attrs, "angle", v)) m.angle_degree = v != "radian";
+        if (attr(t.attrs, "eulerseq", v) && v.size() == 3) m.eulerseq = v;
       } else if (t.name == "default") {
         defaults(m);
       } else if (t.name == "worldbody") {
@@ -369,6 +379,8 @@ class Reader {
         XGeom g = from_class(m, t.attrs, cls, &XDefaults::geom);
         geom_attrs(g, t.attrs);
         b.geoms.push_back(g);
+      } else if (t.name == "site") {
+        b.sites.push_back(attr(t.attrs, "name", v) ? v : std::string());
       } else if (t.name == "inertial") {
         float f;
         b.has_inertial = true;
@@ -411,6 +423,9 @@ class Reader {
       s.type = ty < 0 ? 0 : ty;  // unknown sensor elements read as jointpos
       float f;
       if (attr(t.attrs, "joint", v)) s.joint = v;
+      if (attr(t.attrs, "objtype", v)) s.objtype = v;
+      if (attr(t.attrs, "objname", v)) s.objname = v;
+      if (attr(t.attrs, "site", v)) s.site = v;
       if (attr(t.attrs, "noise", v)) s.noise = num(v, f) ? f : 0.0f;
       m.sensors.push_back(s);
     }
@@ -596,6 +611,169 @@ void add_children(Scene& sc, const XBody& parent, int32_t parent_id, const float
   }
 }
 
+// ---------------------------------------------------------------- corrected semantics
+// Frame math of the corrected loader: plain IEEE single precision in written order (the
+// file is compiled without contraction), quaternions xyzw.
+constexpr float kDeg = 0.017453292519943295f;  // pi / 180
+
+struct Q {
+  float x, y, z, w;
+};
+// quatMultiply order (src/physics/body.zig:238-245)
+Q qmul(Q a, Q b) {
+  return Q{a.w * b.x + a.x * b.w + a.y * b.z - a.z * b.y, a.w * b.y - a.x * b.z + a.y * b.w + a.z * b.x,
+           a.w * b.z + a.x * b.y - a.y * b.x + a.z * b.w, a.w * b.w - a.x * b.x - a.y * b.y - a.z * b.z};
+}
+// rotateByQuat (src/physics/body.zig:254-264): v + 2 (w (q x v) + q x (q x v))
+void qrot(const float v[3], Q q, float o[3]) {
+  const float u0 = q.y * v[2] - q.z * v[1], u1 = q.z * v[0] - q.x * v[2], u2 = q.x * v[1] - q.y * v[0];
+  const float t0 = q.y * u2 - q.z * u1, t1 = q.z * u0 - q.x * u2, t2 = q.x * u1 - q.y * u0;
+  o[0] = v[0] + 2.0f * (q.w * u0 + t0);
+  o[1] = v[1] + 2.0f * (q.w * u1 + t1);
+  o[2] = v[2] + 2.0f * (q.w * u2 + t2);
+}
+Q qunit(Q q) {
+  const float n = std::sqrt(q.x * q.x + q.y * q.y + q.z * q.z + q.w * q.w);
+  if (!(n > 0.0f)) return Q{0, 0, 0, 1};
+  return Q{q.x / n, q.y / n, q.z / n, q.w / n};
+}
+Q from_wxyz(const float* q) { return Q{q[1], q[2], q[3], q[0]}; }
+// Euler angles in the compiler's sequence: lower-case letters rotate about the moving
+// axes (q = q r), upper-case about the fixed axes (q = r q).
+Q euler_seq(const float e[3], bool degree, const std::string& seq) {
+  Q q{0, 0, 0, 1};
+  for (int i = 0; i < 3; ++i) {
+    const char c = seq[size_t(i)];
+    const int ax = (c | 0x20) - 'x';
+    if (ax < 0 || ax > 2) continue;
+    const float a = degree ? e[i] * kDeg : e[i];
+    const float h = a * 0.5f, s = std::sin(h);
+    Q r{0, 0, 0, std::cos(h)};
+    (ax == 0 ? r.x : ax == 1 ? r.y : r.z) = s;
+    q = (c >= 'a') ? qmul(q, r) : qmul(r, q);
+  }
+  return q;
+}
+// Shortest-arc rotation taking local +z onto the direction of d.
+Q z_onto(const float d[3]) {
+  const float len = std::sqrt(d[0] * d[0] + d[1] * d[1] + d[2] * d[2]);
+  if (!(len > 1e-12f)) return Q{0, 0, 0, 1};
+  const float ux = d[0] / len, uy = d[1] / len, uz = d[2] / len;
+  if (uz < -1.0f + 1e-6f) return Q{1, 0, 0, 0};
+  return qunit(Q{-uy, ux, 0.0f, 1.0f + uz});
+}
+bool fromto_oriented(const XGeom& g) { return g.has_fromto && (g.type == 2 || g.type == 3); }
+// Local orientation of a geom: fromto segment, else euler, else the (normalised) quat.
+Q geom_quat(const XGeom& g, const XModel& m) {
+  if (fromto_oriented(g)) {
+    const float d[3] = {g.fromto[3] - g.fromto[0], g.fromto[4] - g.fromto[1], g.fromto[5] - g.fromto[2]};
+    return z_onto(d);
+  }
+  if (g.has_euler) return euler_seq(g.euler, m.angle_degree, m.eulerseq);
+  return qunit(from_wxyz(g.quat_wxyz));
+}
+void geom_centre(const XGeom& g, float c[3]) {
+  for (int k = 0; k < 3; ++k) c[k] = fromto_oriented(g) ? (g.fromto[k] + g.fromto[k + 3]) * 0.5f : g.pos[k];
+}
+
+SGeom to_geom_corrected(const XGeom& x, uint32_t body, const XModel& m) {
+  SGeom g = to_geom(x, body);
+  geom_centre(x, g.pos);
+  if (x.type == 3 && x.has_fromto) g.size[1] = fromto_half_length(x, x.size[1]);
+  const Q q = geom_quat(x, m);
+  g.quat[0] = q.x, g.quat[1] = q.y, g.quat[2] = q.z, g.quat[3] = q.w;
+  return g;
+}
+
+void mass_props_corrected(const XBody& b, SBody& out, const XModel& m) {
+  if (b.has_inertial || b.geoms.empty()) {
+    mass_props(b, out);
+    return;
+  }
+  out.com[0] = out.com[1] = out.com[2] = 0.0f;
+  float M = 0, I[3] = {0, 0, 0}, c[3] = {0, 0, 0};
+  for (const XGeom& g : b.geoms) {
+    const float gm = g.has_mass ? g.mass : g.density * volume(g);
+    float gi[3];
+    geom_inertia(g, gm, gi);
+    const Q q = geom_quat(g, m);
+    const float e0[3] = {1, 0, 0}, e1[3] = {0, 1, 0}, e2[3] = {0, 0, 1};
+    float c0[3], c1[3], c2[3];  // columns of the geom's rotation
+    qrot(e0, q, c0), qrot(e1, q, c1), qrot(e2, q, c2);
+    float d[3];
+    geom_centre(g, d);
+    const float d2[3] = {d[0] * d[0], d[1] * d[1], d[2] * d[2]};
+    for (int k = 0; k < 3; ++k) {
+      const float rk = c0[k] * c0[k] * gi[0] + c1[k] * c1[k] * gi[1] + c2[k] * c2[k] * gi[2];
+      const float off = k == 0 ? d2[1] + d2[2] : k == 1 ? d2[0] + d2[2] : d2[0] + d2[1];
+      I[k] += rk + gm * off;
+    }
+    for (int k = 0; k < 3; ++k) c[k] += gm * d[k];
+    M += gm;
+  }
+  if (M <= 0) M = 1.0f;
+  out.mass = M;
+  std::memcpy(out.inertia, I, 12);
+  for (int k = 0; k < 3; ++k) out.com[k] = c[k] / M;
+}
+
+void add_children_corrected(Scene& sc, const XBody& parent, int32_t parent_id, const float parent_pos[3], Q pq,
+                            const XModel& m, std::unordered_map<std::string, uint32_t>& site_body) {
+  for (const XBody& x : parent.kids) {
+    SBody b;
+    b.name = x.name;
+    b.parent = parent_id;
+    const Q ql = x.has_euler ? euler_seq(x.euler, m.angle_degree, m.eulerseq) : qunit(from_wxyz(x.quat_wxyz));
+    float r[3];
+    qrot(x.pos, pq, r);
+    for (int k = 0; k < 3; ++k) b.pos[k] = parent_pos[k] + r[k];
+    const Q qw = qmul(pq, ql);
+    b.quat[0] = qw.x, b.quat[1] = qw.y, b.quat[2] = qw.z, b.quat[3] = qw.w;
+    mass_props_corrected(x, b, m);
+    const uint32_t id = uint32_t(sc.bodies.size());
+    sc.bodies.push_back(b);
+    if (x.joints.empty() && parent_id >= 0) {  // implicit fixed joint
+      SJoint j;
+      j.type = 0;
+      j.parent = uint32_t(parent_id);
+      j.child = id;
+      std::memcpy(j.anchor_parent, x.pos, 12);
+      sc.joints.push_back(j);
+    }
+    for (const XJoint& xj : x.joints) {
+      SJoint j;
+      j.name = xj.name;
+      j.parent = parent_id >= 0 ? uint32_t(parent_id) : 0u;
+      j.child = id;
+      float t[3], a[3];
+      qrot(xj.pos, ql, t);
+      qrot(xj.axis, ql, a);
+      const float n = std::sqrt(a[0] * a[0] + a[1] * a[1] + a[2] * a[2]);
+      for (int k = 0; k < 3; ++k) {
+        j.anchor_parent[k] = x.pos[k] + t[k];
+        j.anchor_child[k] = xj.pos[k];
+        j.axis[k] = n > 0.0f ? a[k] / n : xj.axis[k];
+      }
+      static const uint32_t kJ[4] = {4, 3, 2, 1};  // free, ball, slide, hinge
+      j.type = kJ[xj.type];
+      j.damping = xj.damping, j.stiffness = xj.stiffness, j.armature = xj.armature, j.ref = xj.ref;
+      if (xj.ranged) {
+        const bool angular = xj.type == 1 || xj.type == 3;
+        const float s = (angular && m.angle_degree) ? kDeg : 1.0f;
+        j.lower = angular && m.angle_degree ? xj.range[0] * s : xj.range[0];
+        j.upper = angular && m.angle_degree ? xj.range[1] * s : xj.range[1];
+        j.limited = true;
+      }
+      if (!j.name.empty()) sc.joint_by_name[j.name] = uint32_t(sc.joints.size());
+      sc.joints.push_back(j);
+    }
+    for (const XGeom& g : x.geoms) sc.geoms.push_back(to_geom_corrected(g, id, m));
+    for (const std::string& s : x.sites)
+      if (!s.empty()) site_body.emplace(s, id);
+    add_children_corrected(sc, x, int32_t(id), b.pos, qw, m, site_body);
+  }
+}
+
 // <include file="..."/>: splice the included file's content between its <mujoco> tags.
 std::string splice_includes(const std::string& xml, const std::string& dir) {
   if (xml.find("<include") == std::string::npos) return xml;
@@ -649,20 +827,30 @@ std::string splice_includes(const std::string& xml, const std::string& dir) {
 
 }  // namespace
 
-bool load_mjcf(const std::string& text, const std::string& base_dir, Scene* out, std::string* err) {
+bool load_mjcf(const std::string& text, const std::string& base_dir, Scene* out, std::string* err,
+               bool corrected) {
   XModel m;
   std::string xml = splice_includes(text, base_dir);
   Reader(xml).read(m);
   Scene sc;
+  sc.corrected = corrected;
   sc.timestep = m.timestep;
   std::memcpy(sc.gravity, m.gravity, 12);
   SBody world;
   world.name = "world";
   world.type = 0;
   sc.bodies.push_back(world);
-  for (const XGeom& g : m.world.geoms) sc.geoms.push_back(to_geom(g, 0));
   const float origin[3] = {0, 0, 0};
-  add_children(sc, m.world, 0, origin);
+  std::unordered_map<std::string, uint32_t> site_body;
+  if (corrected) {
+    for (const XGeom& g : m.world.geoms) sc.geoms.push_back(to_geom_corrected(g, 0, m));
+    for (const std::string& s : m.world.sites)
+      if (!s.empty()) site_body.emplace(s, 0u);
+    add_children_corrected(sc, m.world, 0, origin, Q{0, 0, 0, 1}, m, site_body);
+  } else {
+    for (const XGeom& g : m.world.geoms) sc.geoms.push_back(to_geom(g, 0));
+    add_children(sc, m.world, 0, origin);
+  }
   for (const XActuator& xa : m.actuators) {
     auto it = xa.joint.empty() ? sc.joint_by_name.end() : sc.joint_by_name.find(xa.joint);
     if (it == sc.joint_by_name.end()) continue;
@@ -682,13 +870,28 @@ bool load_mjcf(const std::string& text, const std::string& base_dir, Scene* out,
     if (xs.type <= 1) {
       auto it = xs.joint.empty() ? sc.joint_by_name.end() : sc.joint_by_name.find(xs.joint);
       s.object = it == sc.joint_by_name.end() ? 0u : it->second;
+    } else if (corrected) {  // body named by objname (objtype body / xbody), else the site's body
+      const bool body_obj = xs.objtype.empty() || xs.objtype == "body" || xs.objtype == "xbody";
+      uint32_t obj = 0;
+      if (body_obj && !xs.objname.empty()) {
+        for (uint32_t i = 0; i < sc.bodies.size(); ++i)
+          if (sc.bodies[i].name == xs.objname) {
+            obj = i;
+            break;
+          }
+      } else {
+        const std::string& site = xs.objtype == "site" ? xs.objname : xs.site;
+        auto it = site.empty() ? site_body.end() : site_body.find(site);
+        if (it != site_body.end()) obj = it->second;
+      }
+      s.object = obj;
     }
     sc.sensors.push_back(s);
   }
   if (sc.sensors.empty()) {  // root-body frame sensors plus pos/vel per joint
     uint32_t root = 0;
     for (uint32_t i = 0; i < sc.bodies.size(); ++i)
-      if (sc.bodies[i].type == 2 && sc.bodies[i].parent < 0) {
+      if (sc.bodies[i].type == 2 && (corrected ? sc.bodies[i].parent == 0 : sc.bodies[i].parent < 0)) {
         root = i;
         break;
       }
@@ -704,7 +907,7 @@ bool load_mjcf(const std::string& text, const std::string& base_dir, Scene* out,
   return true;
 }
 
-bool load_mjcf_file(const std::string& path, Scene* out, std::string* err) {
+bool load_mjcf_file(const std::string& path, Scene* out, std::string* err, bool corrected) {
   std::ifstream in(path);
   if (!in) {
     if (err) *err = "file not found: " + path;
@@ -713,7 +916,7 @@ bool load_mjcf_file(const std::string& path, Scene* out, std::string* err) {
   std::stringstream ss;
   ss << in.rdbuf();
   size_t slash = path.find_last_of('/');
-  return load_mjcf(ss.str(), slash == std::string::npos ? "." : path.substr(0, slash), out, err);
+  return load_mjcf(ss.str(), slash == std::string::npos ? "." : path.substr(0, slash), out, err, corrected);
 }
 
 }  // namespace zb

@@ -5,6 +5,7 @@
 //   greedy colouring, stable sort     src/physics/xpbd.zig:533-640
 //   GPU record layouts                world.zig:1573-1637, primitives.zig:424-441, sensors.zig:142-160
 #include <algorithm>
+#include <cmath>
 #include <bitset>
 #include <cstring>
 
@@ -161,6 +162,18 @@ uint32_t colour(std::vector<RefConstraint>& cs, uint32_t nb) {
   return ncol;
 }
 
+// Radius of a sphere around the geom centre that holds the whole geom (corrected broad
+// phase): sphere r, capsule r + half length, box |half extents|, cylinder
+// sqrt(r^2 + half length^2); other types keep size[0].
+float bound_radius(const SGeom& g) {
+  switch (g.type) {
+    case 1: return g.size[0] + g.size[1];
+    case 2: return std::sqrt(g.size[0] * g.size[0] + g.size[1] * g.size[1] + g.size[2] * g.size[2]);
+    case 4: return std::sqrt(g.size[0] * g.size[0] + g.size[1] * g.size[1]);
+    default: return g.size[0];
+  }
+}
+
 template <class T>
 void blob(std::vector<uint8_t>& dst, const std::vector<T>& v) {
   dst.resize(v.size() * sizeof(T));
@@ -171,6 +184,7 @@ void blob(std::vector<uint8_t>& dst, const std::vector<T>& v) {
 
 bool build_model(const Scene& sc, HostModel* m, std::string* err) {
   HostModel h;
+  h.corrected = sc.corrected;
   h.B = uint32_t(sc.bodies.size());
   h.J = uint32_t(sc.joints.size());
   h.A = uint32_t(sc.actuators.size());
@@ -228,7 +242,7 @@ bool build_model(const Scene& sc, HostModel* m, std::string* err) {
       const SGeom &ga = sc.geoms[a], &gb = sc.geoms[b];
       if (ga.body == gb.body) continue;
       if ((ga.contype & gb.conaffinity) == 0 && (gb.contype & ga.conaffinity) == 0) continue;
-      const float md = (ga.size[0] + gb.size[0]) + 0.1f;
+      const float md = (sc.corrected ? bound_radius(ga) + bound_radius(gb) : ga.size[0] + gb.size[0]) + 0.1f;
       h.pairs.push_back(DPair{a, b, md * md, (ga.type == 3 || gb.type == 3) ? 1u : 0u});
     }
   std::vector<uint32_t> seen(h.J, 0);

@@ -25,6 +25,7 @@ struct HostModel {
   std::vector<uint32_t> subtree;
   std::vector<float> init_state;         // B*4 pos, B*4 quat, B*4 vel, B*4 angvel, J jpos, J jvel
   bool actuators_unique = true;
+  bool corrected = false;  // corrected semantics: rotated geom frames and bounds, B->A normals
   // reference-layout records (byte blobs) for model parity checks
   std::vector<uint8_t> ref_bodies, ref_joints, ref_geoms, ref_actuators, ref_sensors, ref_constraints;
 };

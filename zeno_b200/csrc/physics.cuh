@@ -835,6 +835,26 @@ static __device__ __noinline__ bool gjk_contact(const Shape& A, const Shape& B, 
 
 }  // namespace cpu_narrow
 
+// ---- corrected semantics ----
+// quatMultiply (src/physics/body.zig:238-245) in written order, plain IEEE operations.
+__device__ __forceinline__ float4 qmul_ref(float4 a, float4 b) {
+  return make_float4(a.w * b.x + a.x * b.w + a.y * b.z - a.z * b.y, a.w * b.y - a.x * b.z + a.y * b.w + a.z * b.x,
+                     a.w * b.z + a.x * b.y - a.y * b.x + a.z * b.w, a.w * b.w - a.x * b.x - a.y * b.y - a.z * b.z);
+}
+// World centre of a geom (transformPoint of its local position by the body pose).
+__device__ __forceinline__ V3 geom_centre(float4 bp, float4 bq, float4 local) {
+  using namespace cpu_narrow;
+  const P3 c = Xf{P3{bp.x, bp.y, bp.z}, bq}.point(P3{local.x, local.y, local.z});
+  return V3{c.x, c.y, c.z};
+}
+// The routines that return normals from A to B (sphere-sphere, capsule-capsule, box-box,
+// and GJK's box-capsule; the others and every plane pair point from B to A).  Corrected
+// semantics negate these, so that every normal points from B to A, the direction
+// solve_contacts (all_shaders.metal:1731-1745) pushes A along.
+__host__ __device__ inline bool normal_a_to_b(uint32_t ta, uint32_t tb) {
+  return (ta == tb && ta <= 2u) || (ta == 1u && tb == 2u) || (ta == 2u && tb == 1u);
+}
+
 // True for the type pairs narrow_cpu can report a contact for (types 0 sphere, 1 capsule,
 // 2 box, 3 plane; no plane-plane; box-capsule only with GJK + EPA, mode 2).
 __host__ __device__ inline bool narrow_cpu_supported(uint32_t ta, uint32_t tb, bool gjk_pairs = false) {

@@ -8,6 +8,8 @@
 //  * capsule fromto sets the midpoint and half length but keeps an identity local quat
 //  * bodies without joints receive an implicit fixed joint (weld) to their parent
 //  * frame sensors observe body 0 (object id is resolved only for joint sensors)
+// A world created with corrected semantics (ZENO_SEMANTICS_CORRECTED) instead follows the
+// MJCF compiler rules for these items; see load_mjcf.
 #pragma once
 #include <cstdint>
 #include <limits>
@@ -74,11 +76,28 @@ struct Scene {
   float gravity[3] = {0.0f, 0.0f, -9.81f};
   // constants.zig:6-42 PhysicsConfig defaults
   float friction = 1.0f, restitution = 0.0f, baumgarte = 0.2f, slop = 0.005f;
+  bool corrected = false;  // loaded with corrected semantics (frames, angles, sensors)
   uint32_t obs_dim() const;
 };
 
 // Parse MJCF text.  `base_dir` resolves <include file="..."/> (parser.zig:55-171).
-bool load_mjcf(const std::string& text, const std::string& base_dir, Scene* out, std::string* err);
-bool load_mjcf_file(const std::string& path, Scene* out, std::string* err);
+// corrected = false reproduces the reference loader, quirks included.  corrected = true
+// applies the MJCF compiler rules the reference skips:
+//  * <compiler angle> (default "degree") converts hinge/ball ranges and euler angles, and
+//    <compiler eulerseq> (default "xyz"; lower case = moving axes) orders euler rotations;
+//  * body frames compose with the parent's rotation: pos_w = p_parent + R_parent pos,
+//    q_w = q_parent q_local (local quats normalised);
+//  * joint pos and axis are child-frame quantities: anchor_parent = pos + R_local jpos,
+//    axis (kept in the parent frame, as the constraints read it) = normalise(R_local axis);
+//  * geoms keep their orientation: quat / euler attributes, and fromto capsules and
+//    cylinders turn local +z onto the segment (shortest arc); their centre is the midpoint;
+//  * body inertia sums each geom's principal inertia rotated into the body frame (the
+//    diagonal is kept: the step carries a diagonal inverse inertia) plus the parallel-axis
+//    term of the geom centre;
+//  * frame and site sensors resolve objname (objtype body/xbody) or site to their body; the
+//    automatic sensors observe the first child of the world instead of the world.
+bool load_mjcf(const std::string& text, const std::string& base_dir, Scene* out, std::string* err,
+               bool corrected = false);
+bool load_mjcf_file(const std::string& path, Scene* out, std::string* err, bool corrected = false);
 
 }  // namespace zb

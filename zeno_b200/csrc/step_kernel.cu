@@ -126,7 +126,8 @@ struct ArrBodies {
 // reference's CPU detectCollision, src/collision/narrow_phase.zig:28-136; mode 2: as 1,
 // with GJK + EPA, src/collision/gjk.zig, for box-capsule pairs)
 __device__ __forceinline__ void narrow(uint32_t pk, const DGeom* geoms, const float4* pos, const float4* quat,
-                                       uint32_t mode, float restitution, float4& cpp, float4& cnf, float4& cim) {
+                                       uint32_t mode, uint32_t corrected, float restitution, float4& cpp, float4& cnf,
+                                       float4& cim) {
   const DGeom& gA = geoms[pk_ga(pk)];
   const DGeom& gB = geoms[pk_gb(pk)];
   const float4 ga0 = __ldg(reinterpret_cast<const float4*>(gA.pos_size0));
@@ -138,8 +139,18 @@ __device__ __forceinline__ void narrow(uint32_t pk, const DGeom* geoms, const fl
   if (mode >= 1) {
     const float2 sa = make_float2(__ldg(&gA.size12_fr_rest[0]), __ldg(&gA.size12_fr_rest[1]));
     const float2 sb = make_float2(__ldg(&gB.size12_fr_rest[0]), __ldg(&gB.size12_fr_rest[1]));
-    hit = narrow_cpu(ta, tb, ga0, sa, gb0, sb, pos[pk_a(pk)], quat[pk_a(pk)], pos[pk_b(pk)], quat[pk_b(pk)], point,
-                     normal, pen, mode == 2);
+    if (corrected) {  // each geom placed by its own world frame: body pose (x) geom local pose
+      const float4 qa = quat[pk_a(pk)], qb = quat[pk_b(pk)];
+      const V3 ca = geom_centre(pos[pk_a(pk)], qa, ga0), cb = geom_centre(pos[pk_b(pk)], qb, gb0);
+      const float4 wqa = qmul_ref(qa, __ldg(reinterpret_cast<const float4*>(gA.quat)));
+      const float4 wqb = qmul_ref(qb, __ldg(reinterpret_cast<const float4*>(gB.quat)));
+      hit = narrow_cpu(ta, tb, make_float4(0.0f, 0.0f, 0.0f, ga0.w), sa, make_float4(0.0f, 0.0f, 0.0f, gb0.w), sb,
+                       with_w(ca, 0.0f), wqa, with_w(cb, 0.0f), wqb, point, normal, pen, mode == 2);
+      if (hit && normal_a_to_b(ta, tb)) normal = v3(-normal.x, -normal.y, -normal.z);
+    } else {
+      hit = narrow_cpu(ta, tb, ga0, sa, gb0, sb, pos[pk_a(pk)], quat[pk_a(pk)], pos[pk_b(pk)], quat[pk_b(pk)],
+                       point, normal, pen, mode == 2);
+    }
   } else {
     const V3 pa = v3(pos[pk_a(pk)]) + v3(ga0), pb = v3(pos[pk_b(pk)]) + v3(gb0);
     const DGeom& cg = ta == 1 ? gA : gB;
@@ -287,6 +298,9 @@ __device__ __forceinline__ void step_env(const StepArgs& a, uint32_t e, unsigned
   const V3 grav{a.gravity[0], a.gravity[1], a.gravity[2]};
   const float* act = a.actions + size_t(e) * A;
 
+  // slots written during this step (corrected semantics rebuild the list each substep,
+  // so a later substep can hold fewer than an earlier one; every written slot goes back)
+  uint32_t n_hi = 0;
   for (uint32_t s = 0; s < a.substeps; ++s) {
     // ---- prev snapshot = final slot list of the previous substep ----
     const uint32_t n_prev = prev_count < M ? prev_count : M;
@@ -361,6 +375,9 @@ __device__ __forceinline__ void step_env(const StepArgs& a, uint32_t e, unsigned
     }
     __syncwarp(gmask);
     // ---- broad phase: candidate pairs in emission order, compacted by ballot ----
+    // (corrected semantics rebuild the list every substep; the reference's counter only
+    // grows, so its list freezes with duplicates once M candidates were emitted)
+    if (a.corrected) count = 0;
     const uint32_t count0 = count;
     for (uint32_t r = 0; r < a.num_pairs; r += L) {
       const uint32_t p = r + l;
@@ -375,8 +392,11 @@ __device__ __forceinline__ void step_env(const StepArgs& a, uint32_t e, unsigned
         if (pr.plane) {
           pass = true;
         } else {
-          const V3 pa = v3(pos[ba]) + v3(__ldg(reinterpret_cast<const float4*>(a.geoms[ga].pos_size0)));
-          const V3 pb = v3(pos[bb]) + v3(__ldg(reinterpret_cast<const float4*>(a.geoms[gb].pos_size0)));
+          const float4 la = __ldg(reinterpret_cast<const float4*>(a.geoms[ga].pos_size0));
+          const float4 lb = __ldg(reinterpret_cast<const float4*>(a.geoms[gb].pos_size0));
+          // corrected semantics rotate the geom offsets with the body (transformPoint)
+          const V3 pa = a.corrected ? geom_centre(pos[ba], quat[ba], la) : v3(pos[ba]) + v3(la);
+          const V3 pb = a.corrected ? geom_centre(pos[bb], quat[bb], lb) : v3(pos[bb]) + v3(lb);
           const V3 d = pb - pa;
           pass = !(dot(d, d) >= pr.min_dist_sq);
         }
@@ -390,6 +410,7 @@ __device__ __forceinline__ void step_env(const StepArgs& a, uint32_t e, unsigned
     }
     const uint32_t n = count < M ? count : M;
     const uint32_t n_old = count0 < M ? count0 : M;
+    n_hi = n > n_hi ? n : n_hi;
     __syncwarp(gmask);
     // ---- stable sort by body-pair key (only when slots were appended) ----
     if (n > n_old) {
@@ -409,7 +430,7 @@ __device__ __forceinline__ void step_env(const StepArgs& a, uint32_t e, unsigned
     // ---- narrow phase ----
     for (uint32_t i = l; i < n; i += L) {
       const uint32_t st = ord[i];
-      narrow(cpk[st], a.geoms, pos, quat, a.narrow_mode, a.restitution, cpp[st], cnf[st], cim[st]);
+      narrow(cpk[st], a.geoms, pos, quat, a.narrow_mode, a.corrected, a.restitution, cpp[st], cnf[st], cim[st]);
     }
     __syncwarp(gmask);
     // ---- warm start: best previous contact of the same pair within 0.2 ----
@@ -591,7 +612,8 @@ __device__ __forceinline__ void step_env(const StepArgs& a, uint32_t e, unsigned
     gacc[b] = make_float4((v1.x - v0.x) * a.inv_step, (v1.y - v0.y) * a.inv_step, (v1.z - v0.z) * a.inv_step, 0.0f);
   }
   // ---- contacts back to HBM (slot order) ----
-  for (uint32_t i = l; i < n_fin; i += L) {
+  const uint32_t n_out = n_hi > n_fin ? n_hi : n_fin;
+  for (uint32_t i = l; i < n_out; i += L) {
     const uint32_t st = ord[i], k = cpk[st];
     float4* dst = reinterpret_cast<float4*>(gcw + i);
     dst[0] = cpp[st];

@@ -81,6 +81,7 @@ World* World::create(const Scene& sc, const WorldConfig& cfg, std::string* err) 
   w->envs_per_block_ = int(std::min<uint32_t>(4u, uint32_t(smem_cap) / env_bytes));
   // environment-per-lane kernel when the model packs into its fixed-capacity tables
   std::string why;
+  if (m.corrected) w->narrow_mode_ = 2;  // corrected semantics use the CPU routines + GJK
   w->fast_ok_ = pack_fast_model(m, M, w->narrow_mode_, &w->fmodel_, &w->hot_image_, &why);
 
   if (cudaStreamCreateWithFlags(&w->own_stream_, cudaStreamNonBlocking) != cudaSuccess) return fail("stream", w);
@@ -194,6 +195,7 @@ StepArgs World::args(uint32_t substeps, const float* actions, const uint8_t* mas
   a.substeps = substeps;
   a.actuators_unique = m.actuators_unique ? 1u : 0u;
   a.narrow_mode = narrow_mode_;
+  a.corrected = model_.corrected ? 1u : 0u;
   a.dt = timestep_ / float(substeps > 1 ? substeps : 1u);  // world.zig:699-702
   a.inv_dt = 1.0f / a.dt;
   a.inv_step = timestep_ > 0 ? 1.0f / timestep_ : 0.0f;  // world.zig:736
@@ -415,7 +417,7 @@ int World::set_launch(int lanes, int envs_per_block) {
 // Selects the narrow phase and re-packs the compressed-state model (its hittable pairs
 // depend on it); a model that no longer fits runs on the general kernel.
 int World::set_narrow_phase(uint32_t mode) {
-  if (mode > 2) return -6;
+  if (mode > 2 || (model_.corrected && mode == 0)) return -6;
   if (mode == narrow_mode_) return 0;
   if (cudaStreamSynchronize(stream_) != cudaSuccess) return -4;
   narrow_mode_ = mode;

@@ -63,7 +63,8 @@ struct DGeom {
 // the reference's emission order (geom a ascending, then b ascending).
 struct DPair {
   uint32_t ga, gb;
-  float min_dist_sq;  // ((r_a + r_b) + 0.1)^2, evaluated on the host in float
+  float min_dist_sq;  // ((r_a + r_b) + 0.1)^2, evaluated on the host in float (r: size[0], or
+                      // the bounding radius under corrected semantics)
   uint32_t plane;     // 1: plane pair, always emitted
 };
 
@@ -100,7 +101,9 @@ struct StepArgs {
   uint32_t num_envs, B, J, A, G, S, M, K, obs_dim, num_colors, num_pairs, iterations;
   uint32_t substeps;
   uint32_t actuators_unique;  // 1: no two actuators drive the same joint
-  uint32_t narrow_mode;       // 0: reference GPU narrow phase; 1: its CPU detectCollision
+  uint32_t narrow_mode;       // 0: reference GPU narrow phase; 1: its CPU detectCollision;
+                              // 2: as 1 plus GJK + EPA for box-capsule pairs
+  uint32_t corrected;         // 1: corrected semantics (geom frames, bounds, B->A normals)
   float dt, inv_dt, inv_step;  // dt = timestep/substeps, inv_dt = 1/dt, inv_step = 1/timestep
   float gravity[3];
   float baumgarte, slop, restitution;
