@@ -20,6 +20,12 @@ no collective on the step path (weak scaling); timings are the max over ranks.
 --impl reference times the reference algorithm on the host CPU cores: the reference
 implementation cannot run here (its step exists only as Metal shaders), so the CPU
 restatement in oracle/ is timed with all host threads on a bounded sample of envs.
+
+Other workloads (not the headline line; same JSON contract): --scene humanoid (the
+reference Humanoid, dt 0.015 s, 4 substeps, actions U(-0.4, 0.4), done = torso z < 1.0 with
+U(-0.01, 0.01) reset noise) or --scene collision_stress (the seeded 64-body drop scene,
+4096 envs per GPU, dt 0.005 s, 8 substeps, 256 contact slots, no actuators); --narrow 0/1/2
+selects the narrow phase and --semantics corrected the corrected-semantics mode.
 """
 from __future__ import annotations
 
@@ -48,6 +54,23 @@ ITERATIONS = 4
 MAX_CONTACTS = 64
 METRIC = "env-steps/sec (whole box, Ant 16384 envs/GPU)"
 UNIT = "env-steps/s"
+
+
+def scene_config(name: str) -> dict:
+    """Per-workload settings: envs per GPU, timestep (0: the MJCF's), substeps, solver
+    iterations, contact slots, action scale, the task (done rule and reset noise) or None."""
+    from zeno_b200 import scenes
+    inf = float("inf")
+    return {
+        "ant": dict(xml=scenes.ant, envs=ENVS_PER_GPU, timestep=0.0, substeps=SUBSTEPS, iters=ITERATIONS,
+                    M=MAX_CONTACTS, act=1.0, task=dict(body=1, z_min=0.2, z_max=1.0, noise=0.1),
+                    task_text="done: torso z not in [0.2, 1.0], device auto-reset, U(-0.1,0.1) noise"),
+        "humanoid": dict(xml=scenes.humanoid, envs=ENVS_PER_GPU, timestep=0.015, substeps=4, iters=4, M=64,
+                         act=0.4, task=dict(body=1, z_min=1.0, z_max=inf, noise=0.01),
+                         task_text="done: torso z < 1.0, device auto-reset, U(-0.01,0.01) noise"),
+        "collision_stress": dict(xml=lambda: scenes.collision_stress(0), envs=4096, timestep=0.005, substeps=8,
+                                 iters=4, M=256, act=0.0, task=None, task_text="none (free fall, no actuators)"),
+    }[name]
 
 
 def algorithmic_bytes_per_env_step(B, J, A, obs, K, S):
@@ -149,17 +172,21 @@ def measured_peaks():
     return 6650.0, "fallback"
 
 
-def cpu_baseline(xml, steps, sample_envs, threads, target_s=None):
+def cpu_baseline(xml, steps, sample_envs, threads, target_s=None, sc=None, narrow=None, semantics="reference"):
     """The CPU oracle (reference algorithm restated) on a bounded sample of envs: `steps`
     steps, or (target_s set) as many 10-step batches as fill about target_s seconds.
     Returns (env-steps/s, seconds, steps run)."""
     from oracle.zeno_oracle import OracleWorld
-    o = OracleWorld(xml, num_envs=sample_envs, substeps=SUBSTEPS, contact_iterations=ITERATIONS,
-                    max_contacts_per_env=MAX_CONTACTS)
-    o.set_task(body=1, z_min=0.2, z_max=1.0, auto_reset=True, noise=0.1, seed=1)
+    sc = sc or scene_config("ant")
+    o = OracleWorld(xml, num_envs=sample_envs, timestep=sc["timestep"], substeps=sc["substeps"],
+                    contact_iterations=sc["iters"], max_contacts_per_env=sc["M"], semantics=semantics)
+    if narrow is not None:
+        o.set_narrow_phase(narrow)
+    if sc["task"]:
+        o.set_task(auto_reset=True, seed=1, **sc["task"])
     rng = np.random.default_rng(0)
     batch = 10 if target_s else steps
-    acts = rng.uniform(-1, 1, size=(batch, sample_envs, 8)).astype(np.float32)
+    acts = (sc["act"] * rng.uniform(-1, 1, size=(batch, sample_envs, o.num_actuators))).astype(np.float32)
     o.run(acts[:1], threads=threads)  # warm-up
     done = 0
     t0 = time.perf_counter()
@@ -172,23 +199,40 @@ def cpu_baseline(xml, steps, sample_envs, threads, target_s=None):
     return done * sample_envs / dt, dt, done
 
 
+def metric_name(args, E):
+    if args.scene == "ant" and args.narrow is None and args.semantics == "reference":
+        return METRIC
+    return f"env-steps/sec (whole box, {args.scene} {E} envs/GPU)"
+
+
+def workload_name(args):
+    w = args.scene
+    if args.narrow is not None:
+        w += f", narrow phase {args.narrow}"
+    if args.semantics != "reference":
+        w += f", {args.semantics} semantics"
+    return w
+
+
 def run_reference(args, rank):
     if rank != 0:
         return 0
-    from zeno_b200 import scenes
     threads = os.cpu_count() or 1
-    sample = 2048
-    xml = scenes.ant()
-    val, dt, _ = cpu_baseline(xml, args.warmup + args.steps, sample, threads)
+    sc = scene_config(args.scene)
+    sample = min(2048, sc["envs"])
+    xml = sc["xml"]()
+    val, dt, _ = cpu_baseline(xml, args.warmup + args.steps, sample, threads, sc=sc, narrow=args.narrow,
+                              semantics=args.semantics)
     line = {
-        "impl": "reference", "metric": METRIC, "value": val, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+        "impl": "reference", "metric": metric_name(args, sc["envs"]), "value": val, "unit": UNIT,
+        "n_gpus": args.gpus, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": 1000.0 * sample / val, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "ant", "envs_per_gpu": ENVS_PER_GPU, "substeps": SUBSTEPS,
-                   "contact_iterations": ITERATIONS, "max_contacts_per_env": MAX_CONTACTS,
+        "config": {"workload": workload_name(args), "envs_per_gpu": sc["envs"], "substeps": sc["substeps"],
+                   "contact_iterations": sc["iters"], "max_contacts_per_env": sc["M"],
                    "sample_envs_per_step": sample},
         "cpu_baseline": {"value": val, "unit": UNIT, "cores": threads, "kind": "port",
-                         "sample": f"{sample} Ant envs x {args.warmup + args.steps} steps on {threads} threads "
+                         "sample": f"{sample} {args.scene} envs x {args.warmup + args.steps} steps on {threads} threads "
                                    f"({dt:.1f} s); the reference step exists only as Metal shaders, so the CPU "
                                    "restatement in oracle/ stands in for it"},
         "e2e": {"value": val, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -236,12 +280,15 @@ def run_ours(args, rank, world_size, local_rank):
         dist_.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local_rank))
         dist = dist_
 
-    E = args.envs
-    xml = scenes.ant()
-    w = zeno_b200.ZenoWorld(mjcf_string=xml, num_envs=E, substeps=SUBSTEPS, contact_iterations=ITERATIONS,
-                            max_contacts_per_env=MAX_CONTACTS)
-    w.set_task(body=1, z_min=0.2, z_max=1.0, auto_reset=True, noise=0.1, seed=1,
-               env_offset=shard_env_offset(rank, E))
+    sc = scene_config(args.scene)
+    E = args.envs or sc["envs"]
+    xml = sc["xml"]()
+    w = zeno_b200.ZenoWorld(mjcf_string=xml, num_envs=E, timestep=sc["timestep"], substeps=sc["substeps"],
+                            contact_iterations=sc["iters"], max_contacts_per_env=sc["M"], semantics=args.semantics)
+    if args.narrow is not None:
+        w.set_narrow_phase(args.narrow)
+    if sc["task"]:
+        w.set_task(auto_reset=True, seed=1, env_offset=shard_env_offset(rank, E), **sc["task"])
     # a dedicated stream: the world launches on it and the timing events record on it
     stream = torch.cuda.Stream()
     torch.cuda.set_stream(stream)
@@ -252,7 +299,7 @@ def run_ours(args, rank, world_size, local_rank):
     gen = torch.Generator(device="cuda").manual_seed(1234 + rank)
     total = args.warmup + args.steps
     ring = min(total, ACTION_RING)  # distinct action batches, cycled
-    acts = torch.rand((ring, E, A), device="cuda", generator=gen, dtype=torch.float32) * 2 - 1
+    acts = (torch.rand((ring, E, A), device="cuda", generator=gen, dtype=torch.float32) * 2 - 1) * sc["act"]
     flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device="cuda")  # 256 MiB > 126 MB L2
 
     def barrier():
@@ -296,25 +343,32 @@ def run_ours(args, rank, world_size, local_rank):
         st = w.get_info()
         counts = w.get_contact_counts()
         obs_dim, B, J = w.obs_dim, w.num_bodies, w.num_joints
-        K = 24
-        bpe = algorithmic_bytes_per_env_step(B, J, A, obs_dim, K, MAX_CONTACTS)
+        try:
+            K = len(w.model_table("constraints")) // 96
+        except KeyError:  # no constraints (free bodies only)
+            K = 0
+        bpe = algorithmic_bytes_per_env_step(B, J, A, obs_dim, K, sc["M"])
         mean_ms = statistics.mean(step_ms)
         achieved = bpe * E / (mean_ms / 1000.0) / 1e9
         peak, peak_kind = measured_peaks()
         lanes, epb = w.get_launch()
         kernel = f"zb::fast_step_kernel<{lanes}>" if lanes in (1, 2, 4) else f"zb::step_kernel<{lanes}>"
         traffic = dram_bytes_per_launch(kernel, E)
-        cpu_val, cpu_dt, cpu_steps = (cpu_baseline(xml, 0, CPU_SAMPLE_ENVS, os.cpu_count() or 1, CPU_SAMPLE_S)
+        cpu_envs = min(CPU_SAMPLE_ENVS, E)
+        cpu_val, cpu_dt, cpu_steps = (cpu_baseline(xml, 0, cpu_envs, os.cpu_count() or 1, CPU_SAMPLE_S, sc=sc,
+                                                   narrow=args.narrow, semantics=args.semantics)
                                       if not args.no_cpu else (None, 0, 0))
         clocks = clk.summary()
         line = {
-            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world_size, "steps": args.steps,
+            "metric": metric_name(args, E), "value": value, "unit": UNIT, "n_gpus": world_size, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": t_max * 1000.0 / args.steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "ant", "envs_per_gpu": E, "substeps": SUBSTEPS, "contact_iterations": ITERATIONS,
-                       "max_contacts_per_env": MAX_CONTACTS, "timestep": st["timestep"],
-                       "task": "done: torso z not in [0.2, 1.0], device auto-reset, U(-0.1,0.1) noise",
-                       "actions": "U(-1,1), resident in HBM", "l2": "flushed (256 MiB write) between timed steps",
+            "config": {"workload": workload_name(args), "envs_per_gpu": E, "substeps": sc["substeps"],
+                       "contact_iterations": sc["iters"], "max_contacts_per_env": sc["M"], "timestep": st["timestep"],
+                       "narrow_phase": w.get_narrow_phase(), "semantics": args.semantics,
+                       "task": sc["task_text"],
+                       "actions": f"U(-{sc['act']},{sc['act']}), resident in HBM" if A else "none",
+                       "l2": "flushed (256 MiB write) between timed steps",
                        "launch": {"lanes_per_env": lanes, "envs_per_block": epb},
                        "parallelism": f"env-sharded x{world_size}, no collective on the step path"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
@@ -322,7 +376,7 @@ def run_ours(args, rank, world_size, local_rank):
                          "bytes_per_env_step": bpe, "kernel": kernel,
                          "mean_launch_ms": mean_ms},
             "cpu_baseline": {"value": cpu_val, "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
-                             "sample": f"{CPU_SAMPLE_ENVS} Ant envs x {cpu_steps} steps, oracle on "
+                             "sample": f"{cpu_envs} {args.scene} envs x {cpu_steps} steps, oracle on "
                                        f"{os.cpu_count()} threads ({cpu_dt:.1f} s)"},
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": int(d2h)},
             # per step: the step kernel, plus (environment-per-lane kernel) the hand-over
@@ -348,7 +402,10 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline sample")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end (host buffer) leg")
-    ap.add_argument("--envs", type=int, default=ENVS_PER_GPU, help="environments per GPU")
+    ap.add_argument("--envs", type=int, default=0, help="environments per GPU (0: the workload's)")
+    ap.add_argument("--scene", choices=["ant", "humanoid", "collision_stress"], default="ant")
+    ap.add_argument("--narrow", type=int, choices=[0, 1, 2], default=None, help="narrow phase (default: the world's)")
+    ap.add_argument("--semantics", choices=["reference", "corrected"], default="reference")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
