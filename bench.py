@@ -25,7 +25,10 @@ Other workloads (not the headline line; same JSON contract): --scene humanoid (t
 reference Humanoid, dt 0.015 s, 4 substeps, actions U(-0.4, 0.4), done = torso z < 1.0 with
 U(-0.01, 0.01) reset noise) or --scene collision_stress (the seeded 64-body drop scene,
 4096 envs per GPU, dt 0.005 s, 8 substeps, 256 contact slots, no actuators); --narrow 0/1/2
-selects the narrow phase and --semantics corrected the corrected-semantics mode.
+selects the narrow phase and --semantics corrected the corrected-semantics mode;
+--scene sphere_pile (600 free spheres, 1024 envs per GPU, 1024 contact slots: past the
+reference's 512-geom switch to its spatial hash) with --broad 1 (all candidate pairs) or
+--broad 2 (hashed grid; the default above 512 geoms) times the broad phases.
 """
 from __future__ import annotations
 
@@ -70,6 +73,8 @@ def scene_config(name: str) -> dict:
                          task_text="done: torso z < 1.0, device auto-reset, U(-0.01,0.01) noise"),
         "collision_stress": dict(xml=lambda: scenes.collision_stress(0), envs=4096, timestep=0.005, substeps=8,
                                  iters=4, M=256, act=0.0, task=None, task_text="none (free fall, no actuators)"),
+        "sphere_pile": dict(xml=lambda: scenes.sphere_pile(0), envs=1024, timestep=0.005, substeps=4, iters=4,
+                            M=1024, act=0.0, task=None, task_text="none (600 free spheres, no actuators)"),
     }[name]
 
 
@@ -200,13 +205,15 @@ def cpu_baseline(xml, steps, sample_envs, threads, target_s=None, sc=None, narro
 
 
 def metric_name(args, E):
-    if args.scene == "ant" and args.narrow is None and args.semantics == "reference":
+    if args.scene == "ant" and args.narrow is None and args.semantics == "reference" and args.broad is None:
         return METRIC
     return f"env-steps/sec (whole box, {args.scene} {E} envs/GPU)"
 
 
 def workload_name(args):
     w = args.scene
+    if args.broad is not None:
+        w += f", broad phase {args.broad}"
     if args.narrow is not None:
         w += f", narrow phase {args.narrow}"
     if args.semantics != "reference":
@@ -287,6 +294,8 @@ def run_ours(args, rank, world_size, local_rank):
                             contact_iterations=sc["iters"], max_contacts_per_env=sc["M"], semantics=args.semantics)
     if args.narrow is not None:
         w.set_narrow_phase(args.narrow)
+    if args.broad is not None:
+        w.set_broad_phase(args.broad)
     if sc["task"]:
         w.set_task(auto_reset=True, seed=1, env_offset=shard_env_offset(rank, E), **sc["task"])
     # a dedicated stream: the world launches on it and the timing events record on it
@@ -366,6 +375,7 @@ def run_ours(args, rank, world_size, local_rank):
             "config": {"workload": workload_name(args), "envs_per_gpu": E, "substeps": sc["substeps"],
                        "contact_iterations": sc["iters"], "max_contacts_per_env": sc["M"], "timestep": st["timestep"],
                        "narrow_phase": w.get_narrow_phase(), "semantics": args.semantics,
+                       "broad_phase": w.get_broad_phase(),
                        "task": sc["task_text"],
                        "actions": f"U(-{sc['act']},{sc['act']}), resident in HBM" if A else "none",
                        "l2": "flushed (256 MiB write) between timed steps",
@@ -403,7 +413,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline sample")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end (host buffer) leg")
     ap.add_argument("--envs", type=int, default=0, help="environments per GPU (0: the workload's)")
-    ap.add_argument("--scene", choices=["ant", "humanoid", "collision_stress"], default="ant")
+    ap.add_argument("--scene", choices=["ant", "humanoid", "collision_stress", "sphere_pile"], default="ant")
+    ap.add_argument("--broad", type=int, choices=[0, 1, 2], default=None, help="broad phase (default: the world's)")
     ap.add_argument("--narrow", type=int, choices=[0, 1, 2], default=None, help="narrow phase (default: the world's)")
     ap.add_argument("--semantics", choices=["reference", "corrected"], default="reference")
     args = ap.parse_args()

@@ -211,6 +211,15 @@ int zeno_world_set_task(ZenoWorldHandle world, const ZenoTaskConfig* task);
 int zeno_world_set_narrow_phase(ZenoWorldHandle world, uint32_t mode);
 uint32_t zeno_world_get_narrow_phase(ZenoWorldHandle world);
 
+/* Broad phase of the general kernel (replaces the reference's choice at world.zig:534 and
+ * its racy spatial hash, all_shaders.metal:557-703).  0 (default): a hashed grid above 512
+ * geoms, else all candidate pairs; 1: all candidate pairs; 2: the grid.  The grid emits
+ * exactly the all-pairs sweep's slots, in its order (an environment whose geom centres are
+ * not finite, or more than 500 cells from the origin, is swept for that substep).  Returns
+ * 0, or -6 for another mode or when the grid's shared memory does not fit. */
+int zeno_world_set_broad_phase(ZenoWorldHandle world, uint32_t mode);
+uint32_t zeno_world_get_broad_phase(ZenoWorldHandle world);
+
 /* Launch shape of the step.  lanes 1 or 2: the compressed-state kernel with that many
  * lanes per environment and envs_per_block (1..32) environments per block; lanes 8, 16
  * or 32: the general kernel (lanes * envs_per_block <= 256, shared memory permitting).

@@ -451,3 +451,96 @@ def test_corrected_resting_contact_on_gpu():
     assert not diff_report(st, o.state())
     assert np.abs(st["velocities"][:, 1:, :3]).max() < 0.05
 
+
+
+# ---- grid broad phase (same slots as the all-candidate-pairs sweep) ----
+
+@pytest.mark.parametrize("name,mode,sem", [("ant", 0, "reference"), ("humanoid", 1, "reference"),
+                                           ("cartpole", 0, "reference"), ("ant", 2, "corrected"),
+                                           ("humanoid", 2, "corrected")])
+def test_grid_broad_phase_bit_exact(name, mode, sem):
+    """The general kernel with the hashed grid forced (broad phase 2) against the oracle's
+    all-pairs sweep, bit for bit."""
+    E = 4
+    w, o, c = make_pair(name, E, semantics=sem)
+    w.set_launch(8, 4)
+    w.set_narrow_phase(mode)
+    assert o.set_narrow_phase(mode) == 0
+    w.set_broad_phase(2)
+    assert w.get_broad_phase() == 2
+    rng = np.random.default_rng(23)
+    acts = actions(rng, 12, E, w.action_dim, c["act"])
+    for s in range(12):
+        w.step(acts[s])
+        o.step(acts[s])
+        bad = diff_report(product_state(w), o.state())
+        assert not bad, f"step {s}: {bad}"
+
+
+@pytest.mark.parametrize("sem", ["reference", "corrected"])
+def test_grid_drop_scene(sem):
+    xml = scenes.collision_stress(2)
+    kw = dict(num_envs=2, substeps=4, max_contacts_per_env=256, semantics=sem)
+    w, o = ZenoWorld(mjcf_string=xml, **kw), OracleWorld(xml, **kw)
+    w.set_narrow_phase(1)
+    o.set_narrow_phase(1)
+    w.set_broad_phase(2)
+    none = np.zeros((2, 0), np.float32)
+    for s in range(15):
+        w.step(none)
+        o.step(none)
+        bad = diff_report(product_state(w), o.state())
+        assert not bad, f"step {s}: {bad}"
+
+
+@pytest.mark.parametrize("sem", ["reference", "corrected"])
+def test_large_scene_uses_the_grid(sem):
+    """601 geoms (past the reference's 512-geom switch to its spatial hash): the default
+    broad phase is the grid; its slots equal the oracle's all-pairs sweep and the general
+    kernel's own sweep (broad phase 1)."""
+    xml = scenes.sphere_pile(0)
+    kw = dict(num_envs=2, substeps=4, max_contacts_per_env=1024, semantics=sem)
+    o = OracleWorld(xml, **kw)
+    if sem == "corrected":
+        o.set_narrow_phase(1)
+    runs = []
+    for bp in (0, 1):
+        w = ZenoWorld(mjcf_string=xml, **kw)
+        assert w.get_launch() == (32, 1)  # one warp per (large) environment
+        if sem == "corrected":
+            w.set_narrow_phase(1)
+        w.set_broad_phase(bp)
+        runs.append(w)
+    none = np.zeros((2, 0), np.float32)
+    for s in range(12):
+        for w in runs:
+            w.step(none)
+        o.step(none)
+        ref = o.state()
+        for w in runs:
+            bad = diff_report(product_state(w), ref)
+            assert not bad, f"step {s}, broad phase {w.get_broad_phase()}: {bad}"
+    assert product_state(runs[0])["contact_counts"].min() > 600
+
+
+def test_grid_falls_back_off_grid():
+    """A geom centre more than 500 cells from the origin sends that environment through
+    the all-pairs sweep for the substep; results stay identical to the oracle's."""
+    xml = ('<mujoco><option timestep="0.005"/><worldbody><geom type="plane" size="5 5 .1"/>'
+           '<body pos="0 0 0.3"><joint type="free"/><geom type="sphere" size="0.1"/></body>'
+           '<body pos="0.15 0 0.3"><joint type="free"/><geom type="sphere" size="0.1"/></body>'
+           '<body pos="0 0 0.55"><joint type="free"/><geom type="box" size="0.1 0.1 0.1"/></body>'
+           '<body pos="500 0 0.3"><joint type="free"/><geom type="sphere" size="0.1"/></body>'
+           '</worldbody></mujoco>')
+    kw = dict(num_envs=3, substeps=4, max_contacts_per_env=32)
+    w, o = ZenoWorld(mjcf_string=xml, **kw), OracleWorld(xml, **kw)
+    w.set_launch(8, 4)
+    w.set_narrow_phase(1)
+    o.set_narrow_phase(1)
+    w.set_broad_phase(2)
+    none = np.zeros((3, 0), np.float32)
+    for s in range(10):
+        w.step(none)
+        o.step(none)
+        bad = diff_report(product_state(w), o.state())
+        assert not bad, f"step {s}: {bad}"

@@ -95,6 +95,8 @@ ffi.cdef("""
     int zeno_world_set_task(ZenoWorldHandle world, const ZenoTaskConfig* task);
     int zeno_world_set_narrow_phase(ZenoWorldHandle world, uint32_t mode);
     uint32_t zeno_world_get_narrow_phase(ZenoWorldHandle world);
+    int zeno_world_set_broad_phase(ZenoWorldHandle world, uint32_t mode);
+    uint32_t zeno_world_get_broad_phase(ZenoWorldHandle world);
     int zeno_world_set_launch(ZenoWorldHandle world, int lanes, int envs_per_block);
     int zeno_world_get_launch(ZenoWorldHandle world, int* lanes, int* envs_per_block);
     const void* zeno_world_model_table(ZenoWorldHandle world, const char* name, uint64_t* nbytes);
@@ -439,6 +441,14 @@ class ZenoWorld:
 
     def get_narrow_phase(self) -> int:
         return int(_lib.zeno_world_get_narrow_phase(self._handle))
+
+    def set_broad_phase(self, mode: int) -> None:
+        """0: auto (grid above 512 geoms); 1: all candidate pairs; 2: hashed grid.  Same
+        slots either way."""
+        _check(_lib.zeno_world_set_broad_phase(self._handle, int(mode)), "Set broad phase")
+
+    def get_broad_phase(self) -> int:
+        return int(_lib.zeno_world_get_broad_phase(self._handle))
 
     def set_launch(self, lanes: int, envs_per_block: int) -> None:
         _check(_lib.zeno_world_set_launch(self._handle, lanes, envs_per_block), "Set launch")

@@ -279,6 +279,13 @@ int zeno_world_set_narrow_phase(ZenoWorldHandle world, uint32_t mode) {
 
 uint32_t zeno_world_get_narrow_phase(ZenoWorldHandle world) { return world ? W(world)->narrow_phase() : 0u; }
 
+int zeno_world_set_broad_phase(ZenoWorldHandle world, uint32_t mode) {
+  if (!world) return ZENO_INVALID_HANDLE;
+  return W(world)->set_broad_phase(mode);
+}
+
+uint32_t zeno_world_get_broad_phase(ZenoWorldHandle world) { return world ? W(world)->broad_phase() : 0u; }
+
 int zeno_world_set_task(ZenoWorldHandle world, const ZenoTaskConfig* t) {
   if (!world) return ZENO_INVALID_HANDLE;
   if (!t) return ZENO_INVALID_ARGUMENT;

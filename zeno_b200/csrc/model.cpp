@@ -191,8 +191,8 @@ bool build_model(const Scene& sc, HostModel* m, std::string* err) {
   h.G = uint32_t(sc.geoms.size());
   h.S = uint32_t(sc.sensors.size());
   h.obs_dim = sc.obs_dim();
-  if (h.B > 255 || h.G > 255) {
-    if (err) *err = "more than 255 bodies or geoms per environment";
+  if (h.B > 65535 || h.G > 65535) {
+    if (err) *err = "more than 65535 bodies or geoms per environment";
     return false;
   }
 
@@ -235,6 +235,30 @@ bool build_model(const Scene& sc, HostModel* m, std::string* err) {
     d.size12_fr_rest[2] = sg.friction, d.size12_fr_rest[3] = sg.restitution;
     d.type = sg.type, d.body = sg.body, d.contype = sg.contype, d.conaffinity = sg.conaffinity;
     h.geoms.push_back(d);
+  }
+  // distance-test radius per geom (size[0] in the reference; the whole-geom bound under
+  // corrected semantics) and the grid parameters: the cell edge exceeds every non-plane
+  // pair's distance bound (r_a + r_b) + 0.1 by 0.1 %, so pairs that pass the test lie in
+  // neighbouring cells; buckets: a power of two >= the grid geoms (and >= 32)
+  float r_max = 0.0f;
+  uint32_t n_grid = 0;
+  for (uint32_t g = 0; g < h.G; ++g) {
+    const SGeom& sg = sc.geoms[g];
+    const float r = sc.corrected ? bound_radius(sg) : sg.size[0];
+    h.geom_bound.push_back(r);
+    if (sg.type == 3) {
+      h.plane_geoms.push_back(g);
+    } else {
+      ++n_grid;
+      if (r > r_max) r_max = r;
+    }
+  }
+  {
+    const double cell = (2.0 * double(r_max) + 0.1) * 1.001;
+    h.grid_inv_cell = float(1.0 / cell);
+    uint32_t nb = 32;
+    while (nb < n_grid) nb <<= 1;
+    h.grid_buckets = nb;
   }
   // broad-phase candidates: static filters of all_shaders.metal:494-507, emission order
   for (uint32_t a = 0; a < h.G; ++a)

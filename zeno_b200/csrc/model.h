@@ -18,6 +18,11 @@ struct HostModel {
   std::vector<DJoint> joints;
   std::vector<DGeom> geoms;
   std::vector<DPair> pairs;
+  // grid broad phase: per-geom distance-test radius, plane geoms, cell edge and buckets
+  std::vector<float> geom_bound;
+  std::vector<uint32_t> plane_geoms;
+  float grid_inv_cell = 1.0f;
+  uint32_t grid_buckets = 32;
   std::vector<DActuator> actuators;
   std::vector<DSensor> sensors;
   std::vector<DConstraint> constraints;  // colour-sorted
@@ -31,8 +36,9 @@ struct HostModel {
 };
 
 // Builds every table.  Fails (returns false, fills *err) for models the kernel cannot
-// hold: more than 255 bodies or geoms per environment (contact slots pack the body and
-// geom indices into one byte each).
+// hold: more than 65535 bodies or geoms per environment (contact slots pack the body and
+// geom indices into 16 bits each).  Whether an environment fits the step kernel's shared
+// memory is decided when the world is created.
 bool build_model(const Scene& sc, HostModel* m, std::string* err);
 
 }  // namespace zb

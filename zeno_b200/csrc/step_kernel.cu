@@ -44,20 +44,24 @@ struct Plan {
   uint32_t pos, quat, vel, ang, ppos, pquat, frc, trq;  // float4[B]
   uint32_t jt, jp, jv;                                  // float[J]
   uint32_t cpp, cnf, cim;                               // float4[M] current slots (by storage index)
-  uint32_t cpk;                                         // u32[M] packed body/geom indices
+  uint32_t cpk;                                         // uint2[M] packed body/geom indices
   uint32_t ppp, pim, ppk;                               // prev snapshot (slot order)
   uint32_t ord, sched, sidx, slev;                      // u16[M] each
   uint32_t lvl, lcur;                                   // u16[M+1] each
   uint32_t blev;                                        // u16[B]
   uint32_t flags;                                       // u32
+  uint32_t gcen, gcell, bkt, blist, bits;               // grid broad phase (when used)
   uint32_t bytes;
 };
 
-__host__ __device__ inline Plan make_plan(uint32_t B, uint32_t J, uint32_t M) {
+// Gg, NB: geoms and hash buckets of the grid broad phase (0 when it does not run);
+// L: lanes per environment (one candidate bitmask row of ceil(Gg/32) words per lane).
+__host__ __device__ inline Plan make_plan(uint32_t B, uint32_t J, uint32_t M, uint32_t Gg, uint32_t NB,
+                                          uint32_t L) {
   Plan p;
   uint32_t o = 0;
   const uint32_t b4 = align16(16u * B), j1 = align16(4u * (J > 0 ? J : 1)), m4 = align16(16u * M);
-  const uint32_t m1 = align16(4u * M), h1 = align16(2u * M), h2 = align16(2u * (M + 1)), bb = align16(2u * B);
+  const uint32_t m1 = align16(8u * M), h1 = align16(2u * M), h2 = align16(2u * (M + 1)), bb = align16(2u * B);
   p.pos = o; o += b4;
   p.quat = o; o += b4;
   p.vel = o; o += b4;
@@ -84,26 +88,54 @@ __host__ __device__ inline Plan make_plan(uint32_t B, uint32_t J, uint32_t M) {
   p.lcur = o; o += h2;
   p.blev = o; o += bb;
   p.flags = o; o += 16;
+  p.gcen = o; o += align16(16u * Gg);
+  p.gcell = o; o += align16(4u * Gg);
+  p.bkt = o; o += align16(4u * NB);
+  p.blist = o; o += align16(2u * Gg);
+  p.bits = o; o += align16(4u * L * ((Gg + 31u) >> 5));
   p.bytes = o;
   return p;
 }
 
-uint32_t env_smem_bytes(uint32_t B, uint32_t J, uint32_t M) { return make_plan(B, J, M).bytes; }
+uint32_t env_smem_bytes(uint32_t B, uint32_t J, uint32_t M, uint32_t grid_geoms, uint32_t grid_buckets,
+                        uint32_t lanes) {
+  return make_plan(B, J, M, grid_geoms, grid_buckets, lanes).bytes;
+}
 
-__device__ __forceinline__ uint32_t pack4(uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
-  return a | (b << 8) | (c << 16) | (d << 24);
+// ---- grid broad phase helpers ----
+// Cell coordinates are floor(centre / cell) + 512, packed 10 bits each; centres beyond
+// kGridSpan cells from the origin (or not finite) make the environment fall back to the
+// all-pairs sweep for that substep.  Within the span, float rounding of centre/cell
+// stays below 3e-5 cells, well inside the cell edge's 1e-3 margin over the largest
+// pair distance bound, so every pair that passes the distance test lies in neighbouring
+// cells.
+constexpr float kGridSpan = 500.0f;
+constexpr uint32_t kNoCell = 0xFFFFFFFFu;
+__device__ __forceinline__ uint32_t cell_hash(uint32_t cx, uint32_t cy, uint32_t cz) {
+  return (cx * 73856093u) ^ (cy * 19349663u) ^ (cz * 83492791u);
+}
+// The static filters of the reference broad phase (all_shaders.metal:494-507).
+__device__ __forceinline__ bool pair_filter(const DGeom& ga, const DGeom& gb) {
+  if (__ldg(&ga.body) == __ldg(&gb.body)) return false;
+  return (__ldg(&ga.contype) & __ldg(&gb.conaffinity)) != 0u || (__ldg(&gb.contype) & __ldg(&ga.conaffinity)) != 0u;
+}
+
+// A slot's indices: bodies a | b << 16, geoms ga | gb << 16 (up to 65535 of each).
+typedef uint2 Pk;
+__device__ __forceinline__ Pk pack4(uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  return make_uint2(a | (b << 16), c | (d << 16));
 }
 // Slot indices read back from HBM are trusted only within the model's bounds (the
 // contacts buffer is host-writable through the ABI); out-of-range values become 0.
-__device__ __forceinline__ uint32_t pack_checked(uint4 ix, uint32_t B, uint32_t G) {
+__device__ __forceinline__ Pk pack_checked(uint4 ix, uint32_t B, uint32_t G) {
   return pack4(ix.x < B ? ix.x : 0u, ix.y < B ? ix.y : 0u, ix.z < G ? ix.z : 0u, ix.w < G ? ix.w : 0u);
 }
-__device__ __forceinline__ uint32_t pk_a(uint32_t k) { return k & 0xFFu; }
-__device__ __forceinline__ uint32_t pk_b(uint32_t k) { return (k >> 8) & 0xFFu; }
-__device__ __forceinline__ uint32_t pk_ga(uint32_t k) { return (k >> 16) & 0xFFu; }
-__device__ __forceinline__ uint32_t pk_gb(uint32_t k) { return k >> 24; }
+__device__ __forceinline__ uint32_t pk_a(Pk k) { return k.x & 0xFFFFu; }
+__device__ __forceinline__ uint32_t pk_b(Pk k) { return k.x >> 16; }
+__device__ __forceinline__ uint32_t pk_ga(Pk k) { return k.y & 0xFFFFu; }
+__device__ __forceinline__ uint32_t pk_gb(Pk k) { return k.y >> 16; }
 // sort_contacts key: min(body) << 16 | max(body)
-__device__ __forceinline__ uint32_t pk_key(uint32_t k) {
+__device__ __forceinline__ uint32_t pk_key(Pk k) {
   uint32_t a = pk_a(k), b = pk_b(k);
   return ((a < b ? a : b) << 16) | (a < b ? b : a);
 }
@@ -125,7 +157,7 @@ struct ArrBodies {
 // Narrow phase for one slot (narrow_phase, all_shaders.metal:751-894; mode 1: the
 // reference's CPU detectCollision, src/collision/narrow_phase.zig:28-136; mode 2: as 1,
 // with GJK + EPA, src/collision/gjk.zig, for box-capsule pairs)
-__device__ __forceinline__ void narrow(uint32_t pk, const DGeom* geoms, const float4* pos, const float4* quat,
+__device__ __forceinline__ void narrow(Pk pk, const DGeom* geoms, const float4* pos, const float4* quat,
                                        uint32_t mode, uint32_t corrected, float restitution, float4& cpp, float4& cnf,
                                        float4& cim) {
   const DGeom& gA = geoms[pk_ga(pk)];
@@ -213,6 +245,155 @@ __device__ void reset_env_noise(const StepArgs& a, uint32_t e, float4* pos, floa
   }
 }
 
+// Grid broad phase of one environment: the all-pairs sweep's slots, in its order, for
+// one substep.  Returns the new contact count, or kNoCell when a geom centre is off the
+// grid (the caller then runs the sweep).  Kept out of line so that its registers do not
+// add to the step kernel's.
+struct GridIn {
+  const DGeom* geoms;
+  const float* geom_bound;
+  const uint32_t* plane_geoms;
+  const float4* pos;
+  const float4* quat;
+  float4* gcen;
+  uint32_t* gcell;
+  uint32_t* bkt;
+  uint16_t* blist;
+  uint32_t* bits;
+  Pk* cpk;
+  const uint16_t* ord;
+  uint32_t G, NB, M, num_planes, corrected;
+  float inv_cell;
+};
+
+template <int L>
+__device__ __noinline__ uint32_t grid_broad_phase(GridIn in, uint32_t count, uint32_t l) {
+  const unsigned gmask = L == 32 ? 0xFFFFFFFFu : (((1u << L) - 1u) << ((threadIdx.x & 31u) & ~(L - 1u)));
+  const uint32_t gshift = (threadIdx.x & 31u) & ~(L - 1u);
+  const uint32_t NB = in.NB, G = in.G, M = in.M;
+  // geom centres and cells (planes stay out of the grid: they pair with everything)
+  bool off_grid = false;
+  for (uint32_t g = l; g < G; g += L) {
+    const DGeom& gd = in.geoms[g];
+    const uint32_t bg = __ldg(&gd.body);
+    const float4 lp = __ldg(reinterpret_cast<const float4*>(gd.pos_size0));
+    const V3 c = in.corrected ? geom_centre(in.pos[bg], in.quat[bg], lp) : v3(in.pos[bg]) + v3(lp);
+    in.gcen[g] = make_float4(c.x, c.y, c.z, __ldg(&in.geom_bound[g]));
+    uint32_t cell = kNoCell;
+    if (__ldg(&gd.type) != 3u) {
+      const float ux = c.x * in.inv_cell, uy = c.y * in.inv_cell, uz = c.z * in.inv_cell;
+      if (fabsf(ux) < kGridSpan && fabsf(uy) < kGridSpan && fabsf(uz) < kGridSpan) {  // false for NaN
+        cell = uint32_t(int(floorf(ux)) + 512) | (uint32_t(int(floorf(uy)) + 512) << 10) |
+               (uint32_t(int(floorf(uz)) + 512) << 20);
+      } else {
+        off_grid = true;
+      }
+    }
+    in.gcell[g] = cell;
+  }
+  if (__any_sync(gmask, off_grid)) return kNoCell;
+  __syncwarp(gmask);
+
+  // counting sort of the grid geoms by bucket: counts, exclusive scan, scatter; bucket k
+  // then holds blist[k ? bkt[k-1] : 0, bkt[k])
+  for (uint32_t k = l; k < NB; k += L) in.bkt[k] = 0;
+  __syncwarp(gmask);
+  for (uint32_t g = l; g < G; g += L) {
+    const uint32_t c = in.gcell[g];
+    if (c != kNoCell) atomicAdd(&in.bkt[cell_hash(c & 1023u, (c >> 10) & 1023u, c >> 20) & (NB - 1u)], 1u);
+  }
+  __syncwarp(gmask);
+  {
+    const uint32_t chunk = (NB + L - 1) / L, k0 = min(l * chunk, NB), k1 = min(k0 + chunk, NB);
+    uint32_t s = 0;
+    for (uint32_t k = k0; k < k1; ++k) s += in.bkt[k];
+    uint32_t incl = s;
+    for (uint32_t d = 1; d < L; d <<= 1) {
+      const uint32_t t = __shfl_up_sync(gmask, incl, d, L);
+      if (l >= d) incl += t;
+    }
+    uint32_t run = incl - s;
+    for (uint32_t k = k0; k < k1; ++k) {
+      const uint32_t c = in.bkt[k];
+      in.bkt[k] = run;
+      run += c;
+    }
+  }
+  __syncwarp(gmask);
+  for (uint32_t g = l; g < G; g += L) {
+    const uint32_t c = in.gcell[g];
+    if (c != kNoCell) {
+      const uint32_t p = atomicAdd(&in.bkt[cell_hash(c & 1023u, (c >> 10) & 1023u, c >> 20) & (NB - 1u)], 1u);
+      in.blist[p] = uint16_t(g);
+    }
+  }
+  __syncwarp(gmask);
+
+  // geom a = r0 + l per round: mark every passing b > a in the lane's bitmask, then emit
+  // the set bits in ascending b at the lane's prefix offset, which reproduces the
+  // all-pairs emission order (a ascending, then b ascending)
+  const uint32_t W = (G + 31u) >> 5;
+  uint32_t* mine = in.bits + l * W;
+  for (uint32_t r0 = 0; r0 < G; r0 += L) {
+    const uint32_t ga = r0 + l;
+    uint32_t n_my = 0;
+    if (ga < G) {
+      for (uint32_t w = 0; w < W; ++w) mine[w] = 0u;
+      const DGeom& gA = in.geoms[ga];
+      if (__ldg(&gA.type) == 3u) {  // a plane pairs with every later geom that passes the filters
+        for (uint32_t gb = ga + 1; gb < G; ++gb)
+          if (pair_filter(gA, in.geoms[gb])) mine[gb >> 5] |= 1u << (gb & 31u);
+      } else {
+        for (uint32_t p = 0; p < in.num_planes; ++p) {
+          const uint32_t gb = __ldg(&in.plane_geoms[p]);
+          if (gb > ga && pair_filter(gA, in.geoms[gb])) mine[gb >> 5] |= 1u << (gb & 31u);
+        }
+        const float4 pa4 = in.gcen[ga];
+        const V3 pa = v3(pa4);
+        const uint32_t ca = in.gcell[ga];
+        const uint32_t cx = ca & 1023u, cy = (ca >> 10) & 1023u, cz = ca >> 20;
+        for (int dz = -1; dz <= 1; ++dz)
+          for (int dy = -1; dy <= 1; ++dy)
+            for (int dx = -1; dx <= 1; ++dx) {
+              const uint32_t k = cell_hash(cx + dx, cy + dy, cz + dz) & (NB - 1u);
+              const uint32_t i1 = in.bkt[k];
+              for (uint32_t i = k ? in.bkt[k - 1] : 0u; i < i1; ++i) {
+                const uint32_t gb = in.blist[i];
+                if (gb <= ga || !pair_filter(gA, in.geoms[gb])) continue;
+                const float4 pb4 = in.gcen[gb];
+                const V3 d = v3(pb4) - pa;
+                const float md = (pa4.w + pb4.w) + 0.1f;
+                if (!(dot(d, d) >= md * md)) mine[gb >> 5] |= 1u << (gb & 31u);
+              }
+            }
+      }
+      for (uint32_t w = (ga + 1) >> 5; w < W; ++w) n_my += __popc(mine[w]);
+    }
+    uint32_t incl = n_my;
+    for (uint32_t d = 1; d < L; d <<= 1) {
+      const uint32_t t = __shfl_up_sync(gmask, incl, d, L);
+      if (l >= d) incl += t;
+    }
+    const uint32_t total = __shfl_sync(gmask, incl, gshift + L - 1);
+    if (n_my != 0) {
+      uint32_t slot = count + (incl - n_my);
+      const uint32_t ba = __ldg(&in.geoms[ga].body);
+      for (uint32_t w = (ga + 1) >> 5; w < W && slot < M; ++w) {
+        uint32_t m = mine[w];
+        while (m != 0u && slot < M) {
+          const uint32_t gb = (w << 5) + uint32_t(__ffs(m) - 1);
+          m &= m - 1u;
+          in.cpk[in.ord[slot]] = pack4(ba, __ldg(&in.geoms[gb].body), ga, gb);
+          ++slot;
+        }
+      }
+    }
+    count += total;
+  }
+  __syncwarp(gmask);
+  return count;
+}
+
 // ------------------------------------------------------------------------------------
 // One environment, stepped by the L lanes of group g (syncs are group-local).
 // ------------------------------------------------------------------------------------
@@ -224,7 +405,7 @@ __device__ __forceinline__ void step_env(const StepArgs& a, uint32_t e, unsigned
   const ModelG mg{a.bodies, a.constraints};
 
   const uint32_t B = a.B, J = a.J, A = a.A, M = a.M;
-  const Plan P = make_plan(B, J, M);
+  const Plan P = make_plan(B, J, M, a.broad_grid ? a.G : 0u, a.broad_grid ? a.grid_buckets : 0u, L);
   unsigned char* base = smem_raw + size_t(g) * P.bytes;
   float4* pos = sm<float4>(base, P.pos);
   float4* quat = sm<float4>(base, P.quat);
@@ -240,10 +421,10 @@ __device__ __forceinline__ void step_env(const StepArgs& a, uint32_t e, unsigned
   float4* cpp = sm<float4>(base, P.cpp);
   float4* cnf = sm<float4>(base, P.cnf);
   float4* cim = sm<float4>(base, P.cim);
-  uint32_t* cpk = sm<uint32_t>(base, P.cpk);
+  Pk* cpk = sm<Pk>(base, P.cpk);
   float4* ppp = sm<float4>(base, P.ppp);
   float4* pim = sm<float4>(base, P.pim);
-  uint32_t* ppk = sm<uint32_t>(base, P.ppk);
+  Pk* ppk = sm<Pk>(base, P.ppk);
   uint16_t* ord = sm<uint16_t>(base, P.ord);
   uint16_t* sched = sm<uint16_t>(base, P.sched);
   uint16_t* sidx = sm<uint16_t>(base, P.sidx);
@@ -252,6 +433,11 @@ __device__ __forceinline__ void step_env(const StepArgs& a, uint32_t e, unsigned
   uint16_t* lcur = sm<uint16_t>(base, P.lcur);
   uint16_t* blev = sm<uint16_t>(base, P.blev);
   uint32_t* flags = sm<uint32_t>(base, P.flags);
+  float4* gcen = sm<float4>(base, P.gcen);
+  uint32_t* gcell = sm<uint32_t>(base, P.gcell);
+  uint32_t* bkt = sm<uint32_t>(base, P.bkt);
+  uint16_t* blist = sm<uint16_t>(base, P.blist);
+  uint32_t* bits = sm<uint32_t>(base, P.bits);
   ArrBodies bodies{pos, quat, vel, ang};
 
   // ---------------- load the environment ----------------
@@ -379,7 +565,15 @@ __device__ __forceinline__ void step_env(const StepArgs& a, uint32_t e, unsigned
     // grows, so its list freezes with duplicates once M candidates were emitted)
     if (a.corrected) count = 0;
     const uint32_t count0 = count;
-    for (uint32_t r = 0; r < a.num_pairs; r += L) {
+    bool grid = false;
+    if (a.broad_grid) {
+      const GridIn gi{a.geoms, a.geom_bound, a.plane_geoms, pos, quat, gcen, gcell, bkt, blist, bits, cpk, ord,
+                      a.G, a.grid_buckets, M, a.num_planes, a.corrected, a.grid_inv_cell};
+      const uint32_t c = grid_broad_phase<L>(gi, count, l);
+      grid = c != kNoCell;
+      if (grid) count = c;
+    }
+    for (uint32_t r = 0; r < (grid ? 0u : a.num_pairs); r += L) {
       const uint32_t p = r + l;
       bool pass = false;
       uint32_t ga = 0, gb = 0, ba = 0, bb = 0;
@@ -590,7 +784,8 @@ __device__ __forceinline__ void step_env(const StepArgs& a, uint32_t e, unsigned
     if (stepped) {
       Contact* pc = a.prev_contacts + size_t(e) * M;
       for (uint32_t i = l; i < n_fin; i += L) {
-        const uint32_t st = ord[i], k = cpk[st];
+        const uint32_t st = ord[i];
+        const Pk k = cpk[st];
         float4* dst = reinterpret_cast<float4*>(pc + i);
         dst[0] = cpp[st];
         dst[1] = cnf[st];
@@ -614,7 +809,8 @@ __device__ __forceinline__ void step_env(const StepArgs& a, uint32_t e, unsigned
   // ---- contacts back to HBM (slot order) ----
   const uint32_t n_out = n_hi > n_fin ? n_hi : n_fin;
   for (uint32_t i = l; i < n_out; i += L) {
-    const uint32_t st = ord[i], k = cpk[st];
+    const uint32_t st = ord[i];
+    const Pk k = cpk[st];
     float4* dst = reinterpret_cast<float4*>(gcw + i);
     dst[0] = cpp[st];
     dst[1] = cnf[st];
@@ -710,7 +906,8 @@ __global__ void __launch_bounds__(256) step_kernel(StepArgs a) {
 // ------------------------------------------------------------------------------------
 cudaError_t launch_step(const StepArgs& args, int lanes, int envs_per_block, cudaStream_t stream) {
   if (args.num_envs == 0) return cudaSuccess;
-  const uint32_t env_bytes = env_smem_bytes(args.B, args.J, args.M);
+  const uint32_t env_bytes = env_smem_bytes(args.B, args.J, args.M, args.broad_grid ? args.G : 0u,
+                                            args.broad_grid ? args.grid_buckets : 0u, uint32_t(lanes));
   const uint32_t threads = uint32_t(lanes * envs_per_block);
   const uint32_t full = (args.num_envs + envs_per_block - 1) / envs_per_block;
   // list mode: enough blocks for one group per SM sub-partition, strided over the list

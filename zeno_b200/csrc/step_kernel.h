@@ -10,8 +10,10 @@
 
 namespace zb {
 
-// Shared memory one environment needs for the whole step (general kernel).
-uint32_t env_smem_bytes(uint32_t B, uint32_t J, uint32_t M);
+// Shared memory one environment needs for the whole step (general kernel).  grid_geoms
+// and grid_buckets are 0 unless the grid broad phase runs; lanes: threads per environment.
+uint32_t env_smem_bytes(uint32_t B, uint32_t J, uint32_t M, uint32_t grid_geoms = 0, uint32_t grid_buckets = 0,
+                        uint32_t lanes = 8);
 
 // General kernel: run args.substeps substeps on `stream`, for all args.num_envs
 // environments, or (args.env_list set) for the *args.env_count listed ones.

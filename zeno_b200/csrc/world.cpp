@@ -73,12 +73,19 @@ World* World::create(const Scene& sc, const WorldConfig& cfg, std::string* err) 
   if (M > 65535) return fail("max_contacts_per_env above 65535", w);
 
   // general kernel shape: 8 lanes per env, 4 envs per block (small blocks pack the SM's
-  // shared memory tightly and balance the tail wave better)
-  const uint32_t env_bytes = env_smem_bytes(B, m.J, M);
+  // shared memory tightly and balance the tail wave better); an environment too large
+  // for two per block gets a whole warp
   const int smem_cap = opt_in_smem(w->device_);
-  if (env_bytes > uint32_t(smem_cap)) return fail("model does not fit in shared memory (reduce max_contacts_per_env)", w);
-  w->lanes_ = 8;
-  w->envs_per_block_ = int(std::min<uint32_t>(4u, uint32_t(smem_cap) / env_bytes));
+  const uint32_t env_bytes = w->general_env_bytes(8);
+  if (2 * uint64_t(env_bytes) > uint64_t(smem_cap)) {
+    if (w->general_env_bytes(32) > uint32_t(smem_cap))
+      return fail("model does not fit in shared memory (reduce max_contacts_per_env)", w);
+    w->lanes_ = 32;
+    w->envs_per_block_ = 1;
+  } else {
+    w->lanes_ = 8;
+    w->envs_per_block_ = int(std::min<uint32_t>(4u, uint32_t(smem_cap) / env_bytes));
+  }
   // environment-per-lane kernel when the model packs into its fixed-capacity tables
   std::string why;
   if (m.corrected) w->narrow_mode_ = 2;  // corrected semantics use the CPU routines + GJK
@@ -124,6 +131,8 @@ World* World::create(const Scene& sc, const WorldConfig& cfg, std::string* err) 
   upload(&w->d_colors_, m.color_ranges);
   upload(&w->d_subtree_, m.subtree);
   upload(&w->d_init_, m.init_state);
+  upload(&w->d_bound_, m.geom_bound);
+  upload(&w->d_planes_, m.plane_geoms);
   if (w->fast_ok_) {
     upload(&w->d_hot_, w->hot_image_);
     w->hot_capacity_ = w->hot_image_.size();
@@ -196,6 +205,9 @@ StepArgs World::args(uint32_t substeps, const float* actions, const uint8_t* mas
   a.actuators_unique = m.actuators_unique ? 1u : 0u;
   a.narrow_mode = narrow_mode_;
   a.corrected = model_.corrected ? 1u : 0u;
+  a.broad_grid = grid_on() ? 1u : 0u;
+  a.grid_buckets = m.grid_buckets, a.grid_inv_cell = m.grid_inv_cell;
+  a.num_planes = uint32_t(m.plane_geoms.size()), a.plane_geoms = d_planes_, a.geom_bound = d_bound_;
   a.dt = timestep_ / float(substeps > 1 ? substeps : 1u);  // world.zig:699-702
   a.inv_dt = 1.0f / a.dt;
   a.inv_step = timestep_ > 0 ? 1.0f / timestep_ : 0.0f;  // world.zig:736
@@ -403,7 +415,7 @@ int World::set_launch(int lanes, int envs_per_block) {
     return 0;
   }
   if (lanes != 8 && lanes != 16 && lanes != 32) return -6;
-  const uint32_t env_bytes = env_smem_bytes(model_.B, model_.J, cfg_.max_contacts_per_env);
+  const uint32_t env_bytes = general_env_bytes(lanes);
   if (envs_per_block < 1 || lanes * envs_per_block > 256 ||
       uint64_t(env_bytes) * envs_per_block > uint64_t(opt_in_smem(device_)))
     return -6;
@@ -412,6 +424,30 @@ int World::set_launch(int lanes, int envs_per_block) {
   use_fast_ = false;
   prefer_general_ = true;
   return 0;
+}
+
+uint32_t World::general_env_bytes(int lanes) const {
+  const bool g = grid_on();
+  return env_smem_bytes(model_.B, model_.J, cfg_.max_contacts_per_env, g ? model_.G : 0u,
+                        g ? model_.grid_buckets : 0u, uint32_t(lanes));
+}
+
+// Selects the broad phase of the general kernel.  The grid adds per-environment shared
+// memory; when the current shape no longer fits, one environment per warp is tried.
+int World::set_broad_phase(uint32_t mode) {
+  if (mode > 2) return -6;
+  if (cudaStreamSynchronize(stream_) != cudaSuccess) return -4;
+  const uint32_t old = broad_mode_;
+  broad_mode_ = mode;
+  const uint64_t cap = uint64_t(opt_in_smem(device_));
+  if (uint64_t(general_env_bytes(lanes_)) * uint64_t(envs_per_block_) <= cap) return 0;
+  if (general_env_bytes(32) <= cap) {
+    lanes_ = 32;
+    envs_per_block_ = 1;
+    return 0;
+  }
+  broad_mode_ = old;
+  return -6;
 }
 
 // Selects the narrow phase and re-packs the compressed-state model (its hittable pairs

@@ -54,9 +54,16 @@ class World {
   // 0: the reference's GPU narrow phase (default); 1: its CPU detectCollision routines.
   int set_narrow_phase(uint32_t mode);
   uint32_t narrow_phase() const { return narrow_mode_; }
+  // Broad phase: 0 auto (the grid above 512 geoms, as the reference switches to its
+  // spatial hash), 1 all candidate pairs, 2 grid.  Both give the same slots.
+  int set_broad_phase(uint32_t mode);
+  uint32_t broad_phase() const { return broad_mode_; }
+  bool grid_on() const { return broad_mode_ == 2 || (broad_mode_ == 0 && model_.G > 512); }
   // lanes 1, 2: compressed-state kernel with that many lanes per environment and
   // envs_per_block (1..32) environments per block; lanes 8, 16, 32: general kernel only.
   // -6 when the shape is invalid or unsupported.
+  // Shared memory of one environment in the general kernel with `lanes` lanes.
+  uint32_t general_env_bytes(int lanes) const;
   int set_launch(int lanes, int envs_per_block);
   cudaError_t synchronize();
   void set_stream(cudaStream_t s) { stream_ = s ? s : own_stream_; }
@@ -116,6 +123,7 @@ class World {
   uint8_t* d_hot_ = nullptr;
   size_t hot_capacity_ = 0;
   uint32_t narrow_mode_ = 0;
+  uint32_t broad_mode_ = 0;
   float4* pose_scratch_ = nullptr;
   uint64_t bytes_ = 0;
   cudaStream_t own_stream_ = nullptr;
@@ -134,6 +142,8 @@ class World {
   uint32_t* d_colors_ = nullptr;
   uint32_t* d_subtree_ = nullptr;
   float* d_init_ = nullptr;
+  float* d_bound_ = nullptr;
+  uint32_t* d_planes_ = nullptr;
   // internal state
   uint32_t* prev_counts_ = nullptr;
   Contact* prev_contacts_ = nullptr;

@@ -104,6 +104,13 @@ struct StepArgs {
   uint32_t narrow_mode;       // 0: reference GPU narrow phase; 1: its CPU detectCollision;
                               // 2: as 1 plus GJK + EPA for box-capsule pairs
   uint32_t corrected;         // 1: corrected semantics (geom frames, bounds, B->A normals)
+  // grid broad phase (same pairs, in the same order, as the all-pairs sweep)
+  uint32_t broad_grid;        // 1: hashed grid; 0: all candidate pairs
+  uint32_t grid_buckets;      // power of two
+  float grid_inv_cell;        // 1 / cell edge (cell edge >= largest pair distance bound)
+  uint32_t num_planes;
+  const uint32_t* plane_geoms;  // plane geoms, ascending
+  const float* geom_bound;      // per geom: the radius of the broad-phase distance test
   float dt, inv_dt, inv_step;  // dt = timestep/substeps, inv_dt = 1/dt, inv_step = 1/timestep
   float gravity[3];
   float baumgarte, slop, restitution;

@@ -260,6 +260,32 @@ def collision_stress(seed: int = 0, n_spheres: int = 32, n_capsules: int = 16, n
             + "\n".join(parts) + '\n  </worldbody>\n</mujoco>\n')
 
 
+def sphere_pile(seed: int = 0, n: int = 600, extent: float = 1.5, height: float = 1.0) -> str:
+    """Seeded large scene past the reference's spatial-hash threshold (more than 512 geoms):
+    n free spheres r~U(.03,.06) on a jittered lattice over a 2*extent square, stacked from
+    0.1 m to `height`, a few overlapping their neighbours, above a ground plane; dt 0.005."""
+    rng = np.random.default_rng(seed)
+    side = int(np.ceil(np.sqrt(n / 4)))
+    layers = int(np.ceil(n / (side * side)))
+    parts = []
+    k = 0
+    for i in range(side):
+        for j in range(side):
+            for h in range(layers):
+                if k >= n:
+                    break
+                x = -extent + (i + 0.5) * 2 * extent / side + rng.uniform(-0.02, 0.02)
+                y = -extent + (j + 0.5) * 2 * extent / side + rng.uniform(-0.02, 0.02)
+                z = 0.1 + h * (height - 0.1) / max(layers - 1, 1) + rng.uniform(-0.02, 0.02)
+                r = rng.uniform(0.03, 0.06)
+                k += 1
+                parts.append(f'    <body name="s{k}" pos="{x:.6f} {y:.6f} {z:.6f}">\n      <joint type="free"/>\n'
+                             f'      <geom type="sphere" size="{r:.6f}" friction="0.8 0.005 0.0001"/>\n    </body>')
+    return ('<mujoco model="sphere_pile">\n  <option timestep="0.005" gravity="0 0 -9.81"/>\n'
+            '  <worldbody>\n    <geom type="plane" size="20 20 0.1" friction="0.8 0.005 0.0001"/>\n'
+            + "\n".join(parts) + '\n  </worldbody>\n</mujoco>\n')
+
+
 BY_NAME = {
     "ant": ant,
     "humanoid": humanoid,
