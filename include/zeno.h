@@ -269,6 +269,12 @@ ZenoWorldHandle zeno_world_create_ex(const char* mjcf_path, const ZenoConfig* co
 ZenoWorldHandle zeno_world_create_from_string_ex(const char* mjcf_string, const ZenoConfig* config,
                                                  uint32_t semantics);
 
+/* Diagnostic (no counterpart in the reference): evaluates one of the step kernels'
+ * canonical scalar functions on the current GPU for n host values, results into out.
+ * fn 0: rsq_(x), 1: rcp_(x), 2: atan2r(x, y), 3: asinr(x), 4: len((x, y, x/2)).  y is
+ * needed for fn 2 and 4.  Returns 0, -6 for a bad argument, -4 for a CUDA error. */
+int zeno_eval_math(uint32_t fn, const float* x, const float* y, float* out, uint64_t n);
+
 /* Host-only model build (no GPU needed): parse MJCF text and build the model tables;
  * zeno_model_table takes the same names as zeno_world_model_table. */
 void* zeno_model_create_from_string(const char* mjcf_string);

@@ -195,6 +195,23 @@ int zo_gjk_epa(const float* geom_a, const float* body_a, const float* geom_b, co
   return gjk_epa_query(ga, body_a, body_a + 3, gb, body_b, body_b + 3, out);
 }
 float zo_asin(float x) { return zo::asin_r(x); }
+// The oracle's canonical scalar functions over an array (same numbering as the product's
+// zeno_eval_math): 0 rsq_r, 1 rcp_r, 2 atan2_r(x, y), 3 asin_r, 4 length((x, y, x/2)).
+int zo_eval_math(uint32_t fn, const float* x, const float* y, float* out, uint64_t n) {
+  using namespace zo;
+  if (fn > 4 || !x || !out || ((fn == 2 || fn == 4) && !y)) return -6;
+  for (uint64_t i = 0; i < n; ++i) {
+    const float a = x[i];
+    switch (fn) {
+      case 0: out[i] = rsq_r(a); break;
+      case 1: out[i] = rcp_r(a); break;
+      case 2: out[i] = atan2_r(a, y[i]); break;
+      case 3: out[i] = asin_r(a); break;
+      default: out[i] = length(F3{a, y[i], 0.5f * a}); break;
+    }
+  }
+  return 0;
+}
 // Generalised inverse mass of a contact or positional constraint, the expression the
 // solvers use (all_shaders.metal:1683-1687; xpbd.zig:495-529 computeEffectiveMass):
 // w = 1/m_a + (r_a x n)^T I_a^-1 (r_a x n) + 1/m_b + (r_b x n)^T I_b^-1 (r_b x n)

@@ -5,18 +5,57 @@
 // Metal compute kernels compiled with the Metal compiler's default (fast-math) options
 // (src/metal/device.zig:51-56 passes no compile options), so its exact rounding is
 // unspecified.  The oracle therefore fixes ONE evaluation order: every vector helper
-// below is written with explicit fused multiply-adds and IEEE-754 correctly rounded
-// +,-,*,/,sqrt only.  The CUDA kernel evaluates the same expressions in the same order
-// (built with -fmad=false, so nvcc adds no contractions of its own), which makes the
-// oracle and the GPU bit-identical.  This file is built with -ffp-contract=off.
+// below is written with explicit fused multiply-adds, IEEE-754 correctly rounded +,-,*,
+// and reciprocals / reciprocal square roots built from those by Newton-Raphson (rsq_r,
+// rcp_r).  The CUDA kernel evaluates the same expressions in the same order (built with
+// -fmad=false, so nvcc adds no contractions of its own), which makes the oracle and the
+// GPU bit-identical.  This file is built with -ffp-contract=off.
 #pragma once
 #include <cmath>
 #include <cstdint>
+#include <cstring>
 
 namespace zo {
 
 struct F3 { float x, y, z; };
 struct F4 { float x, y, z, w; };
+
+// Reciprocal square root and reciprocal by Newton-Raphson from a bit-pattern initial
+// guess, residual form, three iterations each (within 1 ulp), from fused multiply-adds and
+// products only:
+//   rsq_r: y0 from 0x5f375a86 - (bits(x) >> 1) (Lomont, "Fast inverse square root",
+//          2003); e = 1 - (x y) y, y = y + (y/2) e; for finite x > 0 (rsq_r(0) is a large
+//          finite value, so |v| = d rsq_r(d) is exactly 0 for d = 0);
+//   rcp_r: y0 = +-float(0x7ef311c3 - bits(|x|)) (exponent negation); e = 1 - x y,
+//          y = y + y e; for finite x != 0 with |x| < 2^125.
+// Outside those domains the results are unspecified but deterministic; the step discards
+// them through its guards.
+static inline uint32_t bits_of(float x) {
+  uint32_t u;
+  std::memcpy(&u, &x, 4);
+  return u;
+}
+static inline float float_of(uint32_t u) {
+  float x;
+  std::memcpy(&x, &u, 4);
+  return x;
+}
+static inline float rsq_r(float x) {
+  float y = float_of(0x5f375a86u - (bits_of(x) >> 1));
+  y = std::fmaf(0.5f * y, std::fmaf(-(x * y), y, 1.0f), y);
+  y = std::fmaf(0.5f * y, std::fmaf(-(x * y), y, 1.0f), y);
+  y = std::fmaf(0.5f * y, std::fmaf(-(x * y), y, 1.0f), y);
+  return y;
+}
+static inline float rcp_r(float x) {
+  const uint32_t sign = bits_of(x) & 0x80000000u, ax = bits_of(x) & 0x7fffffffu;
+  float y = float_of((0x7ef311c3u - ax) | sign);
+  y = std::fmaf(y, std::fmaf(-x, y, 1.0f), y);
+  y = std::fmaf(y, std::fmaf(-x, y, 1.0f), y);
+  y = std::fmaf(y, std::fmaf(-x, y, 1.0f), y);
+  return y;
+}
+static inline float div_r(float a, float b) { return a * rcp_r(b); }
 
 static inline F3 f3(float x, float y, float z) { return F3{x, y, z}; }
 static inline F4 f4(float x, float y, float z, float w) { return F4{x, y, z, w}; }
@@ -42,7 +81,17 @@ static inline F3 cross(F3 a, F3 b) {
   return F3{std::fmaf(a.y, b.z, -(a.z * b.y)), std::fmaf(a.z, b.x, -(a.x * b.z)),
             std::fmaf(a.x, b.y, -(a.y * b.x))};
 }
-static inline float length(F3 a) { return std::sqrt(dot(a, a)); }
+// |a| = d rsq(d) with d = a.a; unit() also returns a / |a| as a * rsq(d)
+static inline float length(F3 a) {
+  const float d = dot(a, a);
+  return d * rsq_r(d);
+}
+static inline F3 unit(F3 a, float* l) {
+  const float d = dot(a, a);
+  const float inv = rsq_r(d);
+  *l = d * inv;
+  return F3{a.x * inv, a.y * inv, a.z * inv};
+}
 
 static inline F4 qmul(F4 a, F4 b) {
   return F4{std::fmaf(a.w, b.x, std::fmaf(a.x, b.w, std::fmaf(a.y, b.z, -(a.z * b.y)))),
@@ -62,17 +111,12 @@ static inline F4 qmsub(F4 d, float s, F4 q) {
   return F4{std::fmaf(-d.x, s, q.x), std::fmaf(-d.y, s, q.y), std::fmaf(-d.z, s, q.z),
             std::fmaf(-d.w, s, q.w)};
 }
-static inline float qlength(F4 q) {
-  return std::sqrt(std::fmaf(q.x, q.x, std::fmaf(q.y, q.y, std::fmaf(q.z, q.z, q.w * q.w))));
-}
 // all_shaders.metal:99-102 quat_normalize: len > 1e-8 ? q/len : identity.
-// Canonical form: one reciprocal, four products.
+// Canonical form: inv = rsq(|q|^2), len = |q|^2 inv, four products.
 static inline F4 qnormalize(F4 q) {
-  float len = qlength(q);
-  if (len > 1e-8f) {
-    float inv = 1.0f / len;
-    return F4{q.x * inv, q.y * inv, q.z * inv, q.w * inv};
-  }
+  const float d = std::fmaf(q.x, q.x, std::fmaf(q.y, q.y, std::fmaf(q.z, q.z, q.w * q.w)));
+  const float inv = rsq_r(d);
+  if (d * inv > 1e-8f) return F4{q.x * inv, q.y * inv, q.z * inv, q.w * inv};
   return F4{0.f, 0.f, 0.f, 1.f};
 }
 // all_shaders.metal:92-97 rotate_by_quat: v + 2*(w*(qv x v) + qv x (qv x v))
@@ -90,7 +134,7 @@ static inline F3 rotate(F3 v, F4 q) {
 // fitted (weighted least squares towards minimax relative error, see
 // zeno_b200/csrc/fit_atan_poly.py) to 1.5e-8 relative error; evaluated by Horner with
 // fused multiply-adds it is within 1.5 ulp of the true value.  atan2 reduces to that
-// interval with one division and the usual octant identities.  Special values: a zero
+// interval with one reciprocal (rcp_r) and the usual octant identities.  Special values: a zero
 // denominator and numerator give +0 (or pi for x<0); a NaN operand returns NaN.  The CUDA kernel carries an identical restatement.
 // ---------------------------------------------------------------------------------
 static const float kAtanC[9] = {1.0f,
@@ -124,7 +168,7 @@ static inline float atan2_r(float y, float x) {
   float ax = std::fabs(x), ay = std::fabs(y);
   float mx = ax > ay ? ax : ay;
   float mn = ax > ay ? ay : ax;
-  float a = (mx == 0.0f) ? 0.0f : mn / mx;
+  float a = (mx == 0.0f) ? 0.0f : mn * rcp_r(mx);
   float r = atan_unit(a);
   if (ay > ax) r = kHalfPi - r;
   if (x < 0.0f) r = kPi - r;
@@ -132,10 +176,10 @@ static inline float atan2_r(float y, float x) {
   return r;
 }
 
-// asin(x) = atan2(x, sqrt((1-x)(1+x))) for x in [-1,1]
+// asin(x) = atan2(x, sqrt((1-x)(1+x))) for x in [-1,1], the root as t rsq(t)
 static inline float asin_r(float x) {
-  float c = std::sqrt((1.0f - x) * (1.0f + x));
-  return atan2_r(x, c);
+  const float t = (1.0f - x) * (1.0f + x);
+  return atan2_r(x, t * rsq_r(t));
 }
 
 static inline float clampf(float x, float lo, float hi) { return std::fmin(std::fmax(x, lo), hi); }

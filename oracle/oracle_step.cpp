@@ -308,7 +308,7 @@ void substep_env(World* w, uint32_t e) {
       st4(&trq[b * 4], F4{0, 0, 0, 0});
       continue;
     }
-    float m = 1.0f / inv_m;
+    float m = rcp_r(inv_m);
     F3 f = mul(grav, m);
     st4(&frc[b * 4], F4{f.x, f.y, f.z, 0});
     F3 cw = rotate(ld3(w->bodies[b].com_offset), ld4(&quat[b * 4]));
@@ -479,10 +479,11 @@ void substep_env(World* w, uint32_t e) {
     if (ta == 0 && tb == 0) {
       float ra = gA.pos_size0[3], rb = gB.pos_size0[3];
       F3 d = sub(pb, pa);
-      float dist = length(d);
+      float dist;
+      F3 nd = unit(d, &dist);
       float md = ra + rb;
       if (dist < md && dist > 1e-6f) {
-        normal = mul(d, 1.0f / dist);
+        normal = nd;
         pen = md - dist;
         point = madd(normal, ra - pen * 0.5f, pa);
         hit = true;
@@ -576,14 +577,14 @@ void substep_env(World* w, uint32_t e) {
         if (type == 2) {  // positional
           F3 ra = rotate(ld3(c.anchor_a), qa), rb = rotate(ld3(c.anchor_b), qb);
           F3 diff = sub(add(pa, ra), add(pb, rb));
-          float C = length(diff);
+          float C;
+          F3 nn = unit(diff, &C);
           if (C > 1e-6f) {
-            F3 nn = mul(diff, 1.0f / C);
             F3 rna = cross(ra, nn), rnb = cross(rb, nn);
             float wa = ima + dot(mulv(rna, Ia), rna);
             float wb = imb + dot(mulv(rnb, Ib), rnb);
             float wsum = wa + wb;
-            float dl = std::fmaf(-alpha, lam, -C) / (wsum + alpha);
+            float dl = div_r(std::fmaf(-alpha, lam, -C), wsum + alpha);
             c.state[0] = lam + dl;
             F3 imp = mul(nn, dl);
             F3 rca = sub(ra, rotate(ld3(w->bodies[ia].com_offset), qa));
@@ -604,13 +605,13 @@ void substep_env(World* w, uint32_t e) {
         } else if (type == 7) {  // weld (body b only)
           F3 ra = rotate(ld3(c.anchor_a), qa), rb = rotate(ld3(c.anchor_b), qb);
           F3 diff = sub(add(pa, ra), add(pb, rb));
-          float C = length(diff);
+          float C;
+          F3 nn = unit(diff, &C);
           if (C > 1e-6f) {
-            F3 nn = mul(diff, 1.0f / C);
             F3 rnb = cross(rb, nn);
             float wb = imb + dot(mulv(rnb, Ib), rnb);
             if (wb > 1e-8f) {
-              float dl = -C / (wb + alpha);
+              float dl = div_r(-C, wb + alpha);
               F3 imp = mul(nn, dl);
               st3(&pos[ib * 4], msub(imp, imb, pb));
               F3 dw = mulv(cross(rb, imp), Ib);
@@ -623,14 +624,14 @@ void substep_env(World* w, uint32_t e) {
           F4 qerr = qmul(qrel, qconj(ld4(c.axis_target)));
           if (qerr.w < 0) qerr = qneg(qerr);
           F3 ev = xyz(qerr);
-          float sh = length(ev);
+          float sh;
+          F3 axr = unit(ev, &sh);
           if (sh > 1e-6f) {
-            F3 axr = mul(ev, 1.0f / sh);
             float ang_ = 2.0f * atan2_r(sh, qerr.w);
             F3 aw = rotate(axr, qau);
             float wb = dot(mulv(aw, Ib), aw);
             if (wb > 1e-8f) {
-              float dl = ang_ / (wb + alpha);
+              float dl = div_r(ang_, wb + alpha);
               F3 ai = mul(aw, dl);
               if (imb > 0) {
                 F3 dw = mulv(ai, Ib);
@@ -642,14 +643,14 @@ void substep_env(World* w, uint32_t e) {
         } else if (type == 3) {  // angular (hinge axis alignment)
           F3 aaw = rotate(ld3(c.anchor_a), qa), abw = rotate(ld3(c.anchor_b), qb);
           F3 cr = cross(aaw, abw);
-          float sa = length(cr);
+          float sa;
+          F3 nn = unit(cr, &sa);
           if (sa > 1e-6f) {
-            F3 nn = mul(cr, 1.0f / sa);
             float angC = asin_r(clampf(sa, -1.0f, 1.0f));
             float wa = dot(mulv(nn, Ia), nn), wb = dot(mulv(nn, Ib), nn);
             float wsum = wa + wb;
             if (wsum > 1e-8f) {
-              float dl = -angC / (wsum + alpha);
+              float dl = div_r(-angC, wsum + alpha);
               if (ima > 0) {
                 F3 dw = mulv(mul(nn, dl), Ia);
                 F4 dq = qmul(F4{dw.x, dw.y, dw.z, 0.0f}, qa);
@@ -676,7 +677,7 @@ void substep_env(World* w, uint32_t e) {
             float wa = dot(mulv(aw, Ia), aw), wb = dot(mulv(aw, Ib), aw);
             float wsum = wa + wb;
             if (wsum > 1e-8f) {
-              float dl = viol / (wsum + alpha);
+              float dl = div_r(viol, wsum + alpha);
               F3 ai = mul(aw, dl);
               if (ima > 0) {
                 F3 dw = mulv(ai, Ia);
@@ -708,7 +709,7 @@ void substep_env(World* w, uint32_t e) {
             float wb = imb + dot(mulv(rnb, Ib), rnb);
             float wsum = wa + wb;
             if (wsum > 1e-8f) {
-              float dl = av / (wsum + alpha);
+              float dl = div_r(av, wsum + alpha);
               F3 imp = mul(nn, dl);
               if (ima > 0) st3(&pos[ia * 4], msub(imp, ima, pa));
               if (imb > 0) st3(&pos[ib * 4], madd(imp, imb, pb));
@@ -720,14 +721,14 @@ void substep_env(World* w, uint32_t e) {
           F3 aw = rotate(ld3(c.axis_target), qa);
           float along = dot(diff, aw);
           F3 perp = msub(aw, along, diff);
-          float pl = length(perp);
+          float pl;
+          F3 nn = unit(perp, &pl);
           if (pl > 1e-6f) {
-            F3 nn = mul(perp, 1.0f / pl);
             F3 rna = cross(ra, nn), rnb = cross(rb, nn);
             float wa = ima + dot(mulv(rna, Ia), rna);
             float wb = imb + dot(mulv(rnb, Ib), rnb);
             float wsum = wa + wb;
-            float dl = (-pl) / (wsum + alpha);
+            float dl = div_r(-pl, wsum + alpha);
             F3 imp = mul(nn, dl);
             if (ima > 0) {
               st3(&pos[ia * 4], madd(imp, ima, pa));
@@ -747,15 +748,15 @@ void substep_env(World* w, uint32_t e) {
           F4 qerr = qmul(qrel, qconj(ld4(c.limits)));
           if (qerr.w < 0) qerr = qneg(qerr);
           F3 ev = xyz(qerr);
-          float sh = length(ev);
+          float sh;
+          F3 axe = unit(ev, &sh);
           if (sh > 1e-6f) {
-            F3 axe = mul(ev, 1.0f / sh);
             float ae = 2.0f * atan2_r(sh, qerr.w);
             F3 aw2 = rotate(axe, qau);
             float wa = dot(mulv(aw2, Ia), aw2), wb = dot(mulv(aw2, Ib), aw2);
             float wsum = wa + wb;
             if (wsum > 1e-8f) {
-              float dl = ae / (wsum + alpha);
+              float dl = div_r(ae, wsum + alpha);
               F3 ai = mul(aw2, dl);
               if (ima > 0) {
                 F3 dw = mulv(ai, Ia);
@@ -796,41 +797,41 @@ void substep_env(World* w, uint32_t e) {
       F3 rv = sub(va, vb);
       float vn = dot(rv, nn);
       F3 vt = msub(nn, vn, rv);
-      float ts = length(vt);
+      float ts;
+      F3 tt = unit(vt, &ts);
       F3 rna = cross(ra, nn), rnb = cross(rb, nn);
       float wna = ima + dot(mulv(rna, Ia), rna);
       float wnb = imb + dot(mulv(rnb, Ib), rnb);
       float wn = wna + wnb;
       if (wn < 1e-8f) continue;
       float excess = std::fmax(pen - P.slop, 0.0f);
-      float bias = P.baumgarte * excess / dt;
+      float bias = div_r(P.baumgarte * excess, dt);
       float rest = c.impulses[3];
       float vrest = vn < -0.5f ? rest * vn : 0.0f;
-      float jn = (-(vn + vrest) + bias) / wn;
+      float jn = div_r(-(vn + vrest) + bias, wn);
       jn = std::fmax(jn, 0.0f);
       F3 in_ = mul(nn, jn);
       float pcorr = P.baumgarte * excess;
       if (ima > 1e-8f) {
         st3(&vel[ia * 4], madd(in_, ima, ld3(&vel[ia * 4])));
         st3(&ang[ia * 4], add(ld3(&ang[ia * 4]), mulv(cross(ra, in_), Ia)));
-        float mr = ima / isum;
+        float mr = div_r(ima, isum);
         st3(&pos[ia * 4], madd(nn, pcorr * mr, ld3(&pos[ia * 4])));
       }
       if (imb > 1e-8f) {
         st3(&vel[ib * 4], msub(in_, imb, ld3(&vel[ib * 4])));
         st3(&ang[ib * 4], sub(ld3(&ang[ib * 4]), mulv(cross(rb, in_), Ib)));
-        float mr = imb / isum;
+        float mr = div_r(imb, isum);
         st3(&pos[ib * 4], msub(nn, pcorr * mr, ld3(&pos[ib * 4])));
       }
       float jacc = c.impulses[0] + jn;
       if (ts > 1e-6f && jacc > 1e-6f) {
-        F3 tt = mul(vt, 1.0f / ts);
         F3 rta = cross(ra, tt), rtb = cross(rb, tt);
         float wta = ima + dot(mulv(rta, Ia), rta);
         float wtb = imb + dot(mulv(rtb, Ib), rtb);
         float wt = wta + wtb;
         if (wt > 1e-8f) {
-          float jdes = ts / wt;
+          float jdes = div_r(ts, wt);
           float jmax = fr * jacc;
           float jt_ = std::fmin(jdes, jmax);
           F3 it_ = mul(tt, jt_);
@@ -1280,7 +1281,7 @@ void world_reset_env_noise(World* w, uint32_t e) {
       F3 ax = rotate(ld3(jr.axis), qp);
       float al = length(ax);
       if (!(al > 1e-8f)) continue;
-      F3 h = mul(ax, (0.5f * th) / al);
+      F3 h = mul(ax, div_r(0.5f * th, al));
       F4 qr = qnormalize(F4{h.x, h.y, h.z, 1.0f});
       for (uint32_t d = ch; d < ch + w->subtree[ch]; d++) {
         F3 rel = sub(ld3(&pos[d * 4]), anchor);

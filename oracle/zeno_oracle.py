@@ -87,6 +87,7 @@ def lib() -> ctypes.CDLL:
         L.zo_set_narrow_mode.argtypes = [vp, ctypes.c_uint32]
         L.zo_narrow_cpu.argtypes = [f32p, f32p, f32p, f32p, f32p, ctypes.c_uint32]
         L.zo_gjk_epa.argtypes = [f32p, f32p, f32p, f32p, f32p]
+        L.zo_eval_math.argtypes = [ctypes.c_uint32, f32p, f32p, f32p, ctypes.c_uint64]
         _lib = L
     return _lib
 
@@ -221,3 +222,14 @@ def gjk_epa(geom_a, body_a, geom_b, body_b):
     if r < 2:
         return bool(r), None
     return True, (out[:3].copy(), float(out[3]), out[4:7].copy(), out[7:10].copy())
+
+
+def eval_math(fn, x, y=None):
+    """The oracle's canonical scalar function `fn` (0 rsq, 1 rcp, 2 atan2(x, y), 3 asin,
+    4 len((x, y, x/2))) over an array."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    yy = None if y is None else np.ascontiguousarray(y, dtype=np.float32)
+    out = np.empty_like(x)
+    if lib().zo_eval_math(fn, _fptr(x), _fptr(yy), _fptr(out), x.size) != 0:
+        raise ValueError("bad arguments")
+    return out

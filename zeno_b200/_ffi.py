@@ -102,6 +102,7 @@ ffi.cdef("""
     const void* zeno_world_model_table(ZenoWorldHandle world, const char* name, uint64_t* nbytes);
     const char* zeno_last_error(void);
     void* zeno_model_create_from_string(const char* mjcf_string);
+    int zeno_eval_math(uint32_t fn, const float* x, const float* y, float* out, uint64_t n);
     void* zeno_model_create_from_string_ex(const char* mjcf_string, uint32_t semantics);
     void zeno_model_destroy(void* model);
     const void* zeno_model_table(void* model, const char* name, uint64_t* nbytes);
@@ -184,6 +185,18 @@ class CudaArray:
 
 
 SEMANTICS = {"reference": 0, "corrected": 1}
+
+
+def eval_math(fn: int, x: np.ndarray, y: Optional[np.ndarray] = None) -> np.ndarray:
+    """The step kernels' canonical scalar function `fn` (0 rsq, 1 rcp, 2 atan2(x, y),
+    3 asin, 4 len((x, y, x/2))) evaluated on the GPU."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    yy = None if y is None else np.ascontiguousarray(y, dtype=np.float32)
+    out = np.empty_like(x)
+    yp = ffi.NULL if yy is None else ffi.cast("float*", yy.ctypes.data)
+    _check(_lib.zeno_eval_math(fn, ffi.cast("float*", x.ctypes.data), yp, ffi.cast("float*", out.ctypes.data),
+                               x.size), "Evaluate math")
+    return out
 
 
 def model_tables(mjcf_string: str, semantics: str = "reference") -> Dict[str, bytes]:

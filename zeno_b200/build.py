@@ -29,7 +29,7 @@ NVCC_FLAGS = ARCH + ["-lineinfo", "-O3", "-std=c++17", "-fmad=false", "-prec-div
                      "-ftz=false", "-Xcompiler", "-fPIC", "-Xptxas", "-warn-spills"]
 CXX_FLAGS = ["-O2", "-std=c++17", "-fPIC", "-ffp-contract=off", "-fno-fast-math", "-Wall",
              f"-I{CUDA_HOME / 'include'}", f"-I{INCLUDE}"]
-CU_SOURCES = ["step_kernel.cu", "fast_step.cu", "noalloc.cu"]
+CU_SOURCES = ["step_kernel.cu", "fast_step.cu", "noalloc.cu", "math_eval.cu"]
 CXX_SOURCES = ["mjcf.cpp", "model.cpp", "fast_model.cpp", "world.cpp", "capi.cpp"]
 HEADERS = ["zeno_types.h", "devmath.cuh", "physics.cuh", "model_access.cuh", "fast_model.h", "step_kernel.h", "scene.h", "model.h", "world.h"]
 

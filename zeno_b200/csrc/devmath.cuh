@@ -2,11 +2,11 @@
 //
 // The reference evaluates these expressions in Metal with the compiler's default
 // fast-math settings, so its rounding is unspecified.  This build fixes one canonical
-// evaluation order -- explicit fused multiply-adds (__fmaf_rn) and correctly rounded
-// +, -, *, /, sqrt, nothing else -- and compiles with -fmad=false so nvcc adds no
-// contractions of its own.  Every operation is then IEEE-754 deterministic, and the
-// results are bit-identical to any other implementation that evaluates the same
-// expressions in the same order (the CPU oracle does).
+// evaluation order -- explicit fused multiply-adds (__fmaf_rn), correctly rounded +, -, *,
+// and reciprocals / reciprocal square roots built from those (rsq_, rcp_) -- and compiles
+// with -fmad=false so nvcc adds no contractions of its own.  Every operation is then
+// IEEE-754 deterministic, and the results are bit-identical to any other implementation
+// that evaluates the same expressions in the same order (the CPU oracle does).
 #pragma once
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -20,9 +20,33 @@ struct V3 {
 __device__ __forceinline__ V3 v3(float x, float y, float z) { return V3{x, y, z}; }
 __device__ __forceinline__ V3 v3(float4 a) { return V3{a.x, a.y, a.z}; }
 __device__ __forceinline__ float fma_(float a, float b, float c) { return __fmaf_rn(a, b, c); }
-// Correctly rounded 1/x.  Bit-identical to __frcp_rn(x) (both are the IEEE reciprocal in
-// round-to-nearest-even); the division form has the shorter latency on sm_100a.
-__device__ __forceinline__ float rcp_(float x) { return __fdiv_rn(1.0f, x); }
+// Reciprocal square root and reciprocal from multiplies and fused multiply-adds only
+// (Newton-Raphson from a bit-pattern initial guess, residual form), three iterations
+// each: within 1 ulp, deterministic, and reproducible by any implementation that runs the
+// same steps.
+//   rsq_: y0 from the bit trick 0x5f375a86 - (bits(x) >> 1) (Lomont, "Fast inverse square
+//         root", 2003); e = 1 - (x y) y, y = y + (y/2) e.  For finite x > 0; rsq_(0) is a
+//         large finite value, so |v| = d rsq_(d) is exactly 0 for d = 0.
+//   rcp_: y0 = +-float(0x7ef311c3 - bits(|x|)) (exponent negation, relative error < 13 %);
+//         e = 1 - x y, y = y + y e.  For finite x != 0 with |x| < 2^125.
+// Outside those domains the results are unspecified (but still deterministic); every use
+// in the step kernels sits behind a guard that discards such a result.
+__device__ __forceinline__ float rsq_(float x) {
+  float y = __uint_as_float(0x5f375a86u - (__float_as_uint(x) >> 1));
+  y = fma_(0.5f * y, fma_(-(x * y), y, 1.0f), y);
+  y = fma_(0.5f * y, fma_(-(x * y), y, 1.0f), y);
+  y = fma_(0.5f * y, fma_(-(x * y), y, 1.0f), y);
+  return y;
+}
+__device__ __forceinline__ float rcp_(float x) {
+  const uint32_t sign = __float_as_uint(x) & 0x80000000u, ax = __float_as_uint(x) & 0x7fffffffu;
+  float y = __uint_as_float((0x7ef311c3u - ax) | sign);
+  y = fma_(y, fma_(-x, y, 1.0f), y);
+  y = fma_(y, fma_(-x, y, 1.0f), y);
+  y = fma_(y, fma_(-x, y, 1.0f), y);
+  return y;
+}
+__device__ __forceinline__ float div_(float a, float b) { return a * rcp_(b); }
 
 __device__ __forceinline__ V3 operator+(V3 a, V3 b) { return V3{a.x + b.x, a.y + b.y, a.z + b.z}; }
 __device__ __forceinline__ V3 operator-(V3 a, V3 b) { return V3{a.x - b.x, a.y - b.y, a.z - b.z}; }
@@ -40,7 +64,17 @@ __device__ __forceinline__ float dot(V3 a, V3 b) { return fma_(a.x, b.x, fma_(a.
 __device__ __forceinline__ V3 cross(V3 a, V3 b) {
   return V3{fma_(a.y, b.z, -(a.z * b.y)), fma_(a.z, b.x, -(a.x * b.z)), fma_(a.x, b.y, -(a.y * b.x))};
 }
-__device__ __forceinline__ float len(V3 a) { return __fsqrt_rn(dot(a, a)); }
+// |a| = d rsq(d), d = a.a; unit(a, l) also returns a / |a| as a * rsq(d).
+__device__ __forceinline__ float len(V3 a) {
+  const float d = dot(a, a);
+  return d * rsq_(d);
+}
+__device__ __forceinline__ V3 unit(V3 a, float& l) {
+  const float d = dot(a, a);
+  const float inv = rsq_(d);
+  l = d * inv;
+  return a * inv;
+}
 
 __device__ __forceinline__ float4 qmul(float4 a, float4 b) {
   return make_float4(fma_(a.w, b.x, fma_(a.x, b.w, fma_(a.y, b.z, -(a.z * b.y)))),
@@ -61,9 +95,9 @@ __device__ __forceinline__ float4 qmsub(float4 d, float s, float4 q) {
 // quat_normalize (all_shaders.metal:99-102): len > 1e-8 ? q * (1/len) : identity.
 // Written as a select (the reciprocal is computed either way): no branch on the chain.
 __device__ __forceinline__ float4 qnormalize(float4 q) {
-  const float l = __fsqrt_rn(fma_(q.x, q.x, fma_(q.y, q.y, fma_(q.z, q.z, q.w * q.w))));
-  const float inv = rcp_(l);
-  const bool ok = l > 1e-8f;
+  const float d = fma_(q.x, q.x, fma_(q.y, q.y, fma_(q.z, q.z, q.w * q.w)));
+  const float inv = rsq_(d);
+  const bool ok = d * inv > 1e-8f;
   return make_float4(ok ? q.x * inv : 0.0f, ok ? q.y * inv : 0.0f, ok ? q.z * inv : 0.0f, ok ? q.w * inv : 1.0f);
 }
 // c ? a : b per component
@@ -104,7 +138,7 @@ __device__ __forceinline__ float atan2r(float y, float x) {
   float ax = fabsf(x), ay = fabsf(y);
   float mx = ax > ay ? ax : ay;
   float mn = ax > ay ? ay : ax;
-  float a = (mx == 0.0f) ? 0.0f : __fdiv_rn(mn, mx);
+  float a = (mx == 0.0f) ? 0.0f : mn * rcp_(mx);
   float r = atan_unit(a);
   if (ay > ax) r = 1.57079632679490f - r;
   if (x < 0.0f) r = 3.14159265358979f - r;
@@ -112,7 +146,8 @@ __device__ __forceinline__ float atan2r(float y, float x) {
   return r;
 }
 __device__ __forceinline__ float asinr(float x) {
-  return atan2r(x, __fsqrt_rn((1.0f - x) * (1.0f + x)));
+  const float t = (1.0f - x) * (1.0f + x);
+  return atan2r(x, t * rsq_(t));
 }
 
 // splitmix64 finalizer (counter-based random numbers for the episode-reset extension)

@@ -725,7 +725,7 @@ __device__ __forceinline__ void run_env(const StepArgs& a, const FModel& f, cons
             const V3 ax = rotate(v3(m.jaxis(j)), qp);
             const float al = len(ax);
             if (!(al > 1e-8f)) continue;
-            const V3 hv = ax * __fdiv_rn(0.5f * th, al);
+            const V3 hv = ax * div_(0.5f * th, al);
             const float4 qr = qnormalize(make_float4(hv.x, hv.y, hv.z, 1.0f));
             const uint32_t end = ch + (m.body(ch) >> 24);
             for (uint32_t d = ch; d < end; ++d) {

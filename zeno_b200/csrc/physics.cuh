@@ -38,12 +38,12 @@ __device__ __forceinline__ void cons_math(const M& m, const ConstraintV& c, floa
   if (T == 2) {  // positional
     const V3 ra = rotate(aa, qa), rb = rotate(ab, qb);
     const V3 diff = (pa + ra) - (pb + rb);
-    const float C = len(diff);
-    const V3 n = diff * rcp_(C);
+    float C;
+    const V3 n = unit(diff, C);
     const V3 rna = cross(ra, n), rnb = cross(rb, n);
     const float wa = ima + dot(hadamard(rna, Ia), rna);
     const float wb = imb + dot(hadamard(rnb, Ib), rnb);
-    const float dl = __fdiv_rn(-C, wa + wb);
+    const float dl = div_(-C, wa + wb);
     const V3 imp = n * dl;
     const V3 rca = ra - rotate(v3(m.com(c.a)), qa), rcb = rb - rotate(v3(m.com(c.b)), qb);
     const bool ok = C > 1e-6f;
@@ -59,11 +59,11 @@ __device__ __forceinline__ void cons_math(const M& m, const ConstraintV& c, floa
   } else if (T == 7) {  // weld: corrections on body b only
     const V3 ra = rotate(aa, qa), rb = rotate(ab, qb);
     const V3 diff = (pa + ra) - (pb + rb);
-    const float C = len(diff);
-    const V3 n = diff * rcp_(C);
+    float C;
+    const V3 n = unit(diff, C);
     const V3 rnb = cross(rb, n);
     const float wb = imb + dot(hadamard(rnb, Ib), rnb);
-    const V3 imp = n * __fdiv_rn(-C, wb);
+    const V3 imp = n * div_(-C, wb);
     const bool u1 = C > 1e-6f && wb > 1e-8f;
     pb4 = sel4(u1, with_w(msub(imp, imb, pb), pb4.w), pb4);
     qb = sel4(u1, qnormalize(qmsub(qmul_v(hadamard(cross(rb, imp), Ib), qb), 0.5f, qb)), qb);
@@ -71,22 +71,22 @@ __device__ __forceinline__ void cons_math(const M& m, const ConstraintV& c, floa
     float4 qerr = qmul(qmul(qconj(qau), qbu), qconj(c.at));
     qerr = sel4(qerr.w < 0.0f, qneg(qerr), qerr);
     const V3 ev = xyz(qerr);
-    const float sh = len(ev);
-    const V3 axr = ev * rcp_(sh);
+    float sh;
+    const V3 axr = unit(ev, sh);
     const float ang = 2.0f * atan2r(sh, qerr.w);
     const V3 aw = rotate(axr, qau);
     const float w2 = dot(hadamard(aw, Ib), aw);
-    const V3 ai = aw * __fdiv_rn(ang, w2);
+    const V3 ai = aw * div_(ang, w2);
     const bool u2 = sh > 1e-6f && w2 > 1e-8f && imb > 0.0f;
     qb = sel4(u2, qnormalize(qmsub(qmul_v(hadamard(ai, Ib), qbu), 0.5f, qbu)), qb);
   } else if (T == 3) {  // angular: keep hinge axes parallel
     const V3 aaw = rotate(aa, qa), abw = rotate(ab, qb);
     const V3 cr = cross(aaw, abw);
-    const float sa = len(cr);
-    const V3 n = cr * rcp_(sa);
+    float sa;
+    const V3 n = unit(cr, sa);
     const float angC = asinr(clampf(sa, -1.0f, 1.0f));
     const float w = dot(hadamard(n, Ia), n) + dot(hadamard(n, Ib), n);
-    const float dl = __fdiv_rn(-angC, w);
+    const float dl = div_(-angC, w);
     const bool ok = sa > 1e-6f && w > 1e-8f;
     const float4 qa_n = qnormalize(qmadd(qmul_v(hadamard(n * dl, Ia), qa), 0.5f, qa));
     const float4 qb_n = qnormalize(qmadd(qmul_v(hadamard(n * (-dl), Ib), qb), 0.5f, qb));
@@ -102,7 +102,7 @@ __device__ __forceinline__ void cons_math(const M& m, const ConstraintV& c, floa
     if (fabsf(viol) > 1e-6f) {  // rarely taken: keep the branch, skip the work
       const V3 aw = rotate(aa, qa);
       const float w = dot(hadamard(aw, Ia), aw) + dot(hadamard(aw, Ib), aw);
-      const V3 ai = aw * __fdiv_rn(viol, w);
+      const V3 ai = aw * div_(viol, w);
       const bool ok = w > 1e-8f;
       const float4 qa_n = qnormalize(qmadd(qmul_v(hadamard(ai, Ia), qa), 0.5f, qa));
       const float4 qb_n = qnormalize(qmsub(qmul_v(hadamard(ai, Ib), qb), 0.5f, qb));
@@ -123,7 +123,7 @@ __device__ __forceinline__ void cons_math(const M& m, const ConstraintV& c, floa
       const float wa = ima + dot(hadamard(rna, Ia), rna);
       const float wb = imb + dot(hadamard(rnb, Ib), rnb);
       const float w = wa + wb;
-      const V3 imp = n * __fdiv_rn(fabsf(viol), w);
+      const V3 imp = n * div_(fabsf(viol), w);
       const bool ok = w > 1e-8f;
       pa4 = sel4(ok && ima > 0.0f, with_w(msub(imp, ima, pa), pa4.w), pa4);
       pb4 = sel4(ok && imb > 0.0f, with_w(madd(imp, imb, pb), pb4.w), pb4);
@@ -133,12 +133,12 @@ __device__ __forceinline__ void cons_math(const M& m, const ConstraintV& c, floa
     const V3 diff = (pa + ra) - (pb + rb);
     const V3 aw = rotate(v3(c.at), qa);
     const V3 perp = msub(aw, dot(diff, aw), diff);
-    const float pl = len(perp);
-    const V3 n = perp * rcp_(pl);
+    float pl;
+    const V3 n = unit(perp, pl);
     const V3 rna = cross(ra, n), rnb = cross(rb, n);
     const float wa = ima + dot(hadamard(rna, Ia), rna);
     const float wb = imb + dot(hadamard(rnb, Ib), rnb);
-    const V3 imp = n * __fdiv_rn(-pl, wa + wb);
+    const V3 imp = n * div_(-pl, wa + wb);
     const bool ok = pl > 1e-6f;
     const float4 qa0 = qa, qb0 = qb;
     const bool ua = ok && ima > 0.0f, ub = ok && imb > 0.0f;
@@ -150,12 +150,12 @@ __device__ __forceinline__ void cons_math(const M& m, const ConstraintV& c, floa
     float4 qerr = qmul(qmul(qconj(qau), qbu), qconj(c.lim));
     qerr = sel4(qerr.w < 0.0f, qneg(qerr), qerr);
     const V3 ev = xyz(qerr);
-    const float sh = len(ev);
-    const V3 axe = ev * rcp_(sh);
+    float sh;
+    const V3 axe = unit(ev, sh);
     const float ae = 2.0f * atan2r(sh, qerr.w);
     const V3 aw2 = rotate(axe, qau);
     const float w = dot(hadamard(aw2, Ia), aw2) + dot(hadamard(aw2, Ib), aw2);
-    const V3 ai = aw2 * __fdiv_rn(ae, w);
+    const V3 ai = aw2 * div_(ae, w);
     const bool ok2 = sh > 1e-6f && w > 1e-8f;
     qa = sel4(ok2 && ima > 0.0f, qnormalize(qmadd(qmul_v(hadamard(ai, Ia), qau), 0.5f, qau)), qa);
     qb = sel4(ok2 && imb > 0.0f, qnormalize(qmsub(qmul_v(hadamard(ai, Ib), qbu), 0.5f, qbu)), qb);
@@ -211,33 +211,33 @@ __device__ __forceinline__ void solve_contact(const M& m, float4 cpp, float4 cnf
   const V3 rv = va - vb;
   const float vn = dot(rv, n);
   const V3 vt = msub(n, vn, rv);
-  const float ts = len(vt);
+  float ts;
+  const V3 t = unit(vt, ts);
   const V3 rna = cross(ra, n), rnb = cross(rb, n);
   const float wn = (ima + dot(hadamard(rna, Ia), rna)) + (imb + dot(hadamard(rnb, Ib), rnb));
   if (wn < 1e-8f) return;
   const float excess = fmaxf(pen - slop, 0.0f);
-  const float bias = __fdiv_rn(baumgarte * excess, dt);
+  const float bias = div_(baumgarte * excess, dt);
   const float vrest = vn < -0.5f ? rest * vn : 0.0f;
-  const float jn = fmaxf(__fdiv_rn(-(vn + vrest) + bias, wn), 0.0f);
+  const float jn = fmaxf(div_(-(vn + vrest) + bias, wn), 0.0f);
   const V3 in_ = n * jn;
   const float pcorr = baumgarte * excess;
   if (ima > 1e-8f) {
     s.vel(ia) = with_w(madd(in_, ima, v3(s.vel(ia))), s.vel(ia).w);
     s.ang(ia) = with_w(v3(s.ang(ia)) + hadamard(cross(ra, in_), Ia), s.ang(ia).w);
-    s.pos(ia) = with_w(madd(n, pcorr * __fdiv_rn(ima, isum), v3(s.pos(ia))), s.pos(ia).w);
+    s.pos(ia) = with_w(madd(n, pcorr * div_(ima, isum), v3(s.pos(ia))), s.pos(ia).w);
   }
   if (imb > 1e-8f) {
     s.vel(ib) = with_w(msub(in_, imb, v3(s.vel(ib))), s.vel(ib).w);
     s.ang(ib) = with_w(v3(s.ang(ib)) - hadamard(cross(rb, in_), Ib), s.ang(ib).w);
-    s.pos(ib) = with_w(msub(n, pcorr * __fdiv_rn(imb, isum), v3(s.pos(ib))), s.pos(ib).w);
+    s.pos(ib) = with_w(msub(n, pcorr * div_(imb, isum), v3(s.pos(ib))), s.pos(ib).w);
   }
   const float jacc = jx + jn;
   if (ts > 1e-6f && jacc > 1e-6f) {
-    const V3 t = vt * rcp_(ts);
     const V3 rta = cross(ra, t), rtb = cross(rb, t);
     const float wt = (ima + dot(hadamard(rta, Ia), rta)) + (imb + dot(hadamard(rtb, Ib), rtb));
     if (wt > 1e-8f) {
-      const float jt = fminf(__fdiv_rn(ts, wt), fr * jacc);
+      const float jt = fminf(div_(ts, wt), fr * jacc);
       const V3 it = t * jt;
       if (ima > 1e-8f) {
         s.vel(ia) = with_w(msub(it, ima, v3(s.vel(ia))), s.vel(ia).w);
@@ -262,10 +262,11 @@ __device__ __forceinline__ bool narrow_core(uint32_t ta, uint32_t tb, V3 pa, V3 
                                             float4 cq, V3& point, V3& normal, float& pen) {
   if (ta == 0 && tb == 0) {
     const V3 d = pb - pa;
-    const float dist = len(d);
+    float dist;
+    const V3 nd = unit(d, dist);
     const float md = ra + rb;
     if (dist < md && dist > 1e-6f) {
-      normal = d * rcp_(dist);
+      normal = nd;
       pen = md - dist;
       point = madd(normal, ra - pen * 0.5f, pa);
       return true;

@@ -233,7 +233,7 @@ __device__ void reset_env_noise(const StepArgs& a, uint32_t e, float4* pos, floa
       const V3 ax = rotate(v3(jd.axis[0], jd.axis[1], jd.axis[2]), qp);
       const float al = len(ax);
       if (!(al > 1e-8f)) continue;
-      const V3 h = ax * __fdiv_rn(0.5f * th, al);
+      const V3 h = ax * div_(0.5f * th, al);
       const float4 qr = qnormalize(make_float4(h.x, h.y, h.z, 1.0f));
       const uint32_t end = ch + a.subtree[ch];
       for (uint32_t d = ch; d < end; ++d) {
@@ -879,7 +879,7 @@ __device__ __forceinline__ void step_env(const StepArgs& a, uint32_t e, unsigned
 // the count for the next step.
 // ------------------------------------------------------------------------------------
 template <int L>
-__global__ void __launch_bounds__(256) step_kernel(StepArgs a) {
+__global__ void __launch_bounds__(256, 1) step_kernel(StepArgs a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const uint32_t NE = blockDim.x / L;
   const uint32_t g = threadIdx.x / L;
