@@ -748,6 +748,24 @@ __device__ __forceinline__ void run_env(const StepArgs& a, const FModel& f, cons
   flags_out = flags;
 }
 
+// Asynchronous global -> shared copies (cp.async, completion tracked per thread in commit
+// groups; wait_group N returns once at most N of the thread's groups are still pending).
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(uint32_t(__cvta_generic_to_shared(smem))),
+               "l"(gmem)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async4(void* smem, const void* gmem) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(uint32_t(__cvta_generic_to_shared(smem))),
+               "l"(gmem)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
+
 // blockDim.x = envs_per_block * L threads (envs_per_block <= 32); group g (= threadIdx.x / L)
 // owns env e0 + g.
 template <int L>
@@ -764,15 +782,9 @@ __global__ void __launch_bounds__(32 * L) fast_step_kernel(const __grid_constant
   // shared memory: the model's hot image, then the per-environment sections
   unsigned char* hot = smem_raw;
   unsigned char* blk = smem_raw + f.hot_bytes;
-  for (uint32_t t = tid; t < f.hot_bytes / 16u; t += nt) reinterpret_cast<uint4*>(hot)[t] = f.hot[t];
-  __syncthreads();
-  // gravity force per body for this step (compute_forces 345-388): g / (1/m), zero when massless
-  for (uint32_t b = tid; b < B; b += nt) {
-    const float4 mi = reinterpret_cast<const float4*>(hot + f.o_imi)[b];
-    const V3 gv{a.gravity[0], a.gravity[1], a.gravity[2]};
-    reinterpret_cast<float4*>(hot + f.o_gforce)[b] =
-        mi.x < 1e-8f ? make_float4(0.0f, 0.0f, 0.0f, 0.0f) : with_w(gv * rcp_(mi.x), 0.0f);
-  }
+  // the hot image and (below) the block's state arrive by cp.async, all copies in flight at once
+  for (uint32_t t = tid; t < f.hot_bytes / 16u; t += nt) cp_async16(reinterpret_cast<uint4*>(hot) + t, f.hot + t);
+  cp_async_commit();
   float4* s_pos = reinterpret_cast<float4*>(blk + pl.pos * ne);
   float4* s_quat = reinterpret_cast<float4*>(blk + pl.quat * ne);
   float4* s_vel = reinterpret_cast<float4*>(blk + pl.vel * ne);
@@ -791,17 +803,27 @@ __global__ void __launch_bounds__(32 * L) fast_step_kernel(const __grid_constant
   float4* gacc = reinterpret_cast<float4*>(a.acc) + eb;
   for (uint32_t t = tid; t < nb * B; t += nt) {
     const uint32_t el = t / B, b = t - el * B, si = b * ne + el;
-    s_pos[si] = gpos[t];
-    s_quat[si] = gquat[t];
-    s_vel[si] = gvel[t];
-    s_ang[si] = gang[t];
+    cp_async16(s_pos + si, gpos + t);
+    cp_async16(s_quat + si, gquat + t);
+    cp_async16(s_vel + si, gvel + t);
+    cp_async16(s_ang + si, gang + t);
   }
   float* gjt = a.jtorque + size_t(e0) * J;
   float* gjp = a.jpos + size_t(e0) * J;
   float* gjv = a.jvel + size_t(e0) * J;
   for (uint32_t t = tid; t < nb * J; t += nt) {
     const uint32_t el = t / J, j = t - el * J;
-    s_jt[j * ne + el] = gjt[t];
+    cp_async4(s_jt + j * ne + el, gjt + t);
+  }
+  cp_async_commit();
+  cp_async_wait<1>();  // this thread's part of the hot image
+  __syncthreads();
+  // gravity force per body for this step (compute_forces 345-388): g / (1/m), zero when massless
+  for (uint32_t b = tid; b < B; b += nt) {
+    const float4 mi = reinterpret_cast<const float4*>(hot + f.o_imi)[b];
+    const V3 gv{a.gravity[0], a.gravity[1], a.gravity[2]};
+    reinterpret_cast<float4*>(hot + f.o_gforce)[b] =
+        mi.x < 1e-8f ? make_float4(0.0f, 0.0f, 0.0f, 0.0f) : with_w(gv * rcp_(mi.x), 0.0f);
   }
   // ---- contact list headers, then the slots: slot words, impulses, previous-list ranks ----
   uint32_t* s_hdr = reinterpret_cast<uint32_t*>(blk + pl.hdr * ne);
@@ -864,6 +886,7 @@ __global__ void __launch_bounds__(32 * L) fast_step_kernel(const __grid_constant
     if (i < s_hdr[el] && sw_rank(s_meta[(i - 1) * ne + el]) > sw_rank(s_meta[i * ne + el])) s_hdr[3 * ne + el] = 1;
     if (i < s_hdr[ne + el] && s_aux[(i - 1) * ne + el] > s_aux[i * ne + el]) s_hdr[3 * ne + el] = 1;
   }
+  cp_async_wait<0>();  // this thread's part of the body state and joint torques
   __syncthreads();
   for (uint32_t el = tid; el < nb; el += nt)
     if (s_hdr[3 * ne + el]) {
