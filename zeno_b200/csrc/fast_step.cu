@@ -334,15 +334,38 @@ __device__ __forceinline__ void run_env(const StepArgs& a, const FModel& f, cons
     }
     const uint32_t n = count < M ? count : M;
     // ---- stable sort by key (sort_contacts 711-745): insert the new slots in order ----
+    // Each insertion shifts the larger-keyed slots up by one; the slot words and impulses
+    // are read four at a time ahead of the comparisons, so four shifts share one
+    // shared-memory latency.
     if (lane == 0) {
       for (uint32_t q = n_old; q < n; ++q) {
         const uint32_t w = meta[q * ne];
         const float x = imp[q * ne];
+        const uint32_t rk = sw_rank(w);
         uint32_t r = q;
-        while (r > 0 && sw_rank(meta[(r - 1) * ne]) > sw_rank(w)) {
-          meta[r * ne] = meta[(r - 1) * ne];
-          imp[r * ne] = imp[(r - 1) * ne];
-          --r;
+        while (r > 0) {
+          uint32_t mw[4];
+          float mi[4];
+#pragma unroll
+          for (uint32_t u = 0; u < 4; ++u) {
+            const uint32_t k = r > u ? r - 1 - u : 0u;
+            mw[u] = meta[k * ne];
+            mi[u] = imp[k * ne];
+          }
+          uint32_t shifted = 0;
+          bool stop = false;
+#pragma unroll
+          for (uint32_t u = 0; u < 4; ++u) {
+            if (stop || u >= r || sw_rank(mw[u]) <= rk) {
+              stop = true;
+              continue;
+            }
+            meta[(r - u) * ne] = mw[u];
+            imp[(r - u) * ne] = mi[u];
+            ++shifted;
+          }
+          r -= shifted;
+          if (stop) break;
         }
         moved |= r != q;
         meta[r * ne] = w;
