@@ -176,6 +176,13 @@ enum : uint32_t {
   kWriteJointState = 2u,  // publish joint positions / velocities
   kAccWritten = 4u,       // accelerations already written (auto-reset replaced the velocities)
 };
+// Deferred write-back of an environment whose sort moved slots (header word 2 after the
+// step: n_fin | n0 << 8 | these bits); the block writes its records once every group is done.
+enum : uint32_t {
+  kWbDeferred = 1u << 16,
+  kWbPublish = 1u << 17,  // into the contacts buffer (else into the step_subset cache)
+};
+constexpr uint32_t kWbParts = 12;  // 16-byte record parts staged per thread
 
 // Everything a group does for its environment between the cooperative load and store.
 // The block has already handed over the environments this kernel cannot represent.
@@ -634,10 +641,15 @@ __device__ __forceinline__ void run_env(const StepArgs& a, const FModel& f, cons
     // last contact; any other slot keeps the record stored at its original position,
     // marked invalid.  When sorting moved slots, the in-place write follows the
     // permutation's cycles (one lane) so that no record is overwritten before it is read.
+    // Environments whose sort moved slots and whose records fit the block's staging
+    // registers are written by the whole block after every group is done
+    // (write_back_moved: all reads first, then all writes); the rest here.
     const uint32_t n_fin = count < M ? count : M;
     Contact* dst = publish ? gc : a.prev_contacts + size_t(e) * M;
     const bool inplace = publish;
-    const uint32_t i0 = moved ? (lane == 0 ? 0u : n_fin) : lane;
+    const bool defer = moved && 4u * n_fin <= kWbParts * ne * uint32_t(L);
+    if (defer && lane == 0) hdr[2 * ne] = n_fin | (n0 << 8) | kWbDeferred | (publish ? kWbPublish : 0u);
+    const uint32_t i0 = defer ? n_fin : (moved ? (lane == 0 ? 0u : n_fin) : lane);
     const uint32_t istep = moved ? 1u : uint32_t(L);
     for (uint32_t i = i0; i < n_fin; i += istep) {
       if (meta[i * ne] & kVisited) continue;
@@ -789,6 +801,83 @@ __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
 }
 
+// Contact records of the block's deferred environments (their sort moved slots), one
+// environment at a time by the whole block: thread t stages parts t, t + nt, ... (part =
+// 16 bytes of a 64-byte record) that copy a stored record, the block synchronises, then
+// every part is written.  A slot whose pair made contact while in the list carries that
+// pair's last contact; any other slot gets the record stored at its original position,
+// marked invalid, with its own indices.  Since all reads precede all writes, the in-place
+// permutation needs no cycle walk.  run_env defers only environments with
+// 4 * n_fin <= kWbParts * nt, so every part has a staging register.
+__device__ __forceinline__ void write_back_moved(const StepArgs& a, const ModelS& m, const FPlan& pl,
+                                                 unsigned char* blk, uint32_t ne, uint32_t nb, uint32_t e0,
+                                                 uint32_t tid, uint32_t nt) {
+  const uint32_t* s_hdr = reinterpret_cast<const uint32_t*>(blk + pl.hdr * ne);
+  const uint32_t* s_meta = reinterpret_cast<const uint32_t*>(blk + pl.meta * ne);
+  const float* s_imp = reinterpret_cast<const float*>(blk + pl.imp * ne);
+  const float4* s_pp = reinterpret_cast<const float4*>(blk + pl.pp * ne);
+  const float4* s_nt = reinterpret_cast<const float4*>(blk + pl.nt * ne);
+  const uint8_t* s_nlh = blk + pl.nlh * ne;
+  const uint32_t M = a.M;
+  for (uint32_t el = 0; el < nb; ++el) {
+    const uint32_t d = s_hdr[2 * ne + el];  // the same for every thread
+    if (!(d & kWbDeferred)) continue;
+    const uint32_t n_fin = d & 0xFFu, n0 = (d >> 8) & 0xFFu, total = 4u * n_fin;
+    const bool pub = (d & kWbPublish) != 0;
+    const Contact* gc = a.contacts + size_t(e0 + el) * M;
+    Contact* dst = pub ? a.contacts + size_t(e0 + el) * M : a.prev_contacts + size_t(e0 + el) * M;
+    uint4 stash[kWbParts];
+#pragma unroll
+    for (uint32_t r = 0; r < kWbParts; ++r) {
+      const uint32_t t = tid + r * nt;
+      if (t >= total) continue;
+      const uint32_t j = t >> 2, w = s_meta[j * ne + el];
+      const uint32_t o = sw_origin(w), hh = sw_hit(w);
+      const bool hit = hh != fm::kNoHit && o < s_nlh[hh * ne + el];
+      if (!hit && !(pub && o == j)) stash[r] = reinterpret_cast<const uint4*>(gc + o)[t & 3u];
+    }
+    __syncthreads();
+#pragma unroll
+    for (uint32_t r = 0; r < kWbParts; ++r) {
+      const uint32_t t = tid + r * nt;
+      if (t >= total) continue;
+      const uint32_t j = t >> 2, part = t & 3u, w = s_meta[j * ne + el];
+      const uint32_t p = sw_pair(w), o = sw_origin(w), hh = sw_hit(w);
+      const bool hit = hh != fm::kNoHit && o < s_nlh[hh * ne + el];
+      uint4* out = reinterpret_cast<uint4*>(dst + j) + part;
+      uint4 idx = make_uint4(0u, 0u, 0u, 0u);
+      if (part == 2) {
+        const uint32_t pi = m.pinfo(p), pbody = m.pbody(p);
+        idx = make_uint4(pbody & 0xFFu, (pbody >> 8) & 0xFFu, pi & 0xFFu, (pi >> 8) & 0xFFu);
+      }
+      if (hit) {
+        uint4 v;
+        if (part == 0) {
+          v = *reinterpret_cast<const uint4*>(&s_pp[hh * ne + el]);
+        } else if (part == 1) {
+          const float4 nn = s_nt[hh * ne + el];
+          const float4 nf = make_float4(nn.x, nn.y, nn.z, m.hfr(hh));
+          v = *reinterpret_cast<const uint4*>(&nf);
+        } else if (part == 2) {
+          v = idx;
+        } else {
+          const float4 im = make_float4(s_imp[j * ne + el], 0.0f, 0.0f, a.restitution);
+          v = *reinterpret_cast<const uint4*>(&im);
+        }
+        *out = v;
+      } else if (pub && o == j) {
+        if (part == 0) reinterpret_cast<float*>(out)[3] = -1.0f;
+        else if (part == 2 && o >= n0) *out = idx;
+      } else {
+        uint4 v = stash[r];
+        if (part == 0) v.w = __float_as_uint(-1.0f);
+        if (part == 2) v = idx;
+        *out = v;
+      }
+    }
+  }
+}
+
 // blockDim.x = envs_per_block * L threads (envs_per_block <= 32); group g (= threadIdx.x / L)
 // owns env e0 + g.
 template <int L>
@@ -930,6 +1019,7 @@ __global__ void __launch_bounds__(32 * L) fast_step_kernel(const __grid_constant
     if (G.lane == 0) s_flags[g] = flags;
   }
   __syncthreads();
+  write_back_moved(a, m, pl, blk, ne, nb, e0, tid, nt);
 
   // ---- coalesced store: state, accelerations, joint torques and states ----
   for (uint32_t t = tid; t < nb * B; t += nt) {
