@@ -183,7 +183,7 @@ bool pack_fast_model(const HostModel& h, uint32_t max_contacts, uint32_t narrow_
   // and the type dispatch happens once per run instead of once per constraint.
   std::vector<uint32_t> runs;
   for (uint32_t col = 0; col < h.num_colors; ++col) {
-    const uint32_t start = h.color_ranges[2 * col], cnt = h.color_ranges[2 * col + 1];
+    const uint32_t start = h.kcolor_ranges[2 * col], cnt = h.kcolor_ranges[2 * col + 1];
     for (uint32_t k = start; k < start + cnt;) {
       const uint32_t t = h.constraints[k].type & 0xFFu;
       uint32_t n = 1;

@@ -298,7 +298,17 @@ bool build_model(const Scene& sc, HostModel* m, std::string* err) {
     if (h.color_ranges[2 * c + 1] == 0) h.color_ranges[2 * c] = i;
     h.color_ranges[2 * c + 1]++;
   }
-  for (const RefConstraint& r : tc) {
+  // Kernel copy.  An angular limit (type 4) whose range contains [-6.29, 6.29] never acts:
+  // the hinge angle is 2 atan2(.), within 2 pi in magnitude, so the violation is always 0
+  // (a NaN angle compares false as well) and the constraint changes nothing.  The
+  // reference's raw-radian MJCF ranges (Ant hips +-30, every Humanoid limit) are of this
+  // kind; dropping them from the colour runs leaves every other constraint's order and
+  // every result unchanged.
+  h.kcolor_ranges.assign(2 * h.num_colors, 0u);
+  for (uint32_t i = 0; i < uint32_t(tc.size()); ++i) {
+    const RefConstraint& r = tc[i];
+    const uint32_t type = r.indices[3] & 0xFFu;
+    if (type == 4 && r.limits[0] < -6.29f && r.limits[1] > 6.29f) continue;
     DConstraint d;
     std::memset(&d, 0, sizeof(d));
     d.body_a = r.indices[0], d.body_b = r.indices[1], d.type = r.indices[3];
@@ -306,8 +316,12 @@ bool build_model(const Scene& sc, HostModel* m, std::string* err) {
     std::memcpy(d.anchor_b, r.anchor_b, 16);
     std::memcpy(d.axis_target, r.axis_target, 16);
     std::memcpy(d.limits, r.limits, 16);
+    const uint32_t c = (r.indices[3] >> 8) & 0xFFu;
+    if (h.kcolor_ranges[2 * c + 1] == 0) h.kcolor_ranges[2 * c] = uint32_t(h.constraints.size());
+    h.kcolor_ranges[2 * c + 1]++;
     h.constraints.push_back(d);
   }
+  h.K = uint32_t(h.constraints.size());
   blob(h.ref_constraints, tc);
 
   // initial-state template (world.zig:663-691, env 0; state.zig:358-388)

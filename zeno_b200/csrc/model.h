@@ -25,8 +25,12 @@ struct HostModel {
   uint32_t grid_buckets = 32;
   std::vector<DActuator> actuators;
   std::vector<DSensor> sensors;
-  std::vector<DConstraint> constraints;  // colour-sorted
-  std::vector<uint32_t> color_ranges;    // (start, count) per colour
+  // Constraints the kernels solve: colour-sorted, without the angular limits no hinge angle
+  // can reach (kcolor_ranges: their (start, count) per colour; K: their number).
+  // color_ranges: the reference's ranges over every constraint (model parity tables).
+  std::vector<DConstraint> constraints;
+  std::vector<uint32_t> kcolor_ranges;
+  std::vector<uint32_t> color_ranges;
   std::vector<uint32_t> subtree;
   std::vector<float> init_state;         // B*4 pos, B*4 quat, B*4 vel, B*4 angvel, J jpos, J jvel
   bool actuators_unique = true;

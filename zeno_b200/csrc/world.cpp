@@ -128,7 +128,7 @@ World* World::create(const Scene& sc, const WorldConfig& cfg, std::string* err) 
   upload(&w->d_act_, m.actuators);
   upload(&w->d_sensors_, m.sensors);
   upload(&w->d_cons_, m.constraints);
-  upload(&w->d_colors_, m.color_ranges);
+  upload(&w->d_colors_, m.kcolor_ranges);
   upload(&w->d_subtree_, m.subtree);
   upload(&w->d_init_, m.init_state);
   upload(&w->d_bound_, m.geom_bound);
@@ -159,7 +159,7 @@ World* World::create(const Scene& sc, const WorldConfig& cfg, std::string* err) 
 void World::choose_fast_shape() {
   uint32_t steps1 = 0, steps2 = 0;
   for (uint32_t col = 0; col < model_.num_colors; ++col) {
-    const uint32_t c = model_.color_ranges[2 * col + 1];
+    const uint32_t c = model_.kcolor_ranges[2 * col + 1];
     steps1 += c;
     steps2 += (c + 1) / 2;
   }
