@@ -783,6 +783,17 @@ __device__ __forceinline__ void run_env(const StepArgs& a, const FModel& f, cons
   flags_out = flags;
 }
 
+// The second half of a 64-byte contact record (indices, impulses: one 32-byte sector) in
+// one 256-bit load; records are 64-byte aligned, so the address is 32-byte aligned.
+__device__ __forceinline__ void load_idx_imp(const Contact* c, uint4& ix, uint4& iq) {
+  uint32_t r0, r1, r2, r3, r4, r5, r6, r7;
+  asm volatile("ld.global.v8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3), "=r"(r4), "=r"(r5), "=r"(r6), "=r"(r7)
+               : "l"(reinterpret_cast<const unsigned char*>(c) + 32));
+  ix = make_uint4(r0, r1, r2, r3);
+  iq = make_uint4(r4, r5, r6, r7);
+}
+
 // Asynchronous global -> shared copies (cp.async, completion tracked per thread in commit
 // groups; wait_group N returns once at most N of the thread's groups are still pending).
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
@@ -964,8 +975,7 @@ __global__ void __launch_bounds__(32 * L) fast_step_kernel(const __grid_constant
     for (uint32_t u = 0; u < kU; ++u) {
       const uint32_t t = t0 + u * nt;
       if (t >= nb * M) continue;
-      ix[u] = *reinterpret_cast<const uint4*>(gcb[t].indices);
-      iq[u] = *reinterpret_cast<const uint4*>(gcb[t].impulses);
+      load_idx_imp(gcb + t, ix[u], iq[u]);
     }
 #pragma unroll
     for (uint32_t u = 0; u < kU; ++u) {
