@@ -554,13 +554,25 @@ __device__ __forceinline__ void run_env(const StepArgs& a, const FModel& f, cons
           G.sync();
         }
     }
-    // ---- velocities from the position change (xpbd_update_velocities 1922-1961) ----
-    for (uint32_t b = lane; b < B; b += L) {
-      if (m.imi(b).x < 1e-8f) continue;
-      S.vel(b) = with_w((v3(S.pos(b)) - v3(ppos[b * pst])) * inv_dt, 0.0f);
-      float4 dq = qmul(S.quat(b), qconj(pquat[b * pst]));
-      if (dq.w < 0.0f) dq = qneg(dq);
-      S.ang(b) = with_w((xyz(dq) * 2.0f) * inv_dt, 0.0f);
+    // ---- velocities from the position change (xpbd_update_velocities 1922-1961); the
+    //      saved poses (L2 scratch) of four bodies per round are loaded before any is used ----
+    constexpr uint32_t kV = 4 / L;  // bodies per lane per round
+    for (uint32_t b0 = lane; b0 < B; b0 += kV * L) {
+      float4 p0[kV], q0[kV];
+#pragma unroll
+      for (uint32_t u = 0; u < kV; ++u) {
+        const uint32_t b = b0 + u * L;
+        if (b < B) p0[u] = ppos[b * pst], q0[u] = pquat[b * pst];
+      }
+#pragma unroll
+      for (uint32_t u = 0; u < kV; ++u) {
+        const uint32_t b = b0 + u * L;
+        if (b >= B || m.imi(b).x < 1e-8f) continue;
+        S.vel(b) = with_w((v3(S.pos(b)) - v3(p0[u])) * inv_dt, 0.0f);
+        float4 dq = qmul(S.quat(b), qconj(q0[u]));
+        if (dq.w < 0.0f) dq = qneg(dq);
+        S.ang(b) = with_w((xyz(dq) * 2.0f) * inv_dt, 0.0f);
+      }
     }
     G.sync();
     prev_hit = hit_now;
