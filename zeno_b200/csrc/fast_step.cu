@@ -1014,11 +1014,27 @@ __global__ void __launch_bounds__(32 * L) fast_step_kernel(const __grid_constant
     }
   }
   __syncthreads();
-  for (uint32_t t = tid; t < nb * M; t += nt) {  // both lists sorted by key
-    const uint32_t el = t / M, i = t - el * M;
-    if (i == 0 || s_hdr[3 * ne + el]) continue;
-    if (i < s_hdr[el] && sw_rank(s_meta[(i - 1) * ne + el]) > sw_rank(s_meta[i * ne + el])) s_hdr[3 * ne + el] = 1;
-    if (i < s_hdr[ne + el] && s_aux[(i - 1) * ne + el] > s_aux[i * ne + el]) s_hdr[3 * ne + el] = 1;
+  // both lists sorted by key: one thread per environment walks its slots (at each slot
+  // index the threads read consecutive words)
+  for (uint32_t el = tid; el < nb; el += nt) {
+    if (s_hdr[3 * ne + el]) continue;
+    const uint32_t nc = min(s_hdr[el], M), np = min(s_hdr[ne + el], M);
+    bool bad = false;
+    uint32_t r0 = nc > 0 ? sw_rank(s_meta[el]) : 0u;
+#pragma unroll 8
+    for (uint32_t i = 1; i < nc; ++i) {
+      const uint32_t r1 = sw_rank(s_meta[i * ne + el]);
+      bad |= r0 > r1;
+      r0 = r1;
+    }
+    uint32_t a0 = np > 0 ? s_aux[el] : 0u;
+#pragma unroll 8
+    for (uint32_t i = 1; i < np; ++i) {
+      const uint32_t a1 = s_aux[i * ne + el];
+      bad |= a0 > a1;
+      a0 = a1;
+    }
+    if (bad) s_hdr[3 * ne + el] = 1;
   }
   cp_async_wait<0>();  // this thread's part of the body state and joint torques
   __syncthreads();
