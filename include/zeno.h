@@ -179,6 +179,16 @@ void* zeno_world_get_stream(ZenoWorldHandle world);
 int zeno_world_set_stream(ZenoWorldHandle world, void* cuda_stream);
 int zeno_world_device(ZenoWorldHandle world);
 
+/* The step outputs in device memory, for consumers on the GPU.  The reference getters
+ * zeno_world_get_observations / _rewards / _dones / _sensor_data return pinned host
+ * copies of these buffers instead: the first of them called after a step waits for the
+ * step and copies the stale outputs over in one round of DMA copies; later calls return
+ * at once.  (The reference's buffers are CPU/GPU shared memory; here a host read of
+ * device-resident managed memory would migrate it page by page.) */
+float* zeno_world_get_observations_device(ZenoWorldHandle world);
+float* zeno_world_get_rewards_device(ZenoWorldHandle world);
+uint8_t* zeno_world_get_dones_device(ZenoWorldHandle world);
+
 /* Episode task: rewards, dones and device-side auto reset.  The reference never writes
  * rewards or dones (state.zig:93-94 allocates them; no kernel fills them), so this is
  * off by default and the default behaviour matches the reference.  When enabled, after

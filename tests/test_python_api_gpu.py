@@ -211,3 +211,32 @@ def test_make_and_device_views():
         w.step_async(acts)
     s.synchronize()
     np.testing.assert_array_equal(obs_t.cpu().numpy(), w.get_observations())
+
+
+def test_output_host_copies_follow_the_device_buffers():
+    """The host getters return pinned copies of the device outputs, refreshed by the first
+    read after a step; rewards and dones are refreshed only when a step writes them (with
+    the task on), so without the task a host write persists as in the reference, whose
+    kernels never write them."""
+    import torch
+    w = ZenoWorld(mjcf_string=scenes.ant(), num_envs=256, substeps=4)
+    w.reset()
+    dev = {k: torch.as_tensor(w.device_array(k), device="cuda") for k in ("observations", "rewards", "dones")}
+    rng = np.random.default_rng(3)
+    o_zc = w.get_observations(zero_copy=True)
+    for s in range(3):
+        w.step(rng.uniform(-1, 1, (256, w.action_dim)).astype(np.float32))
+        w.step(rng.uniform(-1, 1, (256, w.action_dim)).astype(np.float32))  # two steps, one read
+        obs = w.get_observations()
+        np.testing.assert_array_equal(obs, dev["observations"].cpu().numpy())
+        np.testing.assert_array_equal(o_zc, obs)  # the same host buffer
+        np.testing.assert_array_equal(w.get_sensor_data(), obs)
+    rew = w._view(zeno_b200._ffi._lib.zeno_world_get_rewards(w.handle), (256,))
+    rew[:] = 7.0
+    w.step(np.zeros((256, w.action_dim), np.float32))
+    assert (w.get_rewards() == 7.0).all()
+    w.set_task(auto_reset=False, z_min=0.2, z_max=10.0)
+    w.step(np.zeros((256, w.action_dim), np.float32))
+    np.testing.assert_array_equal(w.get_rewards(), dev["rewards"].cpu().numpy())
+    np.testing.assert_array_equal(w.get_dones(), dev["dones"].cpu().numpy())
+    assert not (w.get_rewards() == 7.0).any()

@@ -92,6 +92,9 @@ ffi.cdef("""
     void* zeno_world_get_stream(ZenoWorldHandle world);
     int zeno_world_set_stream(ZenoWorldHandle world, void* cuda_stream);
     int zeno_world_device(ZenoWorldHandle world);
+    float* zeno_world_get_observations_device(ZenoWorldHandle world);
+    float* zeno_world_get_rewards_device(ZenoWorldHandle world);
+    uint8_t* zeno_world_get_dones_device(ZenoWorldHandle world);
     int zeno_world_set_task(ZenoWorldHandle world, const ZenoTaskConfig* task);
     int zeno_world_set_narrow_phase(ZenoWorldHandle world, uint32_t mode);
     uint32_t zeno_world_get_narrow_phase(ZenoWorldHandle world);
@@ -403,9 +406,9 @@ class ZenoWorld:
 
     # ---- device views (extension) ----
     _DEVICE = {
-        "observations": ("zeno_world_get_observations", lambda w: (w._num_envs, w._obs_dim), "<f4"),
-        "rewards": ("zeno_world_get_rewards", lambda w: (w._num_envs,), "<f4"),
-        "dones": ("zeno_world_get_dones", lambda w: (w._num_envs,), "|u1"),
+        "observations": ("zeno_world_get_observations_device", lambda w: (w._num_envs, w._obs_dim), "<f4"),
+        "rewards": ("zeno_world_get_rewards_device", lambda w: (w._num_envs,), "<f4"),
+        "dones": ("zeno_world_get_dones_device", lambda w: (w._num_envs,), "|u1"),
         "body_positions": ("zeno_world_get_body_positions", lambda w: (w._num_envs, w._num_bodies, 4), "<f4"),
         "body_quaternions": ("zeno_world_get_body_quaternions", lambda w: (w._num_envs, w._num_bodies, 4), "<f4"),
         "body_velocities": ("zeno_world_get_body_velocities", lambda w: (w._num_envs, w._num_bodies, 4), "<f4"),

@@ -109,9 +109,13 @@ int zeno_world_reset_to_state(ZenoWorldHandle world, const float* positions, con
   return W(world)->reset_to_state(positions, quaternions, velocities, angular_velocities, env_mask);
 }
 
-float* zeno_world_get_observations(ZenoWorldHandle world) { return world ? W(world)->obs : nullptr; }
-float* zeno_world_get_rewards(ZenoWorldHandle world) { return world ? W(world)->rewards : nullptr; }
-uint8_t* zeno_world_get_dones(ZenoWorldHandle world) { return world ? W(world)->dones : nullptr; }
+// host copies, refreshed by the first read after a step (World::host_obs)
+float* zeno_world_get_observations(ZenoWorldHandle world) { return world ? W(world)->host_obs() : nullptr; }
+float* zeno_world_get_rewards(ZenoWorldHandle world) { return world ? W(world)->host_rewards() : nullptr; }
+uint8_t* zeno_world_get_dones(ZenoWorldHandle world) { return world ? W(world)->host_dones() : nullptr; }
+float* zeno_world_get_observations_device(ZenoWorldHandle world) { return world ? W(world)->obs : nullptr; }
+float* zeno_world_get_rewards_device(ZenoWorldHandle world) { return world ? W(world)->rewards : nullptr; }
+uint8_t* zeno_world_get_dones_device(ZenoWorldHandle world) { return world ? W(world)->dones : nullptr; }
 uint32_t zeno_world_num_envs(ZenoWorldHandle world) { return world ? W(world)->config().num_envs : 0; }
 uint32_t zeno_world_num_bodies(ZenoWorldHandle world) { return world ? W(world)->model().B : 0; }
 uint32_t zeno_world_num_joints(ZenoWorldHandle world) { return world ? W(world)->model().J : 0; }

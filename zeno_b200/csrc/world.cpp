@@ -39,6 +39,18 @@ cudaError_t World::managed(T** p, size_t n) {
 }
 
 template <class T>
+cudaError_t World::pinned(T** p, size_t n) {
+  n = n ? n : 1;
+  void* q = nullptr;
+  cudaError_t e = cudaHostAlloc(&q, n * sizeof(T), cudaHostAllocDefault);
+  if (e != cudaSuccess) return e;
+  host_allocations_.push_back(q);
+  std::memset(q, 0, n * sizeof(T));
+  *p = static_cast<T*>(q);
+  return cudaSuccess;
+}
+
+template <class T>
 cudaError_t World::device_buf(T** p, size_t n) {
   n = n ? n : 1;
   void* q = nullptr;
@@ -104,9 +116,12 @@ World* World::create(const Scene& sc, const WorldConfig& cfg, std::string* err) 
   e = e ? e : w->managed(&w->jpos, size_t(E) * J1);
   e = e ? e : w->managed(&w->jvel, size_t(E) * J1);
   e = e ? e : w->managed(&w->jtorque, size_t(E) * J1);
-  e = e ? e : w->managed(&w->obs, size_t(E) * (m.obs_dim ? m.obs_dim : 1));
-  e = e ? e : w->managed(&w->rewards, E);
-  e = e ? e : w->managed(&w->dones, E);
+  e = e ? e : w->device_buf(&w->obs, size_t(E) * (m.obs_dim ? m.obs_dim : 1));
+  e = e ? e : w->device_buf(&w->rewards, E);
+  e = e ? e : w->device_buf(&w->dones, E);
+  e = e ? e : w->pinned(&w->h_obs_, size_t(E) * (m.obs_dim ? m.obs_dim : 1));
+  e = e ? e : w->pinned(&w->h_rewards_, E);
+  e = e ? e : w->pinned(&w->h_dones_, E);
   e = e ? e : w->managed(&w->contacts, size_t(E) * M);
   e = e ? e : w->managed(&w->counts, E);
   e = e ? e : w->device_buf(&w->prev_counts_, E);
@@ -189,8 +204,39 @@ void World::choose_fast_shape() {
 
 World::~World() {
   if (own_stream_) cudaStreamSynchronize(own_stream_);
+  if (stream_ && stream_ != own_stream_) cudaStreamSynchronize(stream_);
   for (void* p : allocations_) cudaFree(p);
+  for (void* p : host_allocations_) cudaFreeHost(p);
   if (own_stream_) cudaStreamDestroy(own_stream_);
+}
+
+cudaError_t World::refresh_outputs() {
+  if (!obs_stale_ && !task_stale_) return cudaSuccess;
+  const size_t E = cfg_.num_envs;
+  cudaError_t e = cudaSuccess;
+  if (obs_stale_) e = cudaMemcpyAsync(h_obs_, obs, E * model_.obs_dim * sizeof(float), cudaMemcpyDeviceToHost, out_stream_);
+  if (e == cudaSuccess && task_stale_) {
+    e = cudaMemcpyAsync(h_rewards_, rewards, E * sizeof(float), cudaMemcpyDeviceToHost, out_stream_);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(h_dones_, dones, E, cudaMemcpyDeviceToHost, out_stream_);
+  }
+  if (e == cudaSuccess) e = cudaStreamSynchronize(out_stream_);
+  if (e == cudaSuccess) obs_stale_ = task_stale_ = false;
+  return e;
+}
+
+float* World::host_obs() {
+  refresh_outputs();
+  return h_obs_;
+}
+
+float* World::host_rewards() {
+  refresh_outputs();
+  return h_rewards_;
+}
+
+uint8_t* World::host_dones() {
+  refresh_outputs();
+  return h_dones_;
 }
 
 StepArgs World::args(uint32_t substeps, const float* actions, const uint8_t* mask) const {
@@ -229,6 +275,11 @@ StepArgs World::args(uint32_t substeps, const float* actions, const uint8_t* mas
 
 cudaError_t World::launch(uint32_t substeps, const float* actions, const uint8_t* mask) {
   StepArgs a = args(substeps, actions, mask);
+  // host copies of what this step writes go stale (read_sensors writes every obs entry;
+  // rewards and dones only with the task on, as the reference never writes them)
+  obs_stale_ = obs_stale_ || model_.obs_dim > 0;
+  task_stale_ = task_stale_ || task_.enabled != 0;
+  out_stream_ = stream_;
   if (!use_fast_) return launch_step(a, lanes_, envs_per_block_, stream_);
   cudaError_t e = launch_fast_step(a, fmodel_, fast_lanes_, fast_epb_, stream_);
   if (e != cudaSuccess) return e;
