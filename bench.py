@@ -273,6 +273,28 @@ def run_e2e(w, pinned, acts, args, E, A, dist, barrier, world_size, torch):
     return e2e_value, h2d, int(d2h)
 
 
+def run_gather(w, dist, barrier, torch, reps=20):
+    """All-gather of every rank's observations, rewards and dones (zeno_b200.gather, NCCL
+    over NVLink / NVSwitch), timed with events on the gather's stream, max over ranks."""
+    from zeno_b200.gather import OutputGather
+    g = OutputGather.for_world(w)
+    for _ in range(3):
+        g.all_gather()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(g.stream)
+    for _ in range(reps):
+        g.all_gather()
+    e1.record(g.stream)
+    e1.synchronize()
+    ms = reduce_max(e0.elapsed_time(e1) / reps, dist, "cuda")
+    per_rank = sum(t.numel() * t.element_size() for t in g.inputs)
+    total = sum(t.numel() * t.element_size() for t in g.outputs)
+    return {"op": "all_gather of observations, rewards, dones onto every rank (NCCL), outside the timed steps",
+            "ms": ms, "bytes_per_rank": per_rank, "bytes_gathered": total,
+            "algbw_GBps": total / (ms / 1000.0) / 1e9}
+
+
 def run_ours(args, rank, world_size, local_rank):
     import torch
 
@@ -348,6 +370,9 @@ def run_ours(args, rank, world_size, local_rank):
     if pinned is not None:
         e2e_value, h2d, d2h = run_e2e(w, pinned, acts, args, E, A, dist, barrier, world_size, torch)
 
+    # ---- optional output gather (NCCL), after and outside the timed steps ----
+    gather = run_gather(w, dist, barrier, torch) if args.gather and dist else None
+
     if rank == 0:
         st = w.get_info()
         counts = w.get_contact_counts()
@@ -397,6 +422,8 @@ def run_ours(args, rank, world_size, local_rank):
             "dones_in_last_step": dones_seen,
             "mean_contact_count": float(counts.mean()),
         }
+        if gather:
+            line["gather"] = gather
         print(json.dumps(line), flush=True)
     if dist:
         dist.barrier()
@@ -417,6 +444,8 @@ def main():
     ap.add_argument("--broad", type=int, choices=[0, 1, 2], default=None, help="broad phase (default: the world's)")
     ap.add_argument("--narrow", type=int, choices=[0, 1, 2], default=None, help="narrow phase (default: the world's)")
     ap.add_argument("--semantics", choices=["reference", "corrected"], default="reference")
+    ap.add_argument("--gather", action="store_true",
+                    help="with N > 1: also time the optional NCCL all-gather of the step outputs (not in value)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
