@@ -159,6 +159,30 @@ def test_task_extension_bit_exact(auto_reset):
     assert saw_done
 
 
+@pytest.mark.parametrize("lanes,epb", [(1, 31), (2, 16)])
+def test_refilling_lists_bit_exact(lanes, epb):
+    """Contact lists refilling after auto-resets, in warps with enough active lanes to
+    merge a list cooperatively (70 envs: two full blocks, then a block of 8 or 6 envs that
+    sorts serially), every buffer bit-exact at every step."""
+    E = 70
+    w, o, c = make_pair("ant", E)
+    w.set_launch(lanes, epb)
+    kw = dict(body=1, z_min=0.2, z_max=1.0, auto_reset=True, noise=0.1, seed=5, env_offset=0)
+    w.set_task(**kw)
+    o.set_task(**kw)
+    rng = np.random.default_rng(33)
+    acts = actions(rng, 40, E, w.action_dim, 1.0)
+    resets = 0
+    for s in range(40):
+        w.step(acts[s])
+        o.step(acts[s])
+        st = product_state(w)
+        resets += int(st["dones"].sum())
+        bad = diff_report(st, o.state())
+        assert not bad, f"step {s}: {bad}"
+    assert resets >= 5
+
+
 @pytest.mark.parametrize("lanes,epb", [(1, 32), (1, 7), (1, 1), (2, 32), (2, 5), (2, 1), (8, 4), (16, 2), (32, 1)])
 def test_launch_shapes_agree(lanes, epb):
     """Every launch shape of both kernels computes the same bits: lanes 1, 2 run the

@@ -310,6 +310,9 @@ __device__ __forceinline__ void run_env(const StepArgs& a, const FModel& f, cons
     }
     // ---- broad phase (broad_phase 468-533): candidates in emission order ----
     const uint32_t n_old = count < M ? count : M;
+    uint32_t run_first = 0, run_last = 0;  // key ranks of the first and last appended slots
+    bool run_sorted = true;  // the appended slots are in key order (as emission order gives
+                             // when geoms are numbered in body order)
     for (uint32_t p0 = 0; p0 < P; p0 += 64) {
       const uint32_t pn = P - p0 < 64u ? P - p0 : 64u;
       uint64_t pass = 0;
@@ -335,16 +338,87 @@ __device__ __forceinline__ void run_env(const StepArgs& a, const FModel& f, cons
       while (pass) {
         const uint32_t i = uint32_t(__ffsll(pass)) - 1u;
         pass &= pass - 1;
-        if (count < M && lane == 0) meta[count * ne] = slot_word(m, p0 + i, count);
+        if (count < M) {
+          const uint32_t w = slot_word(m, p0 + i, count);
+          if (count == n_old) run_first = sw_rank(w);
+          run_sorted &= sw_rank(w) >= run_last;
+          run_last = sw_rank(w);
+          if (lane == 0) meta[count * ne] = w;
+        }
         ++count;
       }
     }
     const uint32_t n = count < M ? count : M;
-    // ---- stable sort by key (sort_contacts 711-745): insert the new slots in order ----
-    // Each insertion shifts the larger-keyed slots up by one; the slot words and impulses
-    // are read four at a time ahead of the comparisons, so four shifts share one
-    // shared-memory latency.
-    if (lane == 0) {
+    // ---- stable sort by key (sort_contacts 711-745) ----
+    // The stored slots [0, n_old) are sorted.  When the appended run [n_old, n) is sorted
+    // too, the stable sort is a merge: an old slot i lands at i + #(appended with a
+    // smaller key), an appended slot q at #(old with a key <= its key) + (q - n_old).
+    // Nothing moves when the run starts at or above the last old key (the first substep
+    // after a reset, a list that only grows at its end).  Lists that do move are merged
+    // by the whole warp, one list at a time: each active lane takes up to three slots,
+    // finds their places by binary search in the other run, and all lanes scatter after a
+    // warp barrier (so the list needs no scratch).  Unsorted runs, and warps with too few
+    // active lanes for the list, take the serial insertion sort below.
+    bool need_merge = false;
+    if (run_sorted && n > n_old && n_old > 0) need_merge = run_first < sw_rank(meta[(n_old - 1) * ne]);
+    const uint32_t nact = __popc(G.mask);
+    const bool coop = need_merge && 3u * nact >= M;
+    uint32_t todo = __ballot_sync(G.mask, coop && lane == 0);
+    if (todo) {  // warp-uniform
+      const uint32_t wl = threadIdx.x & 31u;
+      const uint32_t idx = __popc(G.mask & ((1u << wl) - 1u));
+      const uint32_t nbits = 32u - __clz(M);  // binary-search rounds for ranges of up to M slots
+      __syncwarp(G.mask);  // the appended slot words of every group are in place
+      do {
+        const int src = __ffs(todo) - 1;
+        todo &= todo - 1;
+        const uint32_t gs = ((threadIdx.x & ~31u) + uint32_t(src)) / L;
+        const uint32_t so = __shfl_sync(G.mask, n_old, src), sn = __shfl_sync(G.mask, n, src);
+        uint32_t* mt = reinterpret_cast<uint32_t*>(blk + pl.meta * ne) + gs;
+        float* ip = reinterpret_cast<float*>(blk + pl.imp * ne) + gs;
+        uint32_t w[3], lo[3], hi[3], thr[3];
+        float x[3];
+#pragma unroll
+        for (uint32_t u = 0; u < 3; ++u) {
+          const uint32_t sl = idx + u * nact;
+          const bool have = sl < sn;
+          w[u] = have ? mt[sl * ne] : 0u;
+          x[u] = have ? ip[sl * ne] : 0.0f;
+          // old slot: count appended slots with rank < its rank; appended slot: count
+          // old slots with rank <= its rank (rank < rank + 1)
+          const bool old_slot = sl < so;
+          lo[u] = have ? (old_slot ? so : 0u) : 0u;
+          hi[u] = have ? (old_slot ? sn : so) : 0u;
+          thr[u] = sw_rank(w[u]) + (old_slot ? 0u : 1u);
+        }
+        for (uint32_t it = 0; it < nbits; ++it) {
+#pragma unroll
+          for (uint32_t u = 0; u < 3; ++u) {
+            const uint32_t mid = (lo[u] + hi[u]) >> 1;
+            const uint32_t r = sw_rank(mt[(mid < M ? mid : M - 1u) * ne]);
+            if (lo[u] < hi[u]) {
+              if (r < thr[u]) lo[u] = mid + 1u;
+              else hi[u] = mid;
+            }
+          }
+        }
+        __syncwarp(G.mask);
+#pragma unroll
+        for (uint32_t u = 0; u < 3; ++u) {
+          const uint32_t sl = idx + u * nact;
+          if (sl >= sn) continue;
+          const uint32_t pos = sl < so ? sl + (lo[u] - so) : lo[u] + (sl - so);
+          mt[pos * ne] = w[u];
+          ip[pos * ne] = x[u];
+        }
+        __syncwarp(G.mask);
+      } while (todo);
+    }
+    moved |= coop;
+    // Serial insertion: each insertion shifts the larger-keyed slots up by one; the slot
+    // words and impulses are read four at a time ahead of the comparisons, so four shifts
+    // share one shared-memory latency.
+    if (lane == 0 && !coop && n > n_old && (need_merge || !run_sorted)) {
       for (uint32_t q = n_old; q < n; ++q) {
         const uint32_t w = meta[q * ne];
         const float x = imp[q * ne];
