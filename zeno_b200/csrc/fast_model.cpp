@@ -134,6 +134,14 @@ bool pack_fast_model(const HostModel& h, uint32_t max_contacts, uint32_t narrow_
   }
   m.P = P, m.H = H, m.G = h.G;
   m.narrow_mode = narrow_mode;
+  {
+    std::vector<uint8_t> seen(256, 0);
+    m.hit_keys_unique = 1;
+    for (uint32_t hh = 0; hh < H; ++hh) {
+      const uint32_t rank = m.p_info[m.h_pair[hh]] >> 24;
+      if (seen[rank]++) m.hit_keys_unique = 0;
+    }
+  }
 
   // hot image
   std::vector<uint8_t>& img = *hot;

@@ -60,6 +60,10 @@ struct FModel {
   uint32_t s_info[fm::kS];  // type | object << 8 | obs offset << 16
   uint32_t P, H, G;
   uint32_t narrow_mode;  // 0: reference GPU narrow phase; 1: its CPU detectCollision
+  // 1 when no two hittable candidates share a sort key (body pair): the warm-start match
+  // of a hittable then reads only its own previous point, so one narrow-phase pass can
+  // match and store (else a second pass stores once every match has read)
+  uint32_t hit_keys_unique;
   // The tables read inside the substep loop, packed contiguously ("hot image"): the
   // kernel copies them into shared memory once per block, where warp-uniform reads are
   // broadcasts that never miss.  Byte offsets into the image (16-byte aligned sections):

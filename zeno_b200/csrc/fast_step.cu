@@ -316,18 +316,17 @@ __device__ __forceinline__ void run_env(const StepArgs& a, const FModel& f, cons
     for (uint32_t p0 = 0; p0 < P; p0 += 64) {
       const uint32_t pn = P - p0 < 64u ? P - p0 : 64u;
       uint64_t pass = 0;
+      // branch-free, so that the loads of several candidates are in flight together: the
+      // distance test is evaluated for plane pairs too and discarded (they always pass)
 #pragma unroll 4
       for (uint32_t i = lane; i < pn; i += L) {
         const uint32_t p = p0 + i;
         const uint32_t pb = m.pbody(p);
-        bool ok = true;
-        if (!(pb >> 16)) {
-          const uint32_t pi = m.pinfo(p);
-          const V3 pa = v3(S.pos(pb & 0xFFu)) + v3(m.gps(pi & 0xFFu));
-          const V3 pc = v3(S.pos((pb >> 8) & 0xFFu)) + v3(m.gps((pi >> 8) & 0xFFu));
-          const V3 d = pc - pa;
-          ok = !(dot(d, d) >= m.pmd2(p));
-        }
+        const uint32_t pi = m.pinfo(p);
+        const V3 pa = v3(S.pos(pb & 0xFFu)) + v3(m.gps(pi & 0xFFu));
+        const V3 pc = v3(S.pos((pb >> 8) & 0xFFu)) + v3(m.gps((pi >> 8) & 0xFFu));
+        const V3 d = pc - pa;
+        const bool ok = ((pb >> 16) != 0u) | !(dot(d, d) >= m.pmd2(p));
         pass |= uint64_t(ok) << i;
       }
       pass = G.or_all(pass);
@@ -455,12 +454,19 @@ __device__ __forceinline__ void run_env(const StepArgs& a, const FModel& f, cons
     }
     G.sync();
     // ---- narrow phase + warm start (narrow_phase 751-894, match_cached_contacts
-    //      1483-1544), once per hittable pair.  First pass: the match, against the
-    //      previous substep's points, which the second pass then overwrites.
+    //      1483-1544), once per hittable pair.  The match reads the previous substep's
+    //      points of the pairs with this pair's key.  When no two hittable pairs share a
+    //      key, that is only this pair's own point, so one pass matches and then stores;
+    //      otherwise this pass only matches and a second one stores.
+    const bool one_pass = m.f.hit_keys_unique != 0;
+    uint64_t hit_now = 0;
     for (uint32_t h = lane; h < H; h += L) {
       V3 point, normal;
       float pen;
-      if (!narrow_h(m, h, S, point, normal, pen)) continue;
+      if (!narrow_h(m, h, S, point, normal, pen)) {
+        if (one_pass) reinterpret_cast<float*>(&pp[h * ne])[3] = -1.0f;
+        continue;
+      }
       const uint32_t rank = m.pinfo(m.hpair(h)) >> 24;
       float best = 0.04f;
       int js = -1;
@@ -506,11 +512,17 @@ __device__ __forceinline__ void run_env(const StepArgs& a, const FModel& f, cons
         }
         if (js >= 0) val = imp[uint32_t(js) * ne] * 0.8f;
       }
-      reinterpret_cast<float*>(&nt[h * ne])[3] = val;
+      if (one_pass) {
+        pp[h * ne] = with_w(point, pen);
+        nt[h * ne] = with_w(normal, val);
+        nlh[h * ne] = uint8_t(n);
+        hit_now |= 1ull << h;
+      } else {
+        reinterpret_cast<float*>(&nt[h * ne])[3] = val;
+      }
     }
     G.sync();
-    uint64_t hit_now = 0;
-    for (uint32_t h = lane; h < H; h += L) {
+    for (uint32_t h = lane; h < H && !one_pass; h += L) {
       V3 point, normal;
       float pen;
       if (narrow_h(m, h, S, point, normal, pen)) {
@@ -533,11 +545,17 @@ __device__ __forceinline__ void run_env(const StepArgs& a, const FModel& f, cons
     // the previous substep when neither changed (aux holds it from substep 1 on).
     const bool reuse = s > 0 && n == n_prev && hit_now == prev_hit;
     if constexpr (L == 1) {
-      if (!reuse) {
+      if (!reuse) {  // eight slot words per shared-memory round trip
         nh = 0;
-        for (uint32_t i = 0; i < n; ++i) {
-          const uint32_t hh = sw_hit(meta[i * ne]);
-          if (hh != fm::kNoHit && ((hit_now >> hh) & 1ull)) aux[nh++ * ne] = uint8_t(i);
+        for (uint32_t i0 = 0; i0 < n; i0 += 8) {
+          uint32_t w8[8];
+#pragma unroll
+          for (uint32_t u = 0; u < 8; ++u) w8[u] = i0 + u < n ? meta[(i0 + u) * ne] : (fm::kNoHit << 16);
+#pragma unroll
+          for (uint32_t u = 0; u < 8; ++u) {
+            const uint32_t hh = sw_hit(w8[u]);
+            if (hh != fm::kNoHit && ((hit_now >> hh) & 1ull)) aux[nh++ * ne] = uint8_t(i0 + u);
+          }
         }
       }
     } else {
@@ -584,10 +602,21 @@ __device__ __forceinline__ void run_env(const StepArgs& a, const FModel& f, cons
       G.sync();
       nh = lofs[nlev * ne];
     }
-    // slot impulses of the hit slots (narrow zeroes them, a match warm-starts them)
-    for (uint32_t v = lane; v < nh; v += L) {
-      const uint32_t i = aux[v * ne];
-      imp[i * ne] = nt[sw_hit(meta[i * ne]) * ne].w;
+    // slot impulses of the hit slots (narrow zeroes them, a match warm-starts them); four
+    // slots' dependent loads (schedule -> slot word -> pair impulse) per round
+    for (uint32_t v0 = lane; v0 < nh; v0 += 4 * L) {
+      uint32_t i4[4];
+      float w4[4];
+#pragma unroll
+      for (uint32_t u = 0; u < 4; ++u) i4[u] = v0 + u * L < nh ? aux[(v0 + u * L) * ne] : 0u;
+#pragma unroll
+      for (uint32_t u = 0; u < 4; ++u) {  // (listed slots are hit, so their pair index is valid)
+        const uint32_t hh = v0 + u * L < nh ? sw_hit(meta[i4[u] * ne]) : 0u;
+        w4[u] = nt[hh * ne].w;
+      }
+#pragma unroll
+      for (uint32_t u = 0; u < 4; ++u)
+        if (v0 + u * L < nh) imp[i4[u] * ne] = w4[u];
     }
     // ---- XPBD joints (solve_joints 909-1399): colour by colour, as runs of one type; a
     //      run's constraints (one colour: disjoint bodies) split across the lanes.  With
