@@ -114,6 +114,13 @@ __device__ __forceinline__ uint32_t lookup_pair(const ModelS& m, uint4 ix) {
   return p;
 }
 
+// 32 bytes (two 16-byte parts) to a 32-byte aligned global address in one 256-bit store.
+__device__ __forceinline__ void store32(void* p, uint4 a, uint4 b) {
+  asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(p), "r"(a.x), "r"(a.y), "r"(a.z),
+               "r"(a.w), "r"(b.x), "r"(b.y), "r"(b.z), "r"(b.w)
+               : "memory");
+}
+
 // Body state of one environment (stride: environments per block).
 struct EnvBodies {
   float4 *p, *q, *v, *w;
@@ -764,7 +771,52 @@ __device__ __forceinline__ void run_env(const StepArgs& a, const FModel& f, cons
     const bool inplace = publish;
     const bool defer = moved && 4u * n_fin <= kWbParts * ne * uint32_t(L);
     if (defer && lane == 0) hdr[2 * ne] = n_fin | (n0 << 8) | kWbDeferred | (publish ? kWbPublish : 0u);
-    const uint32_t i0 = defer ? n_fin : (moved ? (lane == 0 ? 0u : n_fin) : lane);
+    if (inplace && !moved) {
+      // every slot is at its original position: the records are independent, so four
+      // slots' shared-memory reads are in flight together (no visited marks needed)
+      for (uint32_t j0 = lane; j0 < n_fin; j0 += 4 * L) {
+        uint32_t w4[4], pi4[4], pb4[4];
+        bool hit4[4];
+#pragma unroll
+        for (uint32_t u = 0; u < 4; ++u) w4[u] = j0 + u * L < n_fin ? meta[(j0 + u * L) * ne] : (fm::kNoHit << 16);
+#pragma unroll
+        for (uint32_t u = 0; u < 4; ++u) {
+          const uint32_t hh = sw_hit(w4[u]);
+          pi4[u] = m.pinfo(sw_pair(w4[u]));
+          pb4[u] = m.pbody(sw_pair(w4[u]));
+          hit4[u] = hh != fm::kNoHit && sw_origin(w4[u]) < nlh[(hh != fm::kNoHit ? hh : 0u) * ne];
+        }
+#pragma unroll
+        for (uint32_t u = 0; u < 4; ++u) {
+          const uint32_t j = j0 + u * L;
+          if (j >= n_fin) continue;
+          const uint32_t o = sw_origin(w4[u]), hh = sw_hit(w4[u]);
+          const uint4 idx = make_uint4(pb4[u] & 0xFFu, (pb4[u] >> 8) & 0xFFu, pi4[u] & 0xFFu, (pi4[u] >> 8) & 0xFFu);
+          uint4* out = reinterpret_cast<uint4*>(dst + j);
+          if (hit4[u]) {
+            const float4 nn = nt[hh * ne];
+            const float4 nf = make_float4(nn.x, nn.y, nn.z, m.hfr(hh));
+            const uint4 p0 = *reinterpret_cast<const uint4*>(&pp[hh * ne]), p1 = *reinterpret_cast<const uint4*>(&nf);
+            const float4 im = make_float4(imp[j * ne], 0.0f, 0.0f, a.restitution);
+            const uint4 p3 = *reinterpret_cast<const uint4*>(&im);
+            if constexpr (L == 1) {
+              store32(out, p0, p1);
+              if (o < n0) out[3] = p3;
+              else store32(out + 2, idx, p3);
+            } else {
+              out[0] = p0;
+              out[1] = p1;
+              if (o >= n0) out[2] = idx;
+              out[3] = p3;
+            }
+          } else {
+            reinterpret_cast<float*>(out)[3] = -1.0f;
+            if (o >= n0) out[2] = idx;  // a slot loaded at this position keeps its stored tuple
+          }
+        }
+      }
+    }
+    const uint32_t i0 = (defer || (inplace && !moved)) ? n_fin : (moved ? (lane == 0 ? 0u : n_fin) : lane);
     const uint32_t istep = moved ? 1u : uint32_t(L);
     for (uint32_t i = i0; i < n_fin; i += istep) {
       if (meta[i * ne] & kVisited) continue;
@@ -782,13 +834,25 @@ __device__ __forceinline__ void run_env(const StepArgs& a, const FModel& f, cons
         const uint4 idx = make_uint4(pbody & 0xFFu, (pbody >> 8) & 0xFFu, pi & 0xFFu, (pi >> 8) & 0xFFu);
         uint4* out = reinterpret_cast<uint4*>(dst + j);
         if (hh != fm::kNoHit && o < nlh[hh * ne]) {
+          // a slot loaded at this position keeps its stored tuple (the loader matched it
+          // exactly), so then only the impulses follow the point and normal.  One lane:
+          // 256-bit stores (with two lanes their operands spill registers).
           const float4 nn = nt[hh * ne];
-          out[0] = *reinterpret_cast<const uint4*>(&pp[hh * ne]);
           const float4 nf = make_float4(nn.x, nn.y, nn.z, m.hfr(hh));
-          out[1] = *reinterpret_cast<const uint4*>(&nf);
-          out[2] = idx;
+          const uint4 p0 = *reinterpret_cast<const uint4*>(&pp[hh * ne]), p1 = *reinterpret_cast<const uint4*>(&nf);
           const float4 im = make_float4(imp[j * ne], 0.0f, 0.0f, a.restitution);
-          out[3] = *reinterpret_cast<const uint4*>(&im);
+          const uint4 p3 = *reinterpret_cast<const uint4*>(&im);
+          const bool same_tuple = inplace && o == j && o < n0;
+          if constexpr (L == 1) {
+            store32(out, p0, p1);
+            if (same_tuple) out[3] = p3;
+            else store32(out + 2, idx, p3);
+          } else {
+            out[0] = p0;
+            out[1] = p1;
+            if (!same_tuple) out[2] = idx;
+            out[3] = p3;
+          }
         } else if (inplace && o == j) {
           reinterpret_cast<float*>(out)[3] = -1.0f;
           if (o >= n0) out[2] = idx;  // a slot loaded at this position keeps its stored tuple
