@@ -890,6 +890,10 @@ __global__ void __launch_bounds__(256, 1) step_kernel(StepArgs a) {
     return;
   }
   const uint32_t cnt = *a.env_count;
+  // Nothing handed over (the normal case): nothing to step and no count to clear.  The
+  // count is written only before this launch and cleared after every block has read it,
+  // so all blocks see the same value.
+  if (cnt == 0) return;
   for (uint32_t i = blockIdx.x * NE + g; i < cnt; i += gridDim.x * NE) step_env<L>(a, a.env_list[i], smem_raw, g, l);
   __syncthreads();
   if (threadIdx.x == 0) {
