@@ -357,6 +357,57 @@ BOX_CAPSULE = """<mujoco model="box_capsule">
 """
 
 
+SHARED_KEYS = """<mujoco model="shared_keys">
+  <option timestep="0.01" gravity="0 0 -9.81"/>
+  <worldbody>
+    <geom name="floor" type="plane" size="5 5 0.1"/>
+    <body name="bell" pos="0 0 0.6">
+      <freejoint/>
+      <geom type="sphere" size="0.1" pos="-0.2 0 0"/>
+      <geom type="sphere" size="0.1" pos="0.2 0 0.05"/>
+    </body>
+    <body name="hammer" pos="0.3 0 0.9">
+      <freejoint/>
+      <geom type="sphere" size="0.12" pos="0 0 -0.15"/>
+      <geom type="capsule" size="0.05 0.15" pos="0 0 0.1"/>
+    </body>
+  </worldbody>
+</mujoco>"""
+
+
+@pytest.mark.parametrize("lanes,epb", [(1, 31), (2, 16)])
+@pytest.mark.parametrize("mode", [0, 1])
+def test_shared_key_pairs_bit_exact(lanes, epb, mode):
+    """Two hittable pairs on one body pair (each body's two geoms against the plane and
+    against each other): the warm-start match of one pair reads the other's previous
+    point, so the compressed-state kernel runs its narrow phase in two passes.  Bit-exact
+    against the oracle while the bodies drop, land, tip and settle (40 envs: full warps,
+    so refilling lists are merged cooperatively)."""
+    E = 40
+    kw = dict(num_envs=E, substeps=4, max_contacts_per_env=32)
+    w, o = ZenoWorld(mjcf_string=SHARED_KEYS, **kw), OracleWorld(SHARED_KEYS, **kw)
+    w.set_narrow_phase(mode)
+    assert o.set_narrow_phase(mode) == 0
+    w.set_launch(lanes, epb)
+    assert w.get_launch() == (lanes, epb)
+    rng = np.random.default_rng(8)
+    st0 = product_state(w)
+    pos, quat = st0["positions"].copy(), st0["quaternions"].copy()
+    pos[:, 1:, :3] += rng.uniform(-0.05, 0.05, size=(E, pos.shape[1] - 1, 3)).astype(np.float32)
+    w.reset_to_state(pos, quat)
+    o.reset_to_state(pos, quat)
+    none = np.zeros((E, 0), np.float32)
+    hits = 0
+    for s in range(60):
+        w.step(none)
+        o.step(none)
+        st = product_state(w)
+        bad = diff_report(st, o.state())
+        assert not bad, f"step {s}: {bad}"
+        hits += int((st["contacts"]["position_pen"][..., 3] >= 0).sum())
+    assert hits > 0
+
+
 @pytest.mark.parametrize("lanes", [8, 32])
 def test_gjk_box_capsule_scene(lanes):
     """Capsules resting on and under boxes: with narrow phase 2 the box-capsule pairs go
