@@ -181,9 +181,10 @@ int zeno_world_device(ZenoWorldHandle world);
 
 /* The step outputs in device memory, for consumers on the GPU.  The reference getters
  * zeno_world_get_observations / _rewards / _dones / _sensor_data return pinned host
- * copies of these buffers instead: the first of them called after a step waits for the
- * step and copies the stale outputs over in one round of DMA copies; later calls return
- * at once.  (The reference's buffers are CPU/GPU shared memory; here a host read of
+ * copies of these buffers instead.  zeno_world_step copies the outputs right behind its
+ * kernel, before it returns; after zeno_world_step_async the first of these getters waits
+ * for the step and copies the stale outputs over in one round of DMA copies, and later
+ * calls return at once.  (The reference's buffers are CPU/GPU shared memory; here a host read of
  * device-resident managed memory would migrate it page by page.) */
 float* zeno_world_get_observations_device(ZenoWorldHandle world);
 float* zeno_world_get_rewards_device(ZenoWorldHandle world);

@@ -1084,6 +1084,19 @@ __global__ void __launch_bounds__(32 * L) fast_step_kernel(const __grid_constant
   // shared memory: the model's hot image, then the per-environment sections
   unsigned char* hot = smem_raw;
   unsigned char* blk = smem_raw + f.hot_bytes;
+  // With one lane per environment the slot loader's first round (below) is issued before
+  // anything else: its addresses need neither the image nor the list headers, which take
+  // two memory round trips.  (With two lanes the held registers would spill.)
+  const Contact* gcb = a.contacts + size_t(e0) * M;
+  constexpr uint32_t kU = 8;  // slots per thread per round: their loads are in flight together
+  uint4 ix[kU], iq[kU];
+  if constexpr (L == 1) {
+#pragma unroll
+    for (uint32_t u = 0; u < kU; ++u) {
+      const uint32_t t = tid + u * nt;
+      if (t < nb * M) load_idx_imp(gcb + t, ix[u], iq[u]);
+    }
+  }
   // the hot image and (below) the block's state arrive by cp.async, all copies in flight at once
   for (uint32_t t = tid; t < f.hot_bytes / 16u; t += nt) cp_async16(reinterpret_cast<uint4*>(hot) + t, f.hot + t);
   cp_async_commit();
@@ -1141,20 +1154,18 @@ __global__ void __launch_bounds__(32 * L) fast_step_kernel(const __grid_constant
   }
   __syncthreads();
   const ModelS m{hot, f};
-  const Contact* gcb = a.contacts + size_t(e0) * M;
-  constexpr uint32_t kU = 8;  // slots per thread per round: their loads are in flight together
   // An environment is handed over (s_hdr[3] set) when a slot tuple of either list is not
   // a broad-phase candidate, when a list is not sorted by key, or when a slot of the
   // previous list carries non-zero tangent impulses (a warm start would copy them; this
   // kernel keeps only normal impulses).  This library never writes any of these.  Only
   // the second half of each 64-byte record (indices, impulses) is read.
   for (uint32_t t0 = tid; t0 < nb * M; t0 += kU * nt) {
-    uint4 ix[kU], iq[kU];
+    if (L != 1 || t0 != tid) {
 #pragma unroll
-    for (uint32_t u = 0; u < kU; ++u) {
-      const uint32_t t = t0 + u * nt;
-      if (t >= nb * M) continue;
-      load_idx_imp(gcb + t, ix[u], iq[u]);
+      for (uint32_t u = 0; u < kU; ++u) {
+        const uint32_t t = t0 + u * nt;
+        if (t < nb * M) load_idx_imp(gcb + t, ix[u], iq[u]);
+      }
     }
 #pragma unroll
     for (uint32_t u = 0; u < kU; ++u) {

@@ -210,8 +210,7 @@ World::~World() {
   if (own_stream_) cudaStreamDestroy(own_stream_);
 }
 
-cudaError_t World::refresh_outputs() {
-  if (!obs_stale_ && !task_stale_) return cudaSuccess;
+cudaError_t World::queue_output_copies() {
   const size_t E = cfg_.num_envs;
   cudaError_t e = cudaSuccess;
   if (obs_stale_) e = cudaMemcpyAsync(h_obs_, obs, E * model_.obs_dim * sizeof(float), cudaMemcpyDeviceToHost, out_stream_);
@@ -219,6 +218,12 @@ cudaError_t World::refresh_outputs() {
     e = cudaMemcpyAsync(h_rewards_, rewards, E * sizeof(float), cudaMemcpyDeviceToHost, out_stream_);
     if (e == cudaSuccess) e = cudaMemcpyAsync(h_dones_, dones, E, cudaMemcpyDeviceToHost, out_stream_);
   }
+  return e;
+}
+
+cudaError_t World::refresh_outputs() {
+  if (!obs_stale_ && !task_stale_) return cudaSuccess;
+  cudaError_t e = queue_output_copies();
   if (e == cudaSuccess) e = cudaStreamSynchronize(out_stream_);
   if (e == cudaSuccess) obs_stale_ = task_stale_ = false;
   return e;
@@ -311,8 +316,13 @@ cudaError_t World::step(const float* actions, uint32_t substeps, bool async) {
   cudaError_t e = launch(ns, dev_actions, nullptr);
   if (e != cudaSuccess) return e;
   if (async) return cudaSuccess;
+  // the synchronous step (the reference's) is followed by reads of its outputs: their
+  // host copies ride behind the kernel and share its synchronization
+  e = queue_output_copies();
+  if (e != cudaSuccess) return e;
   e = cudaStreamSynchronize(stream_);
   if (e != cudaSuccess) return e;
+  obs_stale_ = task_stale_ = false;
   if (cfg_.enable_profiling) {
     prof_.total_step_ns =
         float(std::chrono::duration_cast<std::chrono::nanoseconds>(std::chrono::steady_clock::now() - t0).count());

@@ -81,10 +81,11 @@ class World {
   bool fast_available() const { return fast_ok_; }
 
   // Host copies of the step outputs (pinned memory), returned by the ABI getters.  The
-  // first read after a step brings all stale outputs over in one round of DMA copies
-  // on the stream the step ran on; a host read of managed memory would instead migrate
-  // the pages one fault at a time (1.5 ms for Ant's 16384 x 29 observations, four
-  // times the step).  Host writes to a copy last until the next step that produces it.
+  // synchronous step copies them right behind its kernel; after an asynchronous step the
+  // first read brings all stale outputs over in one round of DMA copies on the stream
+  // the step ran on.  (A host read of managed memory would instead migrate
+  // the pages one fault at a time: 1.5 ms for Ant's 16384 x 29 observations, four
+  // times the step.)  Host writes to a copy last until the next step that produces it.
   float* host_obs();
   float* host_rewards();
   uint8_t* host_dones();
@@ -116,6 +117,7 @@ class World {
   cudaError_t device_buf(T** p, size_t n);
   template <class T>
   cudaError_t pinned(T** p, size_t n);
+  cudaError_t queue_output_copies();  // stale outputs -> host copies, on the last step's stream
   cudaError_t refresh_outputs();
 
   Scene scene_;
