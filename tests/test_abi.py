@@ -108,3 +108,25 @@ def test_missing_file_returns_null(L):
     cfg = ZenoConfig(1, 0.0, 4, 64, 42, 1, False, 0, 0, 0)
     L.zeno_world_create.restype = ctypes.c_void_p
     assert L.zeno_world_create(b"/nonexistent/model.xml", ctypes.byref(cfg)) is None
+
+
+def test_missing_library_fails_loudly_but_build_imports():
+    """Without libzeno.so the package has no fallback: every library-backed name raises
+    ImportError, while the build module and the pure-Python scenes still import (a fresh
+    checkout must be able to run `python -m zeno_b200.build`)."""
+    import subprocess
+    import sys
+    from pathlib import Path
+    root = Path(__file__).resolve().parents[1]
+    code = (
+        "import zeno_b200, zeno_b200.build, zeno_b200.scenes\n"
+        "try:\n"
+        "    from zeno_b200 import ZenoWorld\n"
+        "except ImportError as e:\n"
+        "    assert 'libzeno.so not found' in str(e), e\n"
+        "    print('loud')\n"
+    )
+    env = dict(__import__("os").environ, ZENO_B200_LIB=str(root / "no_such_dir" / "libzeno.so"))
+    out = subprocess.run([sys.executable, "-c", code], cwd=root, env=env, capture_output=True, text=True, timeout=120)
+    assert out.returncode == 0, out.stderr
+    assert out.stdout.strip() == "loud"
