@@ -573,34 +573,78 @@ __device__ __forceinline__ void step_env(const StepArgs& a, uint32_t e, unsigned
       grid = c != kNoCell;
       if (grid) count = c;
     }
-    for (uint32_t r = 0; r < (grid ? 0u : a.num_pairs); r += L) {
-      const uint32_t p = r + l;
-      bool pass = false;
-      uint32_t ga = 0, gb = 0, ba = 0, bb = 0;
-      if (p < a.num_pairs) {
-        const DPair pr = a.pairs[p];
-        ga = pr.ga;
-        gb = pr.gb;
-        ba = __ldg(&a.geoms[ga].body);
-        bb = __ldg(&a.geoms[gb].body);
-        if (pr.plane) {
-          pass = true;
-        } else {
-          const float4 la = __ldg(reinterpret_cast<const float4*>(a.geoms[ga].pos_size0));
-          const float4 lb = __ldg(reinterpret_cast<const float4*>(a.geoms[gb].pos_size0));
+    if constexpr (L == 32) {
+      // One warp per environment (large models): four rounds of 32 candidates at a
+      // time, their model and pose loads in flight together (branch-free: plane pairs
+      // evaluate the distance too and discard it), then the four ballots append the
+      // passing candidates in emission order.
+      constexpr uint32_t kR = 4;
+      for (uint32_t r = 0; r < (grid ? 0u : a.num_pairs); r += kR * L) {
+        bool pass[kR];
+        Pk pk[kR];
+        DPair pr[kR];
+        uint32_t ba[kR], bb[kR];
+        float4 la[kR], lb[kR];
+        // loads first, unconditionally (indices clamped into the table), so that all of
+        // them are issued before any is used
+  #pragma unroll
+        for (uint32_t u = 0; u < kR; ++u) pr[u] = a.pairs[min(r + u * L + l, a.num_pairs - 1u)];
+  #pragma unroll
+        for (uint32_t u = 0; u < kR; ++u) {
+          ba[u] = __ldg(&a.geoms[pr[u].ga].body);
+          bb[u] = __ldg(&a.geoms[pr[u].gb].body);
+          la[u] = __ldg(reinterpret_cast<const float4*>(a.geoms[pr[u].ga].pos_size0));
+          lb[u] = __ldg(reinterpret_cast<const float4*>(a.geoms[pr[u].gb].pos_size0));
+        }
+  #pragma unroll
+        for (uint32_t u = 0; u < kR; ++u) {
           // corrected semantics rotate the geom offsets with the body (transformPoint)
-          const V3 pa = a.corrected ? geom_centre(pos[ba], quat[ba], la) : v3(pos[ba]) + v3(la);
-          const V3 pb = a.corrected ? geom_centre(pos[bb], quat[bb], lb) : v3(pos[bb]) + v3(lb);
+          const V3 pa = a.corrected ? geom_centre(pos[ba[u]], quat[ba[u]], la[u]) : v3(pos[ba[u]]) + v3(la[u]);
+          const V3 pb = a.corrected ? geom_centre(pos[bb[u]], quat[bb[u]], lb[u]) : v3(pos[bb[u]]) + v3(lb[u]);
           const V3 d = pb - pa;
-          pass = !(dot(d, d) >= pr.min_dist_sq);
+          pass[u] = r + u * L + l < a.num_pairs && ((pr[u].plane != 0u) | !(dot(d, d) >= pr[u].min_dist_sq));
+          pk[u] = pack4(ba[u], bb[u], pr[u].ga, pr[u].gb);
+        }
+  #pragma unroll
+        for (uint32_t u = 0; u < kR; ++u) {
+          const uint32_t bal = (__ballot_sync(gmask, pass[u]) >> gshift) & (L == 32 ? 0xFFFFFFFFu : ((1u << L) - 1u));
+          if (pass[u]) {
+            const uint32_t slot = count + __popc(bal & ((1u << l) - 1u));
+            if (slot < M) cpk[ord[slot]] = pk[u];
+          }
+          count += __popc(bal);
         }
       }
-      const uint32_t bal = (__ballot_sync(gmask, pass) >> gshift) & (L == 32 ? 0xFFFFFFFFu : ((1u << L) - 1u));
-      if (pass) {
-        const uint32_t slot = count + __popc(bal & ((1u << l) - 1u));
-        if (slot < M) cpk[ord[slot]] = pack4(ba, bb, ga, gb);
+    } else {  // (with 8 or 16 lanes the unrolled form measured slower: Humanoid 1.93 against 1.71 ms)
+      for (uint32_t r = 0; r < (grid ? 0u : a.num_pairs); r += L) {
+        const uint32_t p = r + l;
+        bool pass = false;
+        uint32_t ga = 0, gb = 0, ba = 0, bb = 0;
+        if (p < a.num_pairs) {
+          const DPair pr = a.pairs[p];
+          ga = pr.ga;
+          gb = pr.gb;
+          ba = __ldg(&a.geoms[ga].body);
+          bb = __ldg(&a.geoms[gb].body);
+          if (pr.plane) {
+            pass = true;
+          } else {
+            const float4 la = __ldg(reinterpret_cast<const float4*>(a.geoms[ga].pos_size0));
+            const float4 lb = __ldg(reinterpret_cast<const float4*>(a.geoms[gb].pos_size0));
+            // corrected semantics rotate the geom offsets with the body (transformPoint)
+            const V3 pa = a.corrected ? geom_centre(pos[ba], quat[ba], la) : v3(pos[ba]) + v3(la);
+            const V3 pb = a.corrected ? geom_centre(pos[bb], quat[bb], lb) : v3(pos[bb]) + v3(lb);
+            const V3 d = pb - pa;
+            pass = !(dot(d, d) >= pr.min_dist_sq);
+          }
+        }
+        const uint32_t bal = (__ballot_sync(gmask, pass) >> gshift) & (L == 32 ? 0xFFFFFFFFu : ((1u << L) - 1u));
+        if (pass) {
+          const uint32_t slot = count + __popc(bal & ((1u << l) - 1u));
+          if (slot < M) cpk[ord[slot]] = pack4(ba, bb, ga, gb);
+        }
+        count += __popc(bal);
       }
-      count += __popc(bal);
     }
     const uint32_t n = count < M ? count : M;
     const uint32_t n_old = count0 < M ? count0 : M;
