@@ -589,16 +589,17 @@ __device__ __forceinline__ void step_env(const StepArgs& a, uint32_t e, unsigned
         float4 la[kR], lb[kR];
         // loads first, unconditionally (indices clamped into the table), so that all of
         // them are issued before any is used
-  #pragma unroll
-        for (uint32_t u = 0; u < kR; ++u) pr[u] = a.pairs[min(r + u * L + l, a.num_pairs - 1u)];
-  #pragma unroll
+#pragma unroll
         for (uint32_t u = 0; u < kR; ++u) {
-          ba[u] = __ldg(&a.geoms[pr[u].ga].body);
-          bb[u] = __ldg(&a.geoms[pr[u].gb].body);
-          la[u] = __ldg(reinterpret_cast<const float4*>(a.geoms[pr[u].ga].pos_size0));
-          lb[u] = __ldg(reinterpret_cast<const float4*>(a.geoms[pr[u].gb].pos_size0));
+          const uint32_t p = min(r + u * L + l, a.num_pairs - 1u);
+          pr[u] = a.pairs[p];
+          const uint32_t pbd = __ldg(&a.pair_bodies[p]);
+          ba[u] = pbd & 0xFFFFu;
+          bb[u] = pbd >> 16;
+          la[u] = __ldg(&a.pair_la[p]);
+          lb[u] = __ldg(&a.pair_lb[p]);
         }
-  #pragma unroll
+#pragma unroll
         for (uint32_t u = 0; u < kR; ++u) {
           // corrected semantics rotate the geom offsets with the body (transformPoint)
           const V3 pa = a.corrected ? geom_centre(pos[ba[u]], quat[ba[u]], la[u]) : v3(pos[ba[u]]) + v3(la[u]);
@@ -607,7 +608,7 @@ __device__ __forceinline__ void step_env(const StepArgs& a, uint32_t e, unsigned
           pass[u] = r + u * L + l < a.num_pairs && ((pr[u].plane != 0u) | !(dot(d, d) >= pr[u].min_dist_sq));
           pk[u] = pack4(ba[u], bb[u], pr[u].ga, pr[u].gb);
         }
-  #pragma unroll
+#pragma unroll
         for (uint32_t u = 0; u < kR; ++u) {
           const uint32_t bal = (__ballot_sync(gmask, pass[u]) >> gshift) & (L == 32 ? 0xFFFFFFFFu : ((1u << L) - 1u));
           if (pass[u]) {

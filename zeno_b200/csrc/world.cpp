@@ -145,6 +145,19 @@ World* World::create(const Scene& sc, const WorldConfig& cfg, std::string* err) 
   upload(&w->d_joints_, m.joints);
   upload(&w->d_geoms_, m.geoms);
   upload(&w->d_pairs_, m.pairs);
+  {
+    std::vector<uint32_t> pb;
+    std::vector<float4> la, lb;
+    for (const DPair& p : m.pairs) {
+      const DGeom &ga = m.geoms[p.ga], &gb = m.geoms[p.gb];
+      pb.push_back(ga.body | (gb.body << 16));
+      la.push_back(make_float4(ga.pos_size0[0], ga.pos_size0[1], ga.pos_size0[2], ga.pos_size0[3]));
+      lb.push_back(make_float4(gb.pos_size0[0], gb.pos_size0[1], gb.pos_size0[2], gb.pos_size0[3]));
+    }
+    upload(&w->d_pair_bodies_, pb);
+    upload(&w->d_pair_la_, la);
+    upload(&w->d_pair_lb_, lb);
+  }
   upload(&w->d_act_, m.actuators);
   upload(&w->d_sensors_, m.sensors);
   upload(&w->d_cons_, m.constraints);
@@ -270,6 +283,7 @@ StepArgs World::args(uint32_t substeps, const float* actions, const uint8_t* mas
   std::memcpy(a.gravity, gravity_, 12);
   a.baumgarte = scene_.baumgarte, a.slop = scene_.slop, a.restitution = scene_.restitution;
   a.bodies = d_bodies_, a.jf_list = d_jf_, a.joints = d_joints_, a.geoms = d_geoms_, a.pairs = d_pairs_;
+  a.pair_bodies = d_pair_bodies_, a.pair_la = d_pair_la_, a.pair_lb = d_pair_lb_;
   a.actuators = d_act_, a.sensors = d_sensors_, a.constraints = d_cons_, a.color_ranges = d_colors_;
   a.subtree = d_subtree_, a.init_state = d_init_;
   a.pos = pos, a.quat = quat, a.vel = vel, a.angvel = angvel, a.acc = acc;

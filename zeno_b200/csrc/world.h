@@ -151,6 +151,9 @@ class World {
   DJoint* d_joints_ = nullptr;
   DGeom* d_geoms_ = nullptr;
   DPair* d_pairs_ = nullptr;
+  uint32_t* d_pair_bodies_ = nullptr;
+  float4* d_pair_la_ = nullptr;
+  float4* d_pair_lb_ = nullptr;
   DActuator* d_act_ = nullptr;
   DSensor* d_sensors_ = nullptr;
   DConstraint* d_cons_ = nullptr;

@@ -120,6 +120,11 @@ struct StepArgs {
   const DJoint* joints;
   const DGeom* geoms;
   const DPair* pairs;
+  // per candidate pair, so that the sweep's loads do not wait on the geom table:
+  // body a | body b << 16, and the two geoms' local offsets (xyz, size[0])
+  const uint32_t* pair_bodies;
+  const float4* pair_la;
+  const float4* pair_lb;
   const DActuator* actuators;
   const DSensor* sensors;
   const DConstraint* constraints;
