@@ -568,6 +568,22 @@ __device__ __forceinline__ void run_env(const StepArgs& a, const FModel& f, cons
     } else {
       if (lane == 0 && !reuse) {
         nlev = 0;
+        // the hit slots as a bit mask (eight slot words per shared-memory round trip), so
+        // that the two passes below visit only them (lists of up to 64 slots)
+        uint64_t hs = ~0ull;
+        if (n <= 64) {
+          hs = 0;
+          for (uint32_t i0 = 0; i0 < n; i0 += 8) {
+            uint32_t w8[8];
+#pragma unroll
+            for (uint32_t u = 0; u < 8; ++u) w8[u] = i0 + u < n ? meta[(i0 + u) * ne] : (fm::kNoHit << 16);
+#pragma unroll
+            for (uint32_t u = 0; u < 8; ++u) {
+              const uint32_t hh = sw_hit(w8[u]);
+              if (hh != fm::kNoHit && ((hit_now >> hh) & 1ull)) hs |= 1ull << (i0 + u);
+            }
+          }
+        }
         for (int pass = 0; pass < 2; ++pass) {  // pass 0 counts per level, pass 1 places
           for (uint32_t b = 0; b < B; ++b) blev[b * ne] = 0;
           if (pass == 1) {
@@ -580,7 +596,13 @@ __device__ __forceinline__ void run_env(const StepArgs& a, const FModel& f, cons
           } else {
             for (uint32_t v = 0; v <= n; ++v) lofs[v * ne] = 0;
           }
+          uint64_t todo = hs;
           for (uint32_t i = 0; i < n; ++i) {
+            if (n <= 64) {  // next hit slot from the mask
+              if (!todo) break;
+              i = uint32_t(__ffsll(todo)) - 1u;
+              todo &= todo - 1;
+            }
             const uint32_t hh = sw_hit(meta[i * ne]);
             if (hh == fm::kNoHit || !((hit_now >> hh) & 1ull)) continue;
             const uint32_t hi = m.hinfo(hh);
