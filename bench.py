@@ -17,11 +17,20 @@ memory by zeno_world_step and observations, rewards and dones are read back into
 arrays.  Multi-GPU runs are one process per GPU (torchrun); environments are sharded with
 no collective on the step path (weak scaling); timings are the max over ranks.
 
+Every workload starts from the model pose with joint-coordinate noise (BASELINE: Ant
+U(-0.1, 0.1), Humanoid U(-0.01, 0.01), Pendulum hinge U(-0.1, 0.1), Cartpole qpos and qvel
+U(-0.01, 0.01)), applied by zeno_b200.initial_state and zeno_world_reset_to_state.
+
 --impl reference times the reference algorithm on the host CPU cores: the reference
 implementation cannot run here (its step exists only as Metal shaders), so the CPU
-restatement in oracle/ is timed with all host threads on a bounded sample of envs.
+restatement in oracle/ is timed with all host threads, each step one World.step over a
+sample of the workload's environments sized so the timed steps take at least 6 s, with
+the same settings, initial state, task and `config` as the GPU arm.  That arm loads no
+product library.
 
-Other workloads (not the headline line; same JSON contract): --scene humanoid (the
+Other workloads (not the headline line; same JSON contract): --scene pendulum (BASELINE
+config 1: 1024 envs, dt 0.01 s, 4 substeps, no contacts), --scene cartpole (config 2:
+4096 envs, dt 0.01 s, 1 substep), --scene humanoid (the
 reference Humanoid, dt 0.015 s, 4 substeps, actions U(-0.4, 0.4), done = torso z < 1.0 with
 U(-0.01, 0.01) reset noise) or --scene collision_stress (the seeded 64-body drop scene,
 4096 envs per GPU, dt 0.005 s, 8 substeps, 256 contact slots, no actuators); --narrow 0/1/2
@@ -52,6 +61,7 @@ ACTION_RING = 64   # distinct pre-generated action batches, resident in HBM, cyc
 E2E_STEPS = 200    # steps of the end-to-end leg
 CPU_SAMPLE_ENVS = 2048  # cpu_baseline: envs stepped by the CPU oracle ...
 CPU_SAMPLE_S = 10.0     # ... for about this many seconds
+REF_TARGET_S = 6.0      # --impl reference: the timed steps take at least this long
 SUBSTEPS = 4
 ITERATIONS = 4
 MAX_CONTACTS = 64
@@ -60,22 +70,55 @@ UNIT = "env-steps/s"
 
 
 def scene_config(name: str) -> dict:
-    """Per-workload settings: envs per GPU, timestep (0: the MJCF's), substeps, solver
-    iterations, contact slots, action scale, the task (done rule and reset noise) or None."""
-    from zeno_b200 import scenes
+    """Per-workload settings: envs per GPU, timestep, substeps, solver iterations, contact
+    slots, action scale, initial joint-coordinate noise (qpos, qvel) or None, and the task
+    (done rule and reset noise) or None."""
+    from zeno_b200 import scenes  # pure Python: does not load libzeno.so
     inf = float("inf")
     return {
-        "ant": dict(xml=scenes.ant, envs=ENVS_PER_GPU, timestep=0.0, substeps=SUBSTEPS, iters=ITERATIONS,
-                    M=MAX_CONTACTS, act=1.0, task=dict(body=1, z_min=0.2, z_max=1.0, noise=0.1),
+        "ant": dict(xml=scenes.ant, envs=ENVS_PER_GPU, timestep=0.01, substeps=SUBSTEPS, iters=ITERATIONS,
+                    M=MAX_CONTACTS, act=1.0, init=(0.1, 0.0), task=dict(body=1, z_min=0.2, z_max=1.0, noise=0.1),
                     task_text="done: torso z not in [0.2, 1.0], device auto-reset, U(-0.1,0.1) noise"),
         "humanoid": dict(xml=scenes.humanoid, envs=ENVS_PER_GPU, timestep=0.015, substeps=4, iters=4, M=64,
-                         act=0.4, task=dict(body=1, z_min=1.0, z_max=inf, noise=0.01),
+                         act=0.4, init=(0.01, 0.0), task=dict(body=1, z_min=1.0, z_max=inf, noise=0.01),
                          task_text="done: torso z < 1.0, device auto-reset, U(-0.01,0.01) noise"),
+        "pendulum": dict(xml=scenes.pendulum, envs=1024, timestep=0.01, substeps=4, iters=4, M=64, act=1.0,
+                         init=(0.1, 0.0), task=None, task_text="none (no contacts; hinge angle U(-0.1,0.1) at start)"),
+        "cartpole": dict(xml=scenes.cartpole, envs=4096, timestep=0.01, substeps=1, iters=4, M=64, act=1.0,
+                         init=(0.01, 0.01), task=None, task_text="none (qpos, qvel U(-0.01,0.01) at start)"),
         "collision_stress": dict(xml=lambda: scenes.collision_stress(0), envs=4096, timestep=0.005, substeps=8,
-                                 iters=4, M=256, act=0.0, task=None, task_text="none (free fall, no actuators)"),
+                                 iters=4, M=256, act=0.0, init=None, task=None,
+                                 task_text="none (free fall, no actuators)"),
         "sphere_pile": dict(xml=lambda: scenes.sphere_pile(0), envs=1024, timestep=0.005, substeps=4, iters=4,
-                            M=1024, act=0.0, task=None, task_text="none (600 free spheres, no actuators)"),
+                            M=1024, act=0.0, init=None, task=None, task_text="none (600 free spheres, no actuators)"),
     }[name]
+
+
+def initial_state(tables, pos0, quat0, sc, E, rank):
+    """Per-environment initial body state: the model pose with the workload's joint-coordinate
+    noise (zeno_b200.initial_state), seeded by rank so shards differ; None without noise."""
+    if not sc["init"]:
+        return None
+    from zeno_b200.initial_state import joint_noise_state
+    qpos, qvel = sc["init"]
+    return joint_noise_state(tables["bodies"], tables["joints"], pos0, quat0, E,
+                             np.random.default_rng(1000 + rank), qpos, qvel)
+
+
+def bench_config(args, sc, E, world_size):
+    """The workload's `config` object, identical in both arms."""
+    narrow = args.narrow if args.narrow is not None else (2 if args.semantics == "corrected" else 0)
+    return {"workload": workload_name(args), "envs_per_gpu": E, "substeps": sc["substeps"],
+            "contact_iterations": sc["iters"], "max_contacts_per_env": sc["M"], "timestep": sc["timestep"],
+            "narrow_phase": narrow, "semantics": args.semantics,
+            "broad_phase": args.broad if args.broad is not None else 0,
+            "initial_noise": (f"joint coordinates U(-{sc['init'][0]},{sc['init'][0]})"
+                              + (f", rates U(-{sc['init'][1]},{sc['init'][1]})" if sc["init"][1] else "")
+                              ) if sc["init"] else "none",
+            "task": sc["task_text"],
+            "actions": f"U(-{sc['act']},{sc['act']}) per env per step" if sc["act"] else "none",
+            "l2": "flushed (256 MiB write) between timed steps",
+            "parallelism": f"env-sharded x{world_size}, no collective on the step path"}
 
 
 def algorithmic_bytes_per_env_step(B, J, A, obs, K, S):
@@ -156,17 +199,49 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
-def dram_bytes_per_launch(kernel: str, envs: int):
-    """DRAM bytes (read + write) per launch of `kernel` from the committed ncu summary
-    (profiles/step_traffic.md: a row `| kernel | envs | dram_bytes_per_launch |`), scaled to
-    `envs` environments (traffic is per environment), or None."""
-    import re
-    for f in sorted((ROOT / "profiles").glob("*_traffic.md")):
-        for line in f.read_text().splitlines():
-            m = re.match(r"\|\s*(\S+)\s*\|\s*(\d+)\s*\|\s*([\d.]+)\s*\|", line)
-            if m and m.group(1) == kernel:
-                return float(m.group(3)) * envs / int(m.group(2))
+TRAFFIC_FILE = ROOT / "profiles" / "step_traffic.json"
+
+
+def dram_bytes_per_launch(kernel: str, scene: str, envs: int):
+    """DRAM bytes (read + write) per launch of `kernel` on `scene`, from the ncu capture
+    recorded in profiles/step_traffic.json (written by `bench.py --record-traffic`), scaled
+    to `envs` environments (the traffic is per environment); None when not recorded."""
+    if not TRAFFIC_FILE.exists():
+        return None
+    for r in json.loads(TRAFFIC_FILE.read_text()).get("captures", []):
+        if r["kernel"] == kernel and r["scene"] == scene:
+            return float(r["dram_bytes_per_launch"]) * envs / int(r["envs"])
     return None
+
+
+def record_traffic(csv_path: str, scene: str, envs: int, command: str) -> None:
+    """Reads an ncu raw-page CSV (`ncu -i <rep> --page raw --csv`) and records, per step
+    kernel, dram__bytes_read.sum + dram__bytes_write.sum averaged over its captured
+    launches into profiles/step_traffic.json (replacing the entry of the same kernel and
+    scene)."""
+    import csv
+    rows = list(csv.reader(open(csv_path)))
+    head = rows[0]
+    idx = {k: head.index(k) for k in ("Kernel Name", "dram__bytes_read.sum", "dram__bytes_write.sum")}
+    units = rows[1] if len(rows) > 1 and not rows[1][idx["Kernel Name"]] else None
+    scale = {"byte": 1, "Kbyte": 1e3, "Mbyte": 1e6, "Gbyte": 1e9, "KB": 1e3, "MB": 1e6, "GB": 1e9}
+    per = {}
+    for r in rows[2 if units else 1:]:
+        name = r[idx["Kernel Name"]]
+        k = ("zb::" + name.split("zb::", 1)[1].split("(", 1)[0]) if "zb::" in name else name.split("(", 1)[0]
+        tot = 0.0
+        for m in ("dram__bytes_read.sum", "dram__bytes_write.sum"):
+            u = units[idx[m]] if units else "byte"
+            tot += float(r[idx[m]].replace(",", "")) * scale.get(u, 1)
+        per.setdefault(k, []).append(tot)
+    data = json.loads(TRAFFIC_FILE.read_text()) if TRAFFIC_FILE.exists() else {"captures": []}
+    for k, v in per.items():
+        if not k.startswith("zb::") or "step_kernel" not in k:
+            continue
+        data["captures"] = [c for c in data["captures"] if not (c["kernel"] == k and c["scene"] == scene)]
+        data["captures"].append({"kernel": k, "scene": scene, "envs": envs, "launches": len(v),
+                                 "dram_bytes_per_launch": sum(v) / len(v), "command": command})
+    TRAFFIC_FILE.write_text(json.dumps(data, indent=1) + "\n")
 
 
 def measured_peaks():
@@ -177,31 +252,51 @@ def measured_peaks():
     return 6650.0, "fallback"
 
 
-def cpu_baseline(xml, steps, sample_envs, threads, target_s=None, sc=None, narrow=None, semantics="reference"):
-    """The CPU oracle (reference algorithm restated) on a bounded sample of envs: `steps`
-    steps, or (target_s set) as many 10-step batches as fill about target_s seconds.
-    Returns (env-steps/s, seconds, steps run)."""
+def oracle_world(xml, sc, envs, narrow=None, semantics="reference", rank=0):
+    """The CPU oracle set up like the GPU arm's world: same settings, initial state and task."""
     from oracle.zeno_oracle import OracleWorld
-    sc = sc or scene_config("ant")
-    o = OracleWorld(xml, num_envs=sample_envs, timestep=sc["timestep"], substeps=sc["substeps"],
+    o = OracleWorld(xml, num_envs=envs, timestep=sc["timestep"], substeps=sc["substeps"],
                     contact_iterations=sc["iters"], max_contacts_per_env=sc["M"], semantics=semantics)
     if narrow is not None:
         o.set_narrow_phase(narrow)
+    st = o.state()
+    init = initial_state({"bodies": o.model_table("bodies"), "joints": o.model_table("joints")},
+                         st["positions"][0], st["quaternions"][0], sc, envs, rank)
+    if init is not None:
+        o.reset_to_state(init["positions"], init["quaternions"], init["velocities"], init["angular_velocities"])
     if sc["task"]:
         o.set_task(auto_reset=True, seed=1, **sc["task"])
+    return o
+
+
+def time_oracle(o, sc, threads, warmup=1, steps=0, target_s=0.0):
+    """Steps the oracle world `o` (actions U(-act, act), a ring of distinct batches): `warmup`
+    untimed steps, then `steps` timed steps, repeated until at least `target_s` seconds have
+    passed.  Returns (env-steps/s, seconds, steps timed)."""
     rng = np.random.default_rng(0)
-    batch = 10 if target_s else steps
-    acts = (sc["act"] * rng.uniform(-1, 1, size=(batch, sample_envs, o.num_actuators))).astype(np.float32)
-    o.run(acts[:1], threads=threads)  # warm-up
+    A = max(o.num_actuators, 1)
+    ring = (sc["act"] * rng.uniform(-1, 1, size=(min(max(steps, 10), ACTION_RING), o.num_envs, A))).astype(np.float32)
+    for k in range(warmup):
+        o.run(ring[k % len(ring)][None], threads=threads)
+    batch = max(steps, 10)
     done = 0
     t0 = time.perf_counter()
     while True:
-        o.run(acts, threads=threads)
+        for k in range(0, batch, len(ring)):
+            n = min(len(ring), batch - k)
+            o.run(ring[:n], threads=threads)
         done += batch
         dt = time.perf_counter() - t0
-        if not target_s or dt >= target_s:
+        if dt >= target_s:
             break
-    return done * sample_envs / dt, dt, done
+    return done * o.num_envs / dt, dt, done
+
+
+def cpu_baseline(xml, sc, sample_envs, threads, target_s, narrow=None, semantics="reference"):
+    """The cpu_baseline leg: the CPU oracle on a bounded sample of the workload's envs for
+    about target_s seconds.  Returns (env-steps/s, seconds, steps run)."""
+    o = oracle_world(xml, sc, sample_envs, narrow, semantics)
+    return time_oracle(o, sc, threads, warmup=1, steps=10, target_s=target_s)
 
 
 def metric_name(args, E):
@@ -221,25 +316,36 @@ def workload_name(args):
     return w
 
 
-def run_reference(args, rank):
+def run_reference(args, rank, world_size):
+    """The reference arm: the reference's step algorithm on the host cores.  The reference
+    step exists only as Metal shaders and its Zig host cannot be built here, so the CPU
+    restatement in oracle/ stands in for it (the same arithmetic and step order the GPU is
+    checked against bit for bit), on all host threads.  One step = one World.step over a
+    sample of the workload's environments, sized so the K timed steps take at least
+    REF_TARGET_S seconds (all of them repeated when even the full workload is faster).
+    This arm loads no product library: scenes and initial_state are pure Python."""
     if rank != 0:
         return 0
     threads = os.cpu_count() or 1
     sc = scene_config(args.scene)
-    sample = min(2048, sc["envs"])
+    E = args.envs or sc["envs"]
     xml = sc["xml"]()
-    val, dt, _ = cpu_baseline(xml, args.warmup + args.steps, sample, threads, sc=sc, narrow=args.narrow,
-                              semantics=args.semantics)
+    narrow = args.narrow
+    probe = oracle_world(xml, sc, min(256, E), narrow, args.semantics)
+    rate, _, _ = time_oracle(probe, sc, threads, warmup=2, steps=10, target_s=0.5)
+    del probe
+    sample = int(min(E, max(64, np.ceil(REF_TARGET_S * rate / max(args.steps, 1)))))
+    o = oracle_world(xml, sc, sample, narrow, args.semantics)
+    val, dt, done = time_oracle(o, sc, threads, warmup=args.warmup, steps=args.steps, target_s=REF_TARGET_S)
     line = {
-        "impl": "reference", "metric": metric_name(args, sc["envs"]), "value": val, "unit": UNIT,
-        "n_gpus": args.gpus, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": 1000.0 * sample / val, "higher_is_better": True, "scaling": "weak",
+        "impl": "reference", "metric": metric_name(args, E), "value": val, "unit": UNIT,
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1000.0 * dt / done, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": workload_name(args), "envs_per_gpu": sc["envs"], "substeps": sc["substeps"],
-                   "contact_iterations": sc["iters"], "max_contacts_per_env": sc["M"],
-                   "sample_envs_per_step": sample},
+        "config": bench_config(args, sc, E, world_size),
+        "sample_envs_per_step": sample, "timed_steps": done,
         "cpu_baseline": {"value": val, "unit": UNIT, "cores": threads, "kind": "port",
-                         "sample": f"{sample} {args.scene} envs x {args.warmup + args.steps} steps on {threads} threads "
+                         "sample": f"{sample} of {E} {args.scene} envs per step x {done} steps on {threads} threads "
                                    f"({dt:.1f} s); the reference step exists only as Metal shaders, so the CPU "
                                    "restatement in oracle/ stands in for it"},
         "e2e": {"value": val, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -320,6 +426,14 @@ def run_ours(args, rank, world_size, local_rank):
         w.set_narrow_phase(args.narrow)
     if args.broad is not None:
         w.set_broad_phase(args.broad)
+    config = bench_config(args, sc, E, world_size)
+    if (w.get_narrow_phase(), w.get_broad_phase()) != (config["narrow_phase"], config["broad_phase"]):
+        raise RuntimeError("world settings differ from the reported config")
+    init = initial_state({"bodies": w.model_table("bodies"), "joints": w.model_table("joints")},
+                         w.get_body_positions(zero_copy=False)[0], w.get_body_quaternions(zero_copy=False)[0],
+                         sc, E, rank)
+    if init is not None:
+        w.reset_to_state(init["positions"], init["quaternions"], init["velocities"], init["angular_velocities"])
     if sc["task"]:
         w.set_task(auto_reset=True, seed=1, env_offset=shard_env_offset(rank, E), **sc["task"])
     # a dedicated stream: the world launches on it and the timing events record on it
@@ -389,9 +503,9 @@ def run_ours(args, rank, world_size, local_rank):
         peak, peak_kind = measured_peaks()
         lanes, epb = w.get_launch()
         kernel = f"zb::fast_step_kernel<{lanes}>" if lanes in (1, 2, 4) else f"zb::step_kernel<{lanes}>"
-        traffic = dram_bytes_per_launch(kernel, E)
+        traffic = dram_bytes_per_launch(kernel, args.scene, E)
         cpu_envs = min(CPU_SAMPLE_ENVS, E)
-        cpu_val, cpu_dt, cpu_steps = (cpu_baseline(xml, 0, cpu_envs, os.cpu_count() or 1, CPU_SAMPLE_S, sc=sc,
+        cpu_val, cpu_dt, cpu_steps = (cpu_baseline(xml, sc, cpu_envs, os.cpu_count() or 1, CPU_SAMPLE_S,
                                                    narrow=args.narrow, semantics=args.semantics)
                                       if not args.no_cpu else (None, 0, 0))
         clocks = clk.summary()
@@ -399,15 +513,8 @@ def run_ours(args, rank, world_size, local_rank):
             "metric": metric_name(args, E), "value": value, "unit": UNIT, "n_gpus": world_size, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": t_max * 1000.0 / args.steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": workload_name(args), "envs_per_gpu": E, "substeps": sc["substeps"],
-                       "contact_iterations": sc["iters"], "max_contacts_per_env": sc["M"], "timestep": st["timestep"],
-                       "narrow_phase": w.get_narrow_phase(), "semantics": args.semantics,
-                       "broad_phase": w.get_broad_phase(),
-                       "task": sc["task_text"],
-                       "actions": f"U(-{sc['act']},{sc['act']}), resident in HBM" if A else "none",
-                       "l2": "flushed (256 MiB write) between timed steps",
-                       "launch": {"lanes_per_env": lanes, "envs_per_block": epb},
-                       "parallelism": f"env-sharded x{world_size}, no collective on the step path"},
+            "config": config,
+            "launch": {"lanes_per_env": lanes, "envs_per_block": epb},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic, "peak_kind": peak_kind,
                          "bytes_per_env_step": bpe, "kernel": kernel,
@@ -442,20 +549,27 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline sample")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end (host buffer) leg")
     ap.add_argument("--envs", type=int, default=0, help="environments per GPU (0: the workload's)")
-    ap.add_argument("--scene", choices=["ant", "humanoid", "collision_stress", "sphere_pile"], default="ant")
+    ap.add_argument("--scene", choices=["ant", "humanoid", "pendulum", "cartpole", "collision_stress", "sphere_pile"],
+                    default="ant")
     ap.add_argument("--broad", type=int, choices=[0, 1, 2], default=None, help="broad phase (default: the world's)")
     ap.add_argument("--narrow", type=int, choices=[0, 1, 2], default=None, help="narrow phase (default: the world's)")
     ap.add_argument("--semantics", choices=["reference", "corrected"], default="reference")
     ap.add_argument("--gather", action="store_true",
                     help="with N > 1: also time the optional NCCL all-gather of the step outputs (not in value)")
+    ap.add_argument("--record-traffic", nargs=4, metavar=("CSV", "SCENE", "ENVS", "COMMAND"),
+                    help="record DRAM traffic per launch from an ncu raw CSV into profiles/step_traffic.json")
     args = ap.parse_args()
+    if args.record_traffic:
+        csv_path, scene, envs, command = args.record_traffic
+        record_traffic(csv_path, scene, int(envs), command)
+        return 0
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
     rank = int(os.environ.get("RANK", "0"))
     world_size = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
-        return run_reference(args, rank)
+        return run_reference(args, rank, world_size)
     return run_ours(args, rank, world_size, local_rank)
 
 

@@ -167,6 +167,15 @@ void* zo_buffer(void* h, const char* name, size_t* nbytes) {
 extern "C" {
 float zo_atan2(float y, float x) { return zo::atan2_r(y, x); }
 
+// Arithmetic of the step: 0 canonical (default), 1 literal, 2 literal with FMA contraction
+// (oracle_literal.cpp; the reference semantics only, so a corrected-semantics world
+// refuses 1 and 2).
+int zo_set_arithmetic(void* h, uint32_t mode) {
+  if (!h || mode > 2 || (static_cast<World*>(h)->scene.corrected && mode != 0)) return -6;
+  static_cast<World*>(h)->arithmetic = mode;
+  return 0;
+}
+
 int zo_set_narrow_mode(void* h, uint32_t mode) {
   if (!h || mode > 2 || (static_cast<World*>(h)->scene.corrected && mode == 0)) return -6;
   static_cast<World*>(h)->narrow_mode = mode;

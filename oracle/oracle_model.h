@@ -183,6 +183,9 @@ struct World {
   uint64_t task_env_offset = 0;     // global index of env 0 (multi-GPU sharding)
   uint32_t narrow_mode = 0;         // 0: reference GPU narrow phase; 1: CPU detectCollision;
                                     // 2: as 1, plus GJK + EPA for box-capsule pairs
+  uint32_t arithmetic = 0;          // 0: canonical (the product's arithmetic, bit for bit);
+                                    // 1: literal (the reference kernels' own IEEE arithmetic);
+                                    // 2: literal compiled with FMA contraction
   std::vector<uint32_t> episode;    // per-env reset counter (task extension RNG stream)
   std::vector<uint32_t> subtree;    // per-body subtree size (depth-first body order)
 };
@@ -193,6 +196,9 @@ int world_step_subset(World* w, const float* actions, const uint8_t* mask, uint3
 void world_reset(World* w, const uint8_t* mask);
 void world_apply_task(World* w, const uint8_t* mask);
 void world_reset_env_noise(World* w, uint32_t e);
+// One substep of one environment in the literal arithmetic (oracle_literal.cpp).
+void substep_env_literal(World* w, uint32_t e);
+void substep_env_literal_contracted(World* w, uint32_t e);
 // detectCollision of the reference CPU collision code for one geom pair placed by its
 // bodies' poses (oracle_narrow.cpp).
 bool narrow_cpu(const GeomRec& ga, const float* body_pos_a, const float* body_quat_a, const GeomRec& gb,

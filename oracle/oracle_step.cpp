@@ -1139,6 +1139,13 @@ bool world_init(World* w, const Scene& scene, const Config& cfg) {
   return true;
 }
 
+// The substep in the world's arithmetic mode.
+void substep(World* w, uint32_t e) {
+  if (w->arithmetic == 1) substep_env_literal(w, e);
+  else if (w->arithmetic == 2) substep_env_literal_contracted(w, e);
+  else substep_env(w, e);
+}
+
 // World.step (world.zig:694-792) for all environments.  Environments never share
 // mutable state, so `threads` > 1 splits them across host threads (same results).
 void world_step(World* w, const float* actions, uint32_t substeps, uint32_t threads) {
@@ -1149,14 +1156,14 @@ void world_step(World* w, const float* actions, uint32_t substeps, uint32_t thre
   w->prev_vel = w->vel;
   if (threads <= 1) {
     for (uint32_t s = 0; s < ns; s++)
-      for (uint32_t e = 0; e < E; e++) substep_env(w, e);
+      for (uint32_t e = 0; e < E; e++) substep(w, e);
   } else {
     std::vector<std::thread> pool;
     for (uint32_t t = 0; t < threads; t++)
       pool.emplace_back([w, t, threads, E, ns]() {
         const uint32_t e0 = uint32_t(uint64_t(E) * t / threads), e1 = uint32_t(uint64_t(E) * (t + 1) / threads);
         for (uint32_t e = e0; e < e1; e++)
-          for (uint32_t s = 0; s < ns; s++) substep_env(w, e);
+          for (uint32_t s = 0; s < ns; s++) substep(w, e);
       });
     for (auto& th : pool) th.join();
   }
@@ -1187,7 +1194,7 @@ int world_step_subset(World* w, const float* actions, const uint8_t* mask, uint3
   w->params.dt = w->timestep / float(std::max(ns, 1u));
   w->prev_vel = w->vel;
   for (uint32_t s = 0; s < ns; s++)
-    for (uint32_t e = 0; e < E; e++) substep_env(w, e);
+    for (uint32_t e = 0; e < E; e++) substep(w, e);
   float inv_step = w->timestep > 0 ? 1.0f / w->timestep : 0.0f;
   for (size_t i = 0; i < size_t(E) * B; i++) {
     for (int k = 0; k < 3; k++) w->acc[i * 4 + k] = (w->vel[i * 4 + k] - w->prev_vel[i * 4 + k]) * inv_step;

@@ -63,6 +63,9 @@ extern "C" {
 #endif
 float zo_atan2(float y, float x);
 int zo_set_narrow_mode(void* h, uint32_t mode);
+/* 0: canonical arithmetic (default); 1: literal IEEE arithmetic of the reference kernels;
+   2: the literal source compiled with FMA contraction */
+int zo_set_arithmetic(void* h, uint32_t mode);
 int zo_eval_math(uint32_t fn, const float* x, const float* y, float* out, uint64_t n);
 int zo_gjk_epa(const float* geom_a, const float* body_a, const float* geom_b, const float* body_b, float* out);
 int zo_narrow_cpu(const float* geom_a, const float* body_a, const float* geom_b, const float* body_b, float* out,

@@ -85,6 +85,7 @@ def lib() -> ctypes.CDLL:
         L.zo_buffer.restype = vp
         L.zo_buffer.argtypes = [vp, ctypes.c_char_p, ctypes.POINTER(ctypes.c_size_t)]
         L.zo_set_narrow_mode.argtypes = [vp, ctypes.c_uint32]
+        L.zo_set_arithmetic.argtypes = [vp, ctypes.c_uint32]
         L.zo_narrow_cpu.argtypes = [f32p, f32p, f32p, f32p, f32p, ctypes.c_uint32]
         L.zo_gjk_epa.argtypes = [f32p, f32p, f32p, f32p, f32p]
         L.zo_eval_math.argtypes = [ctypes.c_uint32, f32p, f32p, f32p, ctypes.c_uint64]
@@ -109,7 +110,8 @@ class OracleWorld:
     """A world stepped by the CPU oracle; buffers are numpy views into oracle memory."""
 
     def __init__(self, xml: str, num_envs=1, timestep=0.0, contact_iterations=4,
-                 max_contacts_per_env=64, seed=42, substeps=1, semantics="reference"):
+                 max_contacts_per_env=64, seed=42, substeps=1, semantics="reference",
+                 arithmetic="canonical"):
         cfg = ZoConfig(num_envs, timestep, contact_iterations, max_contacts_per_env, seed, substeps,
                        False, 0, 0, 0)
         sem = {"reference": 0, "corrected": 1}[semantics]
@@ -121,6 +123,8 @@ class OracleWorld:
         (self.num_envs, self.num_bodies, self.num_joints, self.num_actuators, self.num_geoms,
          self.num_sensors, self.max_contacts, self.num_constraints, self.obs_dim,
          self.num_colors) = list(d)
+        if arithmetic != "canonical" and self.set_arithmetic(arithmetic) != 0:
+            raise ValueError(f"arithmetic {arithmetic!r} not available for this world")
 
     def __del__(self):
         if getattr(self, "_h", None):
@@ -194,6 +198,14 @@ class OracleWorld:
         """0: the reference's GPU narrow phase (default); 1: its CPU detectCollision; 2: as 1,
         plus GJK + EPA for box-capsule pairs."""
         return lib().zo_set_narrow_mode(self._h, int(mode))
+
+    def set_arithmetic(self, mode: str) -> int:
+        """'canonical': the arithmetic the product kernel evaluates bit for bit (default);
+        'literal': the reference Metal kernels' own expressions in plain IEEE single precision
+        (oracle_literal.cpp), for tolerance checks of the canonical arithmetic;
+        'contracted': the literal source compiled with FMA contraction (the spread of the
+        reference's own source under two legitimate compilations)."""
+        return lib().zo_set_arithmetic(self._h, {"canonical": 0, "literal": 1, "contracted": 2}[mode])
 
     def model_table(self, name: str) -> bytes:
         return self.raw(name, np.uint8).tobytes()

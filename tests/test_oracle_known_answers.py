@@ -7,7 +7,7 @@ these are the values its unit tests assert, re-checked here against the oracle:
                                       (405-475), actuator torque and clamps (517-629)
   tests/test_collision.zig            sphere-sphere / sphere-plane penetration (55-69, 173-187)
   tests/test_xpbd.zig:370-376         record sizes
-plus the Ant model derived by hand from the reference loader (SURVEY: B=10, J=9, K=24,
+plus the Ant model derived by hand from the reference loader (B=10, J=9, K=24,
 obs=29, 12 colours of sizes 4,4,4,2,2,2,1,1,1,1,1,1)."""
 import ctypes
 import struct

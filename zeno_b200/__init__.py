@@ -5,27 +5,26 @@ The physics step runs as one fused CUDA kernel per World.step behind Zeno's C AB
 Python side of that boundary: ``ZenoWorld`` and ``ZenoEnv``/``make`` keep the reference
 package's interface.
 
-There is no fallback without the library: when ``libzeno.so`` has not been built, the
-package still imports (so that ``python -m zeno_b200.build`` and the pure-Python
-``scenes`` module work), but every name that needs the library raises the ImportError
-that says so.
+The library is loaded on first use of a name that needs it (``ZenoWorld``,
+``is_cuda_available``, ...), not at import, so that the pure-Python modules (``scenes``,
+``initial_state``, ``build``) import without touching it.  There is no fallback: when
+``libzeno.so`` is missing or cannot be loaded, that first use raises the ImportError that
+says so.
 """
-_LIB_NAMES = ("CONTACT_DTYPE", "CudaArray", "ZenoWorld", "ZeroCopyArray", "is_cuda_available", "is_metal_available",
-              "version", "ZenoEnv", "make")
+import importlib
 
-try:
-    from ._ffi import (CONTACT_DTYPE, CudaArray, ZenoWorld, ZeroCopyArray, is_cuda_available, is_metal_available,
-                       version)
-    from .env import ZenoEnv, make
-except ImportError as _e:
-    if "libzeno.so not found" not in str(_e):
-        raise
-    _missing = _e
+_FFI_NAMES = ("CONTACT_DTYPE", "CudaArray", "ZenoWorld", "ZeroCopyArray", "is_cuda_available", "is_metal_available",
+              "version")
+_ENV_NAMES = ("ZenoEnv", "make")
 
-    def __getattr__(name):
-        if name in _LIB_NAMES:
-            raise ImportError(str(_missing)) from _missing
-        raise AttributeError(f"module 'zeno_b200' has no attribute {name!r}")
+
+def __getattr__(name):
+    if name in _FFI_NAMES:
+        return getattr(importlib.import_module("._ffi", __name__), name)
+    if name in _ENV_NAMES:
+        return getattr(importlib.import_module(".env", __name__), name)
+    raise AttributeError(f"module 'zeno_b200' has no attribute {name!r}")
+
 
 __version__ = "0.1.0"
-__all__ = list(_LIB_NAMES)
+__all__ = list(_FFI_NAMES + _ENV_NAMES)

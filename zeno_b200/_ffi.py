@@ -413,6 +413,9 @@ class ZenoWorld:
         "body_quaternions": ("zeno_world_get_body_quaternions", lambda w: (w._num_envs, w._num_bodies, 4), "<f4"),
         "body_velocities": ("zeno_world_get_body_velocities", lambda w: (w._num_envs, w._num_bodies, 4), "<f4"),
         "contact_counts": ("zeno_world_get_contact_counts", lambda w: (w._num_envs,), "<u4"),
+        # 64-byte contact records viewed as 16 floats (position_pen, normal_friction, the
+        # uint32 indices as raw bits, impulses)
+        "contacts": ("zeno_world_get_contacts", lambda w: (w._num_envs, w._max_contacts_per_env, 16), "<f4"),
     }
 
     def device_array(self, name: str) -> CudaArray:

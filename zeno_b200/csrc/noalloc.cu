@@ -83,7 +83,13 @@ extern "C" int zeno_world_reset_to_state_noalloc(ZenoWorldHandle world, const fl
   int prev_dev = -1;
   cudaGetDevice(&prev_dev);
   const int dev = w->device();
-  if (prev_dev != dev && cudaSetDevice(dev) != cudaSuccess) return ZENO_METAL_ERROR;
+  if (prev_dev != dev) {
+    const cudaError_t e = cudaSetDevice(dev);
+    if (e != cudaSuccess) {
+      zb::set_last_error(std::string("zeno_world_reset_to_state_noalloc: cudaSetDevice: ") + cudaGetErrorString(e));
+      return ZENO_METAL_ERROR;
+    }
+  }
   std::string err;
   float* staging = staging_for(dev, &err);
   int rc = ZENO_METAL_ERROR;
