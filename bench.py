@@ -164,6 +164,10 @@ class ClockSampler:
                  "-lms", "50"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self._t = threading.Thread(target=self._read, daemon=True)
             self._t.start()
+            t0 = time.perf_counter()  # the timed region starts once the sampler is reporting
+            while not self.lines and time.perf_counter() - t0 < 5.0 and self.proc.poll() is None:
+                time.sleep(0.01)
+            self.lines.clear()
         except FileNotFoundError:
             self.proc = None
         return self
@@ -497,7 +501,8 @@ def run_ours(args, rank, world_size, local_rank):
             K = len(w.model_table("constraints")) // 96
         except KeyError:  # no constraints (free bodies only)
             K = 0
-        bpe = algorithmic_bytes_per_env_step(B, J, A, obs_dim, K, sc["M"])
+        live_slots = float(np.minimum(counts, sc["M"]).mean())  # S: the slots the step reads and writes
+        bpe = algorithmic_bytes_per_env_step(B, J, A, obs_dim, K, live_slots)
         mean_ms = statistics.mean(step_ms)
         achieved = bpe * E / (mean_ms / 1000.0) / 1e9
         peak, peak_kind = measured_peaks()
@@ -540,6 +545,47 @@ def run_ours(args, rank, world_size, local_rank):
     return 0
 
 
+def run_stage_profile(args):
+    """Per-stage device cycles of the step (a profiling world: the instrumented kernel
+    instantiation, zeno_world_get_stage_cycles), averaged over the timed steps; one JSON
+    line.  Not a throughput measurement: the instrumented kernel is slower."""
+    import torch
+
+    import zeno_b200
+    torch.cuda.set_device(0)
+    sc = scene_config(args.scene)
+    E = args.envs or sc["envs"]
+    w = zeno_b200.ZenoWorld(mjcf_string=sc["xml"](), num_envs=E, timestep=sc["timestep"], substeps=sc["substeps"],
+                            contact_iterations=sc["iters"], max_contacts_per_env=sc["M"], semantics=args.semantics,
+                            enable_profiling=True)
+    if args.narrow is not None:
+        w.set_narrow_phase(args.narrow)
+    init = initial_state({"bodies": w.model_table("bodies"), "joints": w.model_table("joints")},
+                         w.get_body_positions(zero_copy=False)[0], w.get_body_quaternions(zero_copy=False)[0],
+                         sc, E, 0)
+    if init is not None:
+        w.reset_to_state(init["positions"], init["quaternions"], init["velocities"], init["angular_velocities"])
+    if sc["task"]:
+        w.set_task(auto_reset=True, seed=1, **sc["task"])
+    rng = np.random.default_rng(0)
+    acc = {}
+    for s in range(args.warmup + args.steps):
+        a = (sc["act"] * rng.uniform(-1, 1, size=(E, max(w.action_dim, 1)))).astype(np.float32)
+        w.step(a)
+        if s < args.warmup:
+            continue
+        prof = w.get_stage_profile()
+        if not prof:
+            raise RuntimeError("no stage profile: the world does not run the compressed-state kernel")
+        for k, v in prof.items():
+            acc[k] = acc.get(k, 0.0) + v / args.steps
+    lanes, epb = w.get_launch()
+    print(json.dumps({"stage_profile": args.scene, "envs": E, "steps": args.steps, "launch": [lanes, epb],
+                      "cycles_per_block_step": {k: round(v) for k, v in acc.items() if k != "ns_per_cycle"},
+                      "ns_per_cycle": acc.get("ns_per_cycle"), "profiling_data": w.get_profiling_data()}), flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -556,6 +602,8 @@ def main():
     ap.add_argument("--semantics", choices=["reference", "corrected"], default="reference")
     ap.add_argument("--gather", action="store_true",
                     help="with N > 1: also time the optional NCCL all-gather of the step outputs (not in value)")
+    ap.add_argument("--stage-profile", action="store_true",
+                    help="print per-stage device cycles of the step (instrumented kernel; no throughput line)")
     ap.add_argument("--record-traffic", nargs=4, metavar=("CSV", "SCENE", "ENVS", "COMMAND"),
                     help="record DRAM traffic per launch from an ncu raw CSV into profiles/step_traffic.json")
     args = ap.parse_args()
@@ -570,6 +618,8 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         return run_reference(args, rank, world_size)
+    if args.stage_profile:
+        return run_stage_profile(args)
     return run_ours(args, rank, world_size, local_rank)
 
 

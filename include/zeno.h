@@ -245,6 +245,21 @@ int zeno_world_get_launch(ZenoWorldHandle world, int* lanes, int* envs_per_block
  * Returns NULL for an unknown name. */
 const void* zeno_world_model_table(ZenoWorldHandle world, const char* name, uint64_t* nbytes);
 
+/* Stage profile (extends zeno_world_get_profiling, main.zig:666-683).  A world created
+ * with ZenoConfig.enable_profiling runs an instrumented instantiation of the
+ * compressed-state kernel whose blocks time each stage of the step with the SM clock.
+ * After each synchronous zeno_world_step, zeno_world_get_profiling's integrate / broad /
+ * narrow / constraint fields hold those stages' device times (summed over the substeps,
+ * averaged over the blocks, which run side by side), and this call writes up to n values:
+ * the average cycles per block of the 14 stages -- 0 prologue (block loads), 1 actions and
+ * kinematic bodies, 2 wrenches and integration, 3 broad phase, 4 sort, 5 narrow phase and
+ * warm start, 6 contact schedule, 7 joint constraints, 8 contact solve, 9 velocity
+ * update, 10 joint states and sensors, 11 contact write-back, 12 caches and task,
+ * 13 block epilogue -- then the average block span in cycles, then nanoseconds per cycle.
+ * Returns the number of values written (16 at most), 0 when no profile exists (profiling
+ * off, no synchronous step yet, or the world runs the general kernel), -1 for NULL. */
+int zeno_world_get_stage_cycles(ZenoWorldHandle world, double* out, uint32_t n);
+
 /* Message of the last failed zeno_world_create* on this thread ("" if none). */
 const char* zeno_last_error(void);
 

@@ -99,6 +99,20 @@ def valid_contacts(contacts: np.ndarray, counts: np.ndarray, max_contacts: int) 
     return ((contacts["position_pen"][..., 3] >= 0) & live).sum(1)
 
 
+def slog(x: np.ndarray) -> np.ndarray:
+    """sign(x) log10(1 + |x|): the reference Humanoid's energy drift spans 30 orders of
+    magnitude across environments (some explode), so means are compared on this scale."""
+    return np.sign(x) * np.log10(1.0 + np.abs(x))
+
+
+def ks_pvalue(x: np.ndarray, y: np.ndarray) -> float:
+    """Two-sample Kolmogorov-Smirnov p-value (distributions equal)."""
+    if np.array_equal(np.sort(x), np.sort(y)):
+        return 1.0
+    from scipy.stats import ks_2samp
+    return float(ks_2samp(x, y).pvalue)
+
+
 def two_sample_z(x: np.ndarray, y: np.ndarray) -> float:
     """(mean x - mean y) over its standard error."""
     se = np.sqrt(x.var(ddof=1) / x.size + y.var(ddof=1) / y.size)

@@ -104,6 +104,7 @@ ffi.cdef("""
     int zeno_world_get_launch(ZenoWorldHandle world, int* lanes, int* envs_per_block);
     const void* zeno_world_model_table(ZenoWorldHandle world, const char* name, uint64_t* nbytes);
     const char* zeno_last_error(void);
+    int zeno_world_get_stage_cycles(ZenoWorldHandle world, double* out, uint32_t n);
     void* zeno_model_create_from_string(const char* mjcf_string);
     int zeno_eval_math(uint32_t fn, const float* x, const float* y, float* out, uint64_t n);
     void* zeno_model_create_from_string_ex(const char* mjcf_string, uint32_t semantics);
@@ -504,6 +505,22 @@ class ZenoWorld:
                 "collision_narrow_ms": d.collision_narrow_ns / 1e6,
                 "constraint_solve_ms": d.constraint_solve_ns / 1e6, "total_step_ms": d.total_step_ns / 1e6,
                 "num_contacts": d.num_contacts, "num_active_constraints": d.num_active_constraints}
+
+    STAGES = ("prologue", "actions", "integrate", "broad_phase", "sort", "narrow_phase", "schedule", "joints",
+              "contacts", "velocities", "joint_states_sensors", "write_back", "task", "epilogue")
+
+    def get_stage_profile(self) -> Dict[str, float]:
+        """Per-stage device cycles of the last synchronous step, averaged over the kernel's
+        blocks, plus the block span ("span_cycles") and "ns_per_cycle" (a world created with
+        enable_profiling=True on the compressed-state kernel; {} otherwise)."""
+        n = len(self.STAGES) + 2
+        out = ffi.new("double[]", n)
+        got = _lib.zeno_world_get_stage_cycles(self._handle, out, n)
+        if got < n:
+            return {}
+        d = {name: out[i] for i, name in enumerate(self.STAGES)}
+        d["span_cycles"], d["ns_per_cycle"] = out[n - 2], out[n - 1]
+        return d
 
     def reset_profiling(self) -> None:
         _lib.zeno_world_reset_profiling(self._handle)

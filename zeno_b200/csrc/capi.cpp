@@ -197,6 +197,12 @@ int zeno_world_get_profiling(ZenoWorldHandle world, ZenoProfilingData* data) {
   return ZENO_SUCCESS;
 }
 
+int zeno_world_get_stage_cycles(ZenoWorldHandle world, double* out, uint32_t n) {
+  if (!world) return ZENO_INVALID_HANDLE;
+  if (!out && n) return ZENO_INVALID_ARGUMENT;
+  return int(W(world)->stage_cycles(out, n));
+}
+
 void zeno_world_reset_profiling(ZenoWorldHandle world) {
   if (world) W(world)->reset_profiling();
 }

@@ -191,12 +191,33 @@ enum : uint32_t {
 };
 constexpr uint32_t kWbParts = 12;  // 16-byte record parts staged per thread
 
+// Stage profile (profiling worlds only): the block's first thread accumulates clock64
+// deltas per stage in shared memory; with C = false every mark compiles to nothing.
+template <bool C>
+struct StageClock {
+  __device__ __forceinline__ void mark(uint32_t) {}
+};
+template <>
+struct StageClock<true> {
+  unsigned long long* acc;  // shared, kStageCount entries
+  long long last;
+  bool on;                  // the block's first thread
+  __device__ __forceinline__ void mark(uint32_t k) {
+    if (on) {
+      const long long t = clock64();
+      acc[k] += static_cast<unsigned long long>(t - last);
+      last = t;
+    }
+  }
+};
+
 // Everything a group does for its environment between the cooperative load and store.
 // The block has already handed over the environments this kernel cannot represent.
-template <int L>
+template <int L, bool C>
 __device__ __forceinline__ void run_env(const StepArgs& a, const FModel& f, const FPlan& pl, const unsigned char* hot,
                                         unsigned char* blk, uint32_t ne, uint32_t g, const Group<L>& G, uint32_t e,
-                                        uint32_t& flags_out) {
+                                        uint32_t& flags_out, StageClock<C>& clk) {
+  clk.mark(kStPrologue);
   const ModelS m{hot, f};
   const uint32_t B = a.B, J = a.J, A = a.A, M = a.M, H = f.H, P = f.P;
   const uint32_t lane = G.lane;
@@ -260,6 +281,7 @@ __device__ __forceinline__ void run_env(const StepArgs& a, const FModel& f, cons
       S.quat(b) = qnormalize(qmadd(qmul_v((v3(S.ang(b)) * dt) * 0.5f, q), 1.0f, q));
     }
     G.sync();
+    clk.mark(kStActions);
     // ---- wrench (compute_forces 345-388, apply_joint_forces 122-190) and semi-implicit
     //      Euler (save_prev_state 1900-1913, integrate 394-462), children first: a body's
     //      wrench reads only its own and its parent's orientation, neither yet integrated.
@@ -315,6 +337,7 @@ __device__ __forceinline__ void run_env(const StepArgs& a, const FModel& f, cons
       G.sync();
       hi_b -= nc;
     }
+    clk.mark(kStIntegrate);
     // ---- broad phase (broad_phase 468-533): candidates in emission order ----
     const uint32_t n_old = count < M ? count : M;
     uint32_t run_first = 0, run_last = 0;  // key ranks of the first and last appended slots
@@ -355,6 +378,7 @@ __device__ __forceinline__ void run_env(const StepArgs& a, const FModel& f, cons
       }
     }
     const uint32_t n = count < M ? count : M;
+    clk.mark(kStBroad);
     // ---- stable sort by key (sort_contacts 711-745) ----
     // The stored slots [0, n_old) are sorted.  When the appended run [n_old, n) is sorted
     // too, the stable sort is a merge: an old slot i lands at i + #(appended with a
@@ -460,6 +484,7 @@ __device__ __forceinline__ void run_env(const StepArgs& a, const FModel& f, cons
       }
     }
     G.sync();
+    clk.mark(kStSort);
     // ---- narrow phase + warm start (narrow_phase 751-894, match_cached_contacts
     //      1483-1544), once per hittable pair.  The match reads the previous substep's
     //      points of the pairs with this pair's key.  When no two hittable pairs share a
@@ -544,6 +569,7 @@ __device__ __forceinline__ void run_env(const StepArgs& a, const FModel& f, cons
     }
     hit_now = G.or_all(hit_now);
     G.sync();
+    clk.mark(kStNarrow);
     // contact schedule.  L = 1: the hit slots in slot order.  L > 1: the hit slots by
     // level -- a slot's level is one more than the highest level of an earlier hit slot
     // sharing a dynamic body -- stable within a level; solving level by level, a level's
@@ -647,6 +673,7 @@ __device__ __forceinline__ void run_env(const StepArgs& a, const FModel& f, cons
       for (uint32_t u = 0; u < 4; ++u)
         if (v0 + u * L < nh) imp[i4[u] * ne] = w4[u];
     }
+    clk.mark(kStSchedule);
     // ---- XPBD joints (solve_joints 909-1399): colour by colour, as runs of one type; a
     //      run's constraints (one colour: disjoint bodies) split across the lanes.  With
     //      one lane this is the colour-sorted order, which equals colour by colour.
@@ -665,6 +692,7 @@ __device__ __forceinline__ void run_env(const StepArgs& a, const FModel& f, cons
         }
         G.sync();
       }
+    clk.mark(kStJoints);
     // ---- contacts (solve_contacts 1644-1793) ----
     auto contact = [&](uint32_t i) {
       const uint32_t hh = sw_hit(meta[i * ne]);
@@ -686,6 +714,7 @@ __device__ __forceinline__ void run_env(const StepArgs& a, const FModel& f, cons
           G.sync();
         }
     }
+    clk.mark(kStContacts);
     // ---- velocities from the position change (xpbd_update_velocities 1922-1961); the
     //      saved poses (L2 scratch) of four bodies per round are loaded before any is used ----
     constexpr uint32_t kV = 4 / L;  // bodies per lane per round
@@ -707,6 +736,7 @@ __device__ __forceinline__ void run_env(const StepArgs& a, const FModel& f, cons
       }
     }
     G.sync();
+    clk.mark(kStVelocities);
     prev_hit = hit_now;
     n_prev = n;
   }
@@ -780,6 +810,7 @@ __device__ __forceinline__ void run_env(const StepArgs& a, const FModel& f, cons
       }
     }
 
+    clk.mark(kStJointState);
     // ---------------- contact slots back to memory ----------------
     // A slot whose pair made contact while the slot was in the list carries that pair's
     // last contact; any other slot keeps the record stored at its original position,
@@ -897,6 +928,7 @@ __device__ __forceinline__ void run_env(const StepArgs& a, const FModel& f, cons
 
   // ---------------- caches, counters, task extension (one lane) ----------------
   G.sync();
+  clk.mark(kStWriteBack);
   if (!publish) {
     // step_subset: an env outside the mask keeps its public state, but the reference
     // still advanced its contact cache (world.zig:833-929 restores only public buffers).
@@ -905,6 +937,7 @@ __device__ __forceinline__ void run_env(const StepArgs& a, const FModel& f, cons
       a.prev_sep[e] = 1;
     }
     flags_out = flags | kSkipState;
+    clk.mark(kStTask);
     return;
   }
   if (stepped) flags |= kWriteJointState;
@@ -982,6 +1015,7 @@ __device__ __forceinline__ void run_env(const StepArgs& a, const FModel& f, cons
     }
   }
   flags_out = flags;
+  clk.mark(kStTask);
 }
 
 // The second half of a 64-byte contact record (indices, impulses: one 32-byte sector) in
@@ -1092,11 +1126,22 @@ __device__ __forceinline__ void write_back_moved(const StepArgs& a, const ModelS
 
 // blockDim.x = envs_per_block * L threads (envs_per_block <= 32); group g (= threadIdx.x / L)
 // owns env e0 + g.
-template <int L>
+template <int L, bool C>
 __global__ void __launch_bounds__(32 * L) fast_step_kernel(const __grid_constant__ StepArgs a,
                                                         const __grid_constant__ FModel f) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const uint32_t nt = blockDim.x, tid = threadIdx.x;
+  StageClock<C> clk;
+  [[maybe_unused]] long long clk0 = 0, ns0 = 0;
+  if constexpr (C) {
+    __shared__ unsigned long long s_clk[kStageCount];
+    if (tid < kStageCount) s_clk[tid] = 0;
+    clk.acc = s_clk;
+    clk.on = tid == 0;
+    clk.last = clk0 = clock64();
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(ns0));
+    __syncthreads();
+  }
   const uint32_t ne = nt / L;  // environments per block
   const uint32_t e0 = blockIdx.x * ne;
   if (e0 >= a.num_envs) return;
@@ -1253,7 +1298,7 @@ __global__ void __launch_bounds__(32 * L) fast_step_kernel(const __grid_constant
     G.src = int((tid & 31u) - G.lane);
     G.mask = wmask;
     uint32_t flags = kSkipState;
-    run_env<L>(a, f, pl, hot, blk, ne, g, G, e0 + g, flags);
+    run_env<L, C>(a, f, pl, hot, blk, ne, g, G, e0 + g, flags, clk);
     if (G.lane == 0) s_flags[g] = flags;
   }
   __syncthreads();
@@ -1284,6 +1329,17 @@ __global__ void __launch_bounds__(32 * L) fast_step_kernel(const __grid_constant
       gjv[t] = s_jv[j * ne + el];
     }
   }
+  if constexpr (C) {
+    if (tid == 0) {  // (the first thread's own stores are issued; the block's others may still drain)
+      clk.mark(kStEpilogue);
+      long long ns1;
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(ns1));
+      for (uint32_t k = 0; k < kStageCount; ++k) atomicAdd(a.stage_clk + k, clk.acc[k]);
+      atomicAdd(a.stage_clk + kStageCount, static_cast<unsigned long long>(clk.last - clk0));
+      atomicAdd(a.stage_clk + kStageCount + 1, static_cast<unsigned long long>(ns1 - ns0));
+      atomicAdd(a.stage_clk + kStageCount + 2, 1ull);
+    }
+  }
 }
 
 static size_t fast_smem(const StepArgs& args, const FModel& model, int lanes, int envs_per_block) {
@@ -1291,14 +1347,22 @@ static size_t fast_smem(const StepArgs& args, const FModel& model, int lanes, in
          size_t(fast_plan(args.B, args.J, args.M, model.H, uint32_t(lanes)).bytes) * envs_per_block;
 }
 
-template <int L>
-static cudaError_t launch_l(const StepArgs& args, const FModel& model, int envs_per_block, cudaStream_t stream) {
+template <int L, bool C>
+static cudaError_t launch_lc(const StepArgs& args, const FModel& model, int envs_per_block, cudaStream_t stream) {
   const size_t smem = fast_smem(args, model, L, envs_per_block);
-  cudaError_t err = cudaFuncSetAttribute(fast_step_kernel<L>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  cudaError_t err =
+      cudaFuncSetAttribute(fast_step_kernel<L, C>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
   if (err != cudaSuccess) return err;
   const uint32_t blocks = (args.num_envs + envs_per_block - 1) / envs_per_block;
-  fast_step_kernel<L><<<blocks, envs_per_block * L, smem, stream>>>(args, model);
+  fast_step_kernel<L, C><<<blocks, envs_per_block * L, smem, stream>>>(args, model);
   return cudaGetLastError();
+}
+
+// the stage-profiling instantiation runs when args.stage_clk is set
+template <int L>
+static cudaError_t launch_l(const StepArgs& args, const FModel& model, int envs_per_block, cudaStream_t stream) {
+  return args.stage_clk ? launch_lc<L, true>(args, model, envs_per_block, stream)
+                        : launch_lc<L, false>(args, model, envs_per_block, stream);
 }
 
 bool fast_lanes_supported(int lanes) { return lanes == 1 || lanes == 2; }
@@ -1317,13 +1381,13 @@ cudaError_t launch_fast_step(const StepArgs& args, const FModel& model, int lane
 template <int L>
 static int max_active_l(const StepArgs& args, const FModel& model, int envs_per_block) {
   const size_t smem = fast_smem(args, model, L, envs_per_block);
-  if (cudaFuncSetAttribute(fast_step_kernel<L>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) !=
+  if (cudaFuncSetAttribute(fast_step_kernel<L, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) !=
       cudaSuccess) {
     cudaGetLastError();
     return 0;
   }
   int n = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, fast_step_kernel<L>, envs_per_block * L, smem) !=
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, fast_step_kernel<L, false>, envs_per_block * L, smem) !=
       cudaSuccess) {
     cudaGetLastError();
     return 0;

@@ -172,6 +172,10 @@ World* World::create(const Scene& sc, const WorldConfig& cfg, std::string* err) 
     w->fmodel_.hot = reinterpret_cast<const uint4*>(w->d_hot_);
     e = e ? e : w->device_buf(&w->pose_scratch_, size_t(2) * B * E);
   }
+  if (cfg.enable_profiling) {
+    e = e ? e : w->device_buf(&w->d_stage_, size_t(kStageSlots));
+    e = e ? e : w->pinned(&w->h_stage_, size_t(kStageSlots));
+  }
   if (e != cudaSuccess) return fail(std::string("CUDA allocation failed: ") + cudaGetErrorString(e), w);
 
   // initializeState (world.zig:663-691): every env starts from the body definitions
@@ -297,6 +301,18 @@ StepArgs World::args(uint32_t substeps, const float* actions, const uint8_t* mas
   return a;
 }
 
+uint32_t World::stage_cycles(double* out, uint32_t n) const {
+  if (!stage_valid_ || !h_stage_ || h_stage_[kStageCount + 2] == 0) return 0;
+  const double blocks = double(h_stage_[kStageCount + 2]);
+  const double span = double(h_stage_[kStageCount]);
+  const uint32_t total = kStageCount + 2;
+  uint32_t k = 0;
+  for (; k < n && k < kStageCount; ++k) out[k] = double(h_stage_[k]) / blocks;
+  if (k < n) out[k++] = span / blocks;
+  if (k < n) out[k++] = span > 0 ? double(h_stage_[kStageCount + 1]) / span : 0.0;
+  return k < total ? k : total;
+}
+
 cudaError_t World::launch(uint32_t substeps, const float* actions, const uint8_t* mask) {
   StepArgs a = args(substeps, actions, mask);
   // host copies of what this step writes go stale (read_sensors writes every obs entry;
@@ -305,8 +321,19 @@ cudaError_t World::launch(uint32_t substeps, const float* actions, const uint8_t
   task_stale_ = task_stale_ || task_.enabled != 0;
   out_stream_ = stream_;
   if (!use_fast_) return launch_step(a, lanes_, envs_per_block_, stream_);
+  if (d_stage_) {  // profiling world: the stage-profiling instantiation, its sums copied back
+    a.stage_clk = d_stage_;
+    cudaError_t e = cudaMemsetAsync(d_stage_, 0, kStageSlots * sizeof(unsigned long long), stream_);
+    if (e != cudaSuccess) return e;
+  }
   cudaError_t e = launch_fast_step(a, fmodel_, fast_lanes_, fast_epb_, stream_);
   if (e != cudaSuccess) return e;
+  if (d_stage_) {
+    e = cudaMemcpyAsync(h_stage_, d_stage_, kStageSlots * sizeof(unsigned long long), cudaMemcpyDeviceToHost,
+                        stream_);
+    if (e != cudaSuccess) return e;
+    a.stage_clk = nullptr;
+  }
   // environments the fast kernel handed over (normally none): general kernel, list mode
   a.env_list = d_odd_ + 2;
   a.env_count = d_odd_;
@@ -351,6 +378,17 @@ cudaError_t World::step(const float* actions, uint32_t substeps, bool async) {
     for (uint32_t v : c) total += v;
     prof_.num_contacts = uint32_t(total > 0xFFFFFFFFull ? 0xFFFFFFFFull : total);
     prof_.num_active_constraints = model_.K * cfg_.num_envs;
+    // stage times (environment-per-lane kernel): the blocks run side by side, so a stage's
+    // time is its average over the blocks, in cycles converted with the measured ns/cycle
+    double st[kStageCount + 2];
+    stage_valid_ = use_fast_ && d_stage_ != nullptr;
+    if (stage_valid_ && stage_cycles(st, kStageCount + 2) == kStageCount + 2) {
+      const double ns = st[kStageCount + 1];
+      prof_.integrate_ns = float((st[kStActions] + st[kStIntegrate] + st[kStVelocities]) * ns);
+      prof_.collision_broad_ns = float((st[kStBroad] + st[kStSort]) * ns);
+      prof_.collision_narrow_ns = float((st[kStNarrow] + st[kStSchedule]) * ns);
+      prof_.constraint_solve_ns = float((st[kStJoints] + st[kStContacts]) * ns);
+    }
   } else {
     prof_ = Profiling{};
   }

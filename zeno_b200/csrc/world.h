@@ -75,7 +75,15 @@ class World {
   uint64_t memory_usage() const { return bytes_; }
   int device() const { return device_; }
   Profiling profiling() const { return prof_; }
-  void reset_profiling() { prof_ = Profiling{}; }
+  void reset_profiling() {
+    prof_ = Profiling{};
+    stage_valid_ = false;
+  }
+  // Stage profile of the last synchronous step of a profiling world on the
+  // environment-per-lane kernel: per-stage clock cycles averaged over the blocks
+  // (kStageCount values, Stage order), then the average block span in cycles and the
+  // nanoseconds per cycle.  Returns the values written, 0 when no profile exists.
+  uint32_t stage_cycles(double* out, uint32_t n) const;
   int lanes() const { return use_fast_ ? fast_lanes_ : lanes_; }
   int envs_per_block() const { return use_fast_ ? fast_epb_ : envs_per_block_; }
   bool fast_available() const { return fast_ok_; }
@@ -140,6 +148,9 @@ class World {
   uint32_t narrow_mode_ = 0;
   uint32_t broad_mode_ = 0;
   float4* pose_scratch_ = nullptr;
+  unsigned long long* d_stage_ = nullptr;  // profiling: the kernel's stage sums (kStageSlots)
+  unsigned long long* h_stage_ = nullptr;  // pinned copy
+  bool stage_valid_ = false;
   uint64_t bytes_ = 0;
   cudaStream_t own_stream_ = nullptr;
   cudaStream_t stream_ = nullptr;

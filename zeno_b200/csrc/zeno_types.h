@@ -159,6 +159,30 @@ struct StepArgs {
   uint32_t* env_count;
   uint32_t* env_done;        // blocks finished (the last one clears env_count)
   float4* pose_scratch;      // environment-per-lane kernel: 2 * B * num_envs poses before integration
+  // stage profile (environment-per-lane kernel, when profiling is enabled; null otherwise):
+  // kStageCount per-stage clock64 sums over the blocks' first threads, then the sums of the
+  // blocks' clock64 and %globaltimer (ns) spans and the number of blocks
+  unsigned long long* stage_clk;
 };
+
+// Stages of the stage profile, in step order.
+enum Stage : uint32_t {
+  kStPrologue = 0,     // block loads: model image, state, contact lists, hand-over checks
+  kStActions,          // actions -> joint torques, kinematic bodies
+  kStIntegrate,        // gravity and joint wrenches, semi-implicit Euler
+  kStBroad,            // broad phase
+  kStSort,             // contact list sort / merge
+  kStNarrow,           // narrow phase and warm-start match
+  kStSchedule,         // contact schedule and slot impulses
+  kStJoints,           // XPBD joint constraints
+  kStContacts,         // contact solve
+  kStVelocities,       // velocities from the pose change
+  kStJointState,       // joint states and sensors (last substep)
+  kStWriteBack,        // contact records back to memory
+  kStTask,             // caches, counters, task extension
+  kStEpilogue,         // deferred record writes, coalesced state stores
+  kStageCount
+};
+constexpr uint32_t kStageSlots = kStageCount + 3;  // + clock span, ns span, blocks
 
 }  // namespace zb
