@@ -430,6 +430,9 @@ def run_ours(args, rank, world_size, local_rank):
         w.set_narrow_phase(args.narrow)
     if args.broad is not None:
         w.set_broad_phase(args.broad)
+    if args.launch:
+        lanes, epb = (int(x) for x in args.launch.split(","))
+        w.set_launch(lanes, epb)
     config = bench_config(args, sc, E, world_size)
     if (w.get_narrow_phase(), w.get_broad_phase()) != (config["narrow_phase"], config["broad_phase"]):
         raise RuntimeError("world settings differ from the reported config")
@@ -560,6 +563,8 @@ def run_stage_profile(args):
                             enable_profiling=True)
     if args.narrow is not None:
         w.set_narrow_phase(args.narrow)
+    if args.launch:
+        w.set_launch(*(int(x) for x in args.launch.split(",")))
     init = initial_state({"bodies": w.model_table("bodies"), "joints": w.model_table("joints")},
                          w.get_body_positions(zero_copy=False)[0], w.get_body_quaternions(zero_copy=False)[0],
                          sc, E, 0)
@@ -602,6 +607,7 @@ def main():
     ap.add_argument("--semantics", choices=["reference", "corrected"], default="reference")
     ap.add_argument("--gather", action="store_true",
                     help="with N > 1: also time the optional NCCL all-gather of the step outputs (not in value)")
+    ap.add_argument("--launch", default="", help="launch shape 'lanes,envs_per_block' (default: the world's choice)")
     ap.add_argument("--stage-profile", action="store_true",
                     help="print per-stage device cycles of the step (instrumented kernel; no throughput line)")
     ap.add_argument("--record-traffic", nargs=4, metavar=("CSV", "SCENE", "ENVS", "COMMAND"),

@@ -5,6 +5,9 @@ floating-point operation is the one written in the source (explicit __fmaf_rn ca
 are the only fused operations); host model-building code is compiled with
 -ffp-contract=off for the same reason.
 
+The library is also copied to <repo>/zig-out/lib/libzeno.so, where the reference's own
+Python package and ABI check look for it.  The sources compile in parallel.
+
 Usage: python -m zeno_b200.build [--force]
 """
 from __future__ import annotations
@@ -13,6 +16,7 @@ import os
 import shutil
 import subprocess
 import sys
+from concurrent.futures import ThreadPoolExecutor
 from pathlib import Path
 
 PKG = Path(__file__).resolve().parent
@@ -20,6 +24,9 @@ CSRC = PKG / "csrc"
 INCLUDE = PKG.parent / "include"
 OUT_DIR = PKG / "lib"
 LIB = OUT_DIR / "libzeno.so"
+# where the reference's own Python package (python/zeno/_ffi.py _find_library) and its
+# tests/check_abi_contract.py look for the library: <repo>/zig-out/lib/libzeno.so
+ZIG_OUT_LIB = PKG.parent / "zig-out" / "lib" / "libzeno.so"
 OBJ_DIR = PKG / "_build"
 
 CUDA_HOME = Path(os.environ.get("CUDA_HOME", "/usr/local/cuda"))
@@ -48,7 +55,6 @@ def build(force: bool = False, verbose: bool = False) -> Path:
         return LIB
     OBJ_DIR.mkdir(exist_ok=True)
     OUT_DIR.mkdir(exist_ok=True)
-    objs = []
     cxx = shutil.which("g++") or "g++"
 
     def run(cmd):
@@ -60,17 +66,19 @@ def build(force: bool = False, verbose: bool = False) -> Path:
         if verbose and (r.stdout or r.stderr):
             print(r.stdout, r.stderr)
 
-    for src in CU_SOURCES:
-        obj = OBJ_DIR / (src + ".o")
-        run([NVCC, *NVCC_FLAGS, f"-I{INCLUDE}", "-c", str(CSRC / src), "-o", str(obj)])
-        objs.append(str(obj))
-    for src in CXX_SOURCES:
-        obj = OBJ_DIR / (src + ".o")
-        run([cxx, *CXX_FLAGS, "-c", str(CSRC / src), "-o", str(obj)])
-        objs.append(str(obj))
+    jobs = [[NVCC, *NVCC_FLAGS, f"-I{INCLUDE}", "-c", str(CSRC / src), "-o", str(OBJ_DIR / (src + ".o"))]
+            for src in CU_SOURCES]
+    jobs += [[cxx, *CXX_FLAGS, "-c", str(CSRC / src), "-o", str(OBJ_DIR / (src + ".o"))] for src in CXX_SOURCES]
+    objs = [cmd[-1] for cmd in jobs]
+    with ThreadPoolExecutor(max_workers=max(1, min(len(jobs), os.cpu_count() or 1))) as pool:
+        for f in [pool.submit(run, cmd) for cmd in jobs]:
+            f.result()
     tmp = LIB.with_suffix(".so.tmp")
     run([NVCC, *ARCH, "-shared", "-o", str(tmp), *objs, "-Xlinker", "--no-undefined"])
     os.replace(tmp, LIB)
+    ZIG_OUT_LIB.parent.mkdir(parents=True, exist_ok=True)
+    shutil.copyfile(LIB, ZIG_OUT_LIB.with_suffix(".so.tmp"))
+    os.replace(ZIG_OUT_LIB.with_suffix(".so.tmp"), ZIG_OUT_LIB)
     return LIB
 
 

@@ -158,7 +158,7 @@ float* zeno_world_get_joint_velocities(ZenoWorldHandle world) { return world ? W
 float* zeno_world_get_joint_forces(ZenoWorldHandle world) { return world ? W(world)->jtorque : nullptr; }
 uint32_t* zeno_world_get_contact_counts(ZenoWorldHandle world) { return world ? W(world)->counts : nullptr; }
 float* zeno_world_get_sensor_data(ZenoWorldHandle world) { return zeno_world_get_observations(world); }
-void* zeno_world_get_contacts(ZenoWorldHandle world) { return world ? W(world)->contacts : nullptr; }
+void* zeno_world_get_contacts(ZenoWorldHandle world) { return world ? W(world)->expose_contacts() : nullptr; }
 
 int zeno_world_set_body_positions(ZenoWorldHandle world, const float* positions, const uint8_t* env_mask) {
   if (!world) return ZENO_INVALID_HANDLE;

@@ -1127,7 +1127,7 @@ __device__ __forceinline__ void write_back_moved(const StepArgs& a, const ModelS
 // blockDim.x = envs_per_block * L threads (envs_per_block <= 32); group g (= threadIdx.x / L)
 // owns env e0 + g.
 template <int L, bool C>
-__global__ void __launch_bounds__(32 * L) fast_step_kernel(const __grid_constant__ StepArgs a,
+__global__ void __launch_bounds__(32 * L, 1) fast_step_kernel(const __grid_constant__ StepArgs a,
                                                         const __grid_constant__ FModel f) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const uint32_t nt = blockDim.x, tid = threadIdx.x;
@@ -1154,14 +1154,20 @@ __global__ void __launch_bounds__(32 * L) fast_step_kernel(const __grid_constant
   // With one lane per environment the slot loader's first round (below) is issued before
   // anything else: its addresses need neither the image nor the list headers, which take
   // two memory round trips.  (With two lanes the held registers would spill.)
+  // With the slot cache (the kernel's own copy of the lists it wrote last step) the lists
+  // arrive by cp.async with the state instead, and only environments whose cache entry is
+  // not current read the records.
+  const bool cached = a.slot_cache_w != nullptr;
   const Contact* gcb = a.contacts + size_t(e0) * M;
   constexpr uint32_t kU = 8;  // slots per thread per round: their loads are in flight together
   uint4 ix[kU], iq[kU];
   if constexpr (L == 1) {
+    if (!cached) {
 #pragma unroll
-    for (uint32_t u = 0; u < kU; ++u) {
-      const uint32_t t = tid + u * nt;
-      if (t < nb * M) load_idx_imp(gcb + t, ix[u], iq[u]);
+      for (uint32_t u = 0; u < kU; ++u) {
+        const uint32_t t = tid + u * nt;
+        if (t < nb * M) load_idx_imp(gcb + t, ix[u], iq[u]);
+      }
     }
   }
   // the hot image and (below) the block's state arrive by cp.async, all copies in flight at once
@@ -1197,6 +1203,18 @@ __global__ void __launch_bounds__(32 * L) fast_step_kernel(const __grid_constant
     const uint32_t el = t / J, j = t - el * J;
     cp_async4(s_jt + j * ne + el, gjt + t);
   }
+  uint32_t* s_hdr = reinterpret_cast<uint32_t*>(blk + pl.hdr * ne);
+  float* s_imp = reinterpret_cast<float*>(blk + pl.imp * ne);
+  uint32_t* s_meta = reinterpret_cast<uint32_t*>(blk + pl.meta * ne);
+  uint8_t* s_aux = blk + pl.aux * ne;
+  const size_t E = a.num_envs;
+  if (cached) {  // slot words and impulses from the cache, straight into their places
+    for (uint32_t t = tid; t < nb * M; t += nt) {
+      const uint32_t i = t / nb, el = t - i * nb;
+      cp_async4(s_meta + i * ne + el, a.slot_cache_w + size_t(i) * E + e0 + el);
+      cp_async4(s_imp + i * ne + el, a.slot_cache_imp + size_t(i) * E + e0 + el);
+    }
+  }
   cp_async_commit();
   cp_async_wait<1>();  // this thread's part of the hot image
   __syncthreads();
@@ -1208,30 +1226,38 @@ __global__ void __launch_bounds__(32 * L) fast_step_kernel(const __grid_constant
         mi.x < 1e-8f ? make_float4(0.0f, 0.0f, 0.0f, 0.0f) : with_w(gv * rcp_(mi.x), 0.0f);
   }
   // ---- contact list headers, then the slots: slot words, impulses, previous-list ranks ----
-  uint32_t* s_hdr = reinterpret_cast<uint32_t*>(blk + pl.hdr * ne);
-  float* s_imp = reinterpret_cast<float*>(blk + pl.imp * ne);
-  uint32_t* s_meta = reinterpret_cast<uint32_t*>(blk + pl.meta * ne);
-  uint8_t* s_aux = blk + pl.aux * ne;
   for (uint32_t el = tid; el < nb; el += nt) {
     const uint32_t e = e0 + el;
-    s_hdr[el] = a.counts[e];
-    s_hdr[ne + el] = a.prev_counts[e];
-    s_hdr[2 * ne + el] = a.prev_sep[e];
+    const uint32_t c = a.counts[e], pc = a.prev_counts[e], sep = a.prev_sep[e];
+    s_hdr[el] = c;
+    s_hdr[ne + el] = pc;
+    s_hdr[2 * ne + el] = sep;
     s_hdr[3 * ne + el] = 0;
+    // (cached launches) 1: read this environment's records.  The cache holds the list the
+    // last step left, so it serves when that step wrote it, the previous list was not
+    // separated by a subset step, and the counter has not grown since (it only shrinks,
+    // by a reset)
+    if (cached) s_flags[el] = (a.slot_cache_ok[e] != 0 && sep == 0 && c <= pc) ? 0u : 1u;
   }
-  __syncthreads();
+  bool need_records = true;
+  if (cached) need_records = __syncthreads_or(tid < nb && s_flags[tid] != 0) != 0;
+  else __syncthreads();
+  if (cached && need_records) {  // the cache copies land before any record overwrites them
+    cp_async_wait<0>();
+    __syncthreads();
+  }
   const ModelS m{hot, f};
   // An environment is handed over (s_hdr[3] set) when a slot tuple of either list is not
   // a broad-phase candidate, when a list is not sorted by key, or when a slot of the
   // previous list carries non-zero tangent impulses (a warm start would copy them; this
   // kernel keeps only normal impulses).  This library never writes any of these.  Only
   // the second half of each 64-byte record (indices, impulses) is read.
-  for (uint32_t t0 = tid; t0 < nb * M; t0 += kU * nt) {
-    if (L != 1 || t0 != tid) {
+  for (uint32_t t0 = tid; need_records && t0 < nb * M; t0 += kU * nt) {
+    if (L != 1 || t0 != tid || cached) {
 #pragma unroll
       for (uint32_t u = 0; u < kU; ++u) {
         const uint32_t t = t0 + u * nt;
-        if (t < nb * M) load_idx_imp(gcb + t, ix[u], iq[u]);
+        if (t < nb * M && !(cached && s_flags[t / M] == 0)) load_idx_imp(gcb + t, ix[u], iq[u]);
       }
     }
 #pragma unroll
@@ -1239,6 +1265,7 @@ __global__ void __launch_bounds__(32 * L) fast_step_kernel(const __grid_constant
       const uint32_t t = t0 + u * nt;
       if (t >= nb * M) continue;
       const uint32_t el = t / M, i = t - el * M;
+      if (cached && s_flags[el] == 0) continue;
       s_imp[i * ne + el] = __uint_as_float(iq[u].x);
       if (i < s_hdr[el]) {  // i < min(count, M)
         const uint32_t p = lookup_pair(m, ix[u]);
@@ -1261,8 +1288,8 @@ __global__ void __launch_bounds__(32 * L) fast_step_kernel(const __grid_constant
   __syncthreads();
   // both lists sorted by key: one thread per environment walks its slots (at each slot
   // index the threads read consecutive words)
-  for (uint32_t el = tid; el < nb; el += nt) {
-    if (s_hdr[3 * ne + el]) continue;
+  for (uint32_t el = tid; need_records && el < nb; el += nt) {
+    if (s_hdr[3 * ne + el] || (cached && s_flags[el] == 0)) continue;
     const uint32_t nc = min(s_hdr[el], M), np = min(s_hdr[ne + el], M);
     bool bad = false;
     uint32_t r0 = nc > 0 ? sw_rank(s_meta[el]) : 0u;
@@ -1281,8 +1308,21 @@ __global__ void __launch_bounds__(32 * L) fast_step_kernel(const __grid_constant
     }
     if (bad) s_hdr[3 * ne + el] = 1;
   }
-  cp_async_wait<0>();  // this thread's part of the body state and joint torques
+  cp_async_wait<0>();  // this thread's part of the body state and joint torques (and cache)
   __syncthreads();
+  if (cached) {
+    // cached lists: each slot word gets its slot as origin (the cache holds the words as
+    // the last step left them), and the previous-list key ranks are the stored list's
+    for (uint32_t t = tid; t < nb * M; t += nt) {
+      const uint32_t i = t / nb, el = t - i * nb;
+      if (s_flags[el] != 0 || i >= min(s_hdr[ne + el], M)) continue;
+      const uint32_t w = s_meta[i * ne + el];
+      s_meta[i * ne + el] = (w & ~(0xFFu << 8 | kVisited)) | (i << 8);
+      s_aux[i * ne + el] = uint8_t(sw_rank(w));
+    }
+    __syncthreads();
+    for (uint32_t el = tid; el < nb; el += nt) s_flags[el] = 0;
+  }
   for (uint32_t el = tid; el < nb; el += nt)
     if (s_hdr[3 * ne + el]) {
       a.odd_list[atomicAdd(a.odd_count, 1u)] = e0 + el;
@@ -1328,6 +1368,18 @@ __global__ void __launch_bounds__(32 * L) fast_step_kernel(const __grid_constant
       gjp[t] = s_jp[j * ne + el];
       gjv[t] = s_jv[j * ne + el];
     }
+  }
+  if (a.slot_cache_w != nullptr) {  // the lists as this step left them, for the next step's slot cache
+    // (slot words as they stand; the next step's prologue re-sets their origin fields)
+    const size_t En = a.num_envs;  // (re-read from the parameters: nothing stays live across the step)
+#pragma unroll 4
+    for (uint32_t t = tid; t < nb * M; t += nt) {
+      const uint32_t i = t / nb, el = t - i * nb;
+      if (s_flags[el] & kSkipState) continue;
+      a.slot_cache_w[size_t(i) * En + e0 + el] = s_meta[i * ne + el];
+      a.slot_cache_imp[size_t(i) * En + e0 + el] = s_imp[i * ne + el];
+    }
+    for (uint32_t el = tid; el < nb; el += nt) a.slot_cache_ok[e0 + el] = (s_flags[el] & kSkipState) ? 0 : 1;
   }
   if constexpr (C) {
     if (tid == 0) {  // (the first thread's own stores are issued; the block's others may still drain)

@@ -171,6 +171,9 @@ World* World::create(const Scene& sc, const WorldConfig& cfg, std::string* err) 
     w->hot_capacity_ = w->hot_image_.size();
     w->fmodel_.hot = reinterpret_cast<const uint4*>(w->d_hot_);
     e = e ? e : w->device_buf(&w->pose_scratch_, size_t(2) * B * E);
+    e = e ? e : w->device_buf(&w->d_cache_w_, size_t(M) * E);
+    e = e ? e : w->device_buf(&w->d_cache_imp_, size_t(M) * E);
+    e = e ? e : w->device_buf(&w->d_cache_ok_, size_t(E));
   }
   if (cfg.enable_profiling) {
     e = e ? e : w->device_buf(&w->d_stage_, size_t(kStageSlots));
@@ -320,7 +323,18 @@ cudaError_t World::launch(uint32_t substeps, const float* actions, const uint8_t
   obs_stale_ = obs_stale_ || model_.obs_dim > 0;
   task_stale_ = task_stale_ || task_.enabled != 0;
   out_stream_ = stream_;
-  if (!use_fast_) return launch_step(a, lanes_, envs_per_block_, stream_);
+  if (!use_fast_) {
+    cache_dirty_ = true;  // the general kernel does not maintain the slot cache
+    return launch_step(a, lanes_, envs_per_block_, stream_);
+  }
+  if (d_cache_w_ && !contacts_exposed_) {  // the slot cache (see World::expose_contacts)
+    if (cache_dirty_) {
+      cudaError_t e = cudaMemsetAsync(d_cache_ok_, 0, cfg_.num_envs, stream_);
+      if (e != cudaSuccess) return e;
+      cache_dirty_ = false;
+    }
+    a.slot_cache_w = d_cache_w_, a.slot_cache_imp = d_cache_imp_, a.slot_cache_ok = d_cache_ok_;
+  }
   if (d_stage_) {  // profiling world: the stage-profiling instantiation, its sums copied back
     a.stage_clk = d_stage_;
     cudaError_t e = cudaMemsetAsync(d_stage_, 0, kStageSlots * sizeof(unsigned long long), stream_);
@@ -334,6 +348,7 @@ cudaError_t World::launch(uint32_t substeps, const float* actions, const uint8_t
     if (e != cudaSuccess) return e;
     a.stage_clk = nullptr;
   }
+  a.slot_cache_w = nullptr, a.slot_cache_imp = nullptr, a.slot_cache_ok = nullptr;
   // environments the fast kernel handed over (normally none): general kernel, list mode
   a.env_list = d_odd_ + 2;
   a.env_count = d_odd_;
@@ -575,6 +590,7 @@ int World::set_narrow_phase(uint32_t mode) {
   if (mode == narrow_mode_) return 0;
   if (cudaStreamSynchronize(stream_) != cudaSuccess) return -4;
   narrow_mode_ = mode;
+  cache_dirty_ = true;  // hittable indices in the cached slot words depend on the narrow phase
   std::string why;
   std::vector<uint8_t> img;
   FModel fm{};

@@ -84,6 +84,12 @@ class World {
   // (kStageCount values, Stage order), then the average block span in cycles and the
   // nanoseconds per cycle.  Returns the values written, 0 when no profile exists.
   uint32_t stage_cycles(double* out, uint32_t n) const;
+  // The contacts buffer pointer for the caller (zeno_world_get_contacts).  From then on
+  // every step reads the contact records themselves, so that the caller's writes count.
+  Contact* expose_contacts() {
+    contacts_exposed_ = true;
+    return contacts;
+  }
   int lanes() const { return use_fast_ ? fast_lanes_ : lanes_; }
   int envs_per_block() const { return use_fast_ ? fast_epb_ : envs_per_block_; }
   bool fast_available() const { return fast_ok_; }
@@ -148,6 +154,14 @@ class World {
   uint32_t narrow_mode_ = 0;
   uint32_t broad_mode_ = 0;
   float4* pose_scratch_ = nullptr;
+  // slot cache of the environment-per-lane kernel (StepArgs.slot_cache_*): used until the
+  // contacts buffer is handed to the caller; its flags are cleared when a launch did not
+  // maintain it (general kernel, model re-pack)
+  uint32_t* d_cache_w_ = nullptr;
+  float* d_cache_imp_ = nullptr;
+  uint8_t* d_cache_ok_ = nullptr;
+  bool contacts_exposed_ = false;
+  bool cache_dirty_ = true;
   unsigned long long* d_stage_ = nullptr;  // profiling: the kernel's stage sums (kStageSlots)
   unsigned long long* h_stage_ = nullptr;  // pinned copy
   bool stage_valid_ = false;

@@ -163,6 +163,14 @@ struct StepArgs {
   // kStageCount per-stage clock64 sums over the blocks' first threads, then the sums of the
   // blocks' clock64 and %globaltimer (ns) spans and the number of blocks
   unsigned long long* stage_clk;
+  // slot cache (environment-per-lane kernel; null when the contacts buffer has been handed
+  // to the caller, whose writes the next step must then read): per environment the contact
+  // list as the kernel left it, [slot][env]: slot words (candidate | slot << 8 | hittable
+  // << 16 | key rank << 24) and impulses[0] of every slot, and a per-env flag set when the
+  // environment's entries are current
+  uint32_t* slot_cache_w;
+  float* slot_cache_imp;
+  uint8_t* slot_cache_ok;
 };
 
 // Stages of the stage profile, in step order.
