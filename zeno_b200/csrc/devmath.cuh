@@ -145,9 +145,29 @@ __device__ __forceinline__ float atan2r(float y, float x) {
   if (y < 0.0f) r = -r;
   return r;
 }
+// Arcsine with the classic range reduction (Cody & Waite): |x| <= 1/2: a + a z P(z),
+// z = a^2; above: pi/2 - 2 (s + s z P(z)), z = (1 - a)/2, s = sqrt(z) = z rsq(z).  P of
+// degree 4 on [0, 1/4] fitted by zeno_b200/csrc/fit_asin_poly.py; within 2.4 ulp.  The
+// branch skips the square root where the joint solver's small angles fall.
 __device__ __forceinline__ float asinr(float x) {
-  const float t = (1.0f - x) * (1.0f + x);
-  return atan2r(x, t * rsq_(t));
+  const float a = fabsf(x);
+  const bool small = a <= 0.5f;
+  float z, s;
+  if (small) {
+    z = a * a;
+    s = a;
+  } else {
+    z = 0.5f * (1.0f - a);
+    s = z * rsq_(z);
+  }
+  float p = 0.0421663373708725f;
+  p = fma_(p, z, 0.024179499596357346f);
+  p = fma_(p, z, 0.045470379292964935f);
+  p = fma_(p, z, 0.07495297491550446f);
+  p = fma_(p, z, 0.16666752099990845f);
+  const float t = fma_(s * z, p, s);
+  const float r = small ? t : fma_(-2.0f, t, 1.57079632679490f);
+  return x < 0.0f ? -r : r;
 }
 
 // splitmix64 finalizer (counter-based random numbers for the episode-reset extension)

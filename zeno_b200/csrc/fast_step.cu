@@ -1208,11 +1208,12 @@ __global__ void __launch_bounds__(32 * L, 1) fast_step_kernel(const __grid_const
   uint32_t* s_meta = reinterpret_cast<uint32_t*>(blk + pl.meta * ne);
   uint8_t* s_aux = blk + pl.aux * ne;
   const size_t E = a.num_envs;
-  if (cached) {  // slot words and impulses from the cache, straight into their places
-    for (uint32_t t = tid; t < nb * M; t += nt) {
-      const uint32_t i = t / nb, el = t - i * nb;
-      cp_async4(s_meta + i * ne + el, a.slot_cache_w + size_t(i) * E + e0 + el);
-      cp_async4(s_imp + i * ne + el, a.slot_cache_imp + size_t(i) * E + e0 + el);
+  // slot loops of the cache: thread tid serves environment tid % ne, slots tid / ne + k L
+  const uint32_t sc_el = tid % ne, sc_i0 = tid / ne;
+  if (cached && sc_el < nb) {  // slot words and impulses from the cache, straight into their places
+    for (uint32_t i = sc_i0; i < M; i += L) {
+      cp_async4(s_meta + i * ne + sc_el, a.slot_cache_w + size_t(i) * E + e0 + sc_el);
+      cp_async4(s_imp + i * ne + sc_el, a.slot_cache_imp + size_t(i) * E + e0 + sc_el);
     }
   }
   cp_async_commit();
@@ -1313,12 +1314,14 @@ __global__ void __launch_bounds__(32 * L, 1) fast_step_kernel(const __grid_const
   if (cached) {
     // cached lists: each slot word gets its slot as origin (the cache holds the words as
     // the last step left them), and the previous-list key ranks are the stored list's
-    for (uint32_t t = tid; t < nb * M; t += nt) {
-      const uint32_t i = t / nb, el = t - i * nb;
-      if (s_flags[el] != 0 || i >= min(s_hdr[ne + el], M)) continue;
-      const uint32_t w = s_meta[i * ne + el];
-      s_meta[i * ne + el] = (w & ~(0xFFu << 8 | kVisited)) | (i << 8);
-      s_aux[i * ne + el] = uint8_t(sw_rank(w));
+    if (sc_el < nb && s_flags[sc_el] == 0) {
+      const uint32_t np = min(s_hdr[ne + sc_el], M);
+#pragma unroll 4
+      for (uint32_t i = sc_i0; i < np; i += L) {
+        const uint32_t w = s_meta[i * ne + sc_el];
+        s_meta[i * ne + sc_el] = (w & ~(0xFFu << 8 | kVisited)) | (i << 8);
+        s_aux[i * ne + sc_el] = uint8_t(sw_rank(w));
+      }
     }
     __syncthreads();
     for (uint32_t el = tid; el < nb; el += nt) s_flags[el] = 0;
@@ -1344,20 +1347,34 @@ __global__ void __launch_bounds__(32 * L, 1) fast_step_kernel(const __grid_const
   __syncthreads();
   write_back_moved(a, m, pl, blk, ne, nb, e0, tid, nt);
 
-  // ---- coalesced store: state, accelerations, joint torques and states ----
-  for (uint32_t t = tid; t < nb * B; t += nt) {
-    const uint32_t el = t / B, b = t - el * B, si = b * ne + el;
-    const uint32_t fl = s_flags[el];
-    if (fl & kSkipState) continue;
-    const float4 v1 = s_vel[si];
-    if (!(fl & kAccWritten)) {
-      const float4 v0 = gvel[t];
-      gacc[t] = make_float4((v1.x - v0.x) * a.inv_step, (v1.y - v0.y) * a.inv_step, (v1.z - v0.z) * a.inv_step, 0.0f);
+  // ---- coalesced store: state, accelerations, joint torques and states; the step-start
+  //      velocities (for the accelerations) of four elements are loaded before any store ----
+  for (uint32_t t0 = tid; t0 < nb * B; t0 += 4 * nt) {
+    uint32_t fl[4], si[4];
+    float4 v0[4];
+#pragma unroll
+    for (uint32_t u = 0; u < 4; ++u) {
+      const uint32_t t = t0 + u * nt;
+      fl[u] = kSkipState;
+      if (t >= nb * B) continue;
+      const uint32_t el = t / B, b = t - el * B;
+      si[u] = b * ne + el;
+      fl[u] = s_flags[el];
+      if (!(fl[u] & (kSkipState | kAccWritten))) v0[u] = gvel[t];
     }
-    gpos[t] = s_pos[si];
-    gquat[t] = s_quat[si];
-    gvel[t] = v1;
-    gang[t] = s_ang[si];
+#pragma unroll
+    for (uint32_t u = 0; u < 4; ++u) {
+      const uint32_t t = t0 + u * nt;
+      if (fl[u] & kSkipState) continue;
+      const float4 v1 = s_vel[si[u]];
+      if (!(fl[u] & kAccWritten))
+        gacc[t] = make_float4((v1.x - v0[u].x) * a.inv_step, (v1.y - v0[u].y) * a.inv_step,
+                              (v1.z - v0[u].z) * a.inv_step, 0.0f);
+      gpos[t] = s_pos[si[u]];
+      gquat[t] = s_quat[si[u]];
+      gvel[t] = v1;
+      gang[t] = s_ang[si[u]];
+    }
   }
   for (uint32_t t = tid; t < nb * J; t += nt) {
     const uint32_t el = t / J, j = t - el * J;
@@ -1372,12 +1389,13 @@ __global__ void __launch_bounds__(32 * L, 1) fast_step_kernel(const __grid_const
   if (a.slot_cache_w != nullptr) {  // the lists as this step left them, for the next step's slot cache
     // (slot words as they stand; the next step's prologue re-sets their origin fields)
     const size_t En = a.num_envs;  // (re-read from the parameters: nothing stays live across the step)
+    const uint32_t el = tid % ne;
+    if (el < nb && !(s_flags[el] & kSkipState)) {
 #pragma unroll 4
-    for (uint32_t t = tid; t < nb * M; t += nt) {
-      const uint32_t i = t / nb, el = t - i * nb;
-      if (s_flags[el] & kSkipState) continue;
-      a.slot_cache_w[size_t(i) * En + e0 + el] = s_meta[i * ne + el];
-      a.slot_cache_imp[size_t(i) * En + e0 + el] = s_imp[i * ne + el];
+      for (uint32_t i = tid / ne; i < M; i += L) {
+        a.slot_cache_w[size_t(i) * En + e0 + el] = s_meta[i * ne + el];
+        a.slot_cache_imp[size_t(i) * En + e0 + el] = s_imp[i * ne + el];
+      }
     }
     for (uint32_t el = tid; el < nb; el += nt) a.slot_cache_ok[e0 + el] = (s_flags[el] & kSkipState) ? 0 : 1;
   }
