@@ -229,10 +229,13 @@ def record_traffic(csv_path: str, scene: str, envs: int, command: str) -> None:
     idx = {k: head.index(k) for k in ("Kernel Name", "dram__bytes_read.sum", "dram__bytes_write.sum")}
     units = rows[1] if len(rows) > 1 and not rows[1][idx["Kernel Name"]] else None
     scale = {"byte": 1, "Kbyte": 1e3, "Mbyte": 1e6, "Gbyte": 1e9, "KB": 1e3, "MB": 1e6, "GB": 1e9}
+    import re
     per = {}
     for r in rows[2 if units else 1:]:
-        name = r[idx["Kernel Name"]]
-        k = ("zb::" + name.split("zb::", 1)[1].split("(", 1)[0]) if "zb::" in name else name.split("(", 1)[0]
+        km = re.search(r"\b(fast_step_kernel|step_kernel)<(\d+)", r[idx["Kernel Name"]])
+        if not km:
+            continue
+        k = f"zb::{km.group(1)}<{km.group(2)}>"  # the name bench.py reports (lanes only)
         tot = 0.0
         for m in ("dram__bytes_read.sum", "dram__bytes_write.sum"):
             u = units[idx[m]] if units else "byte"
@@ -240,8 +243,6 @@ def record_traffic(csv_path: str, scene: str, envs: int, command: str) -> None:
         per.setdefault(k, []).append(tot)
     data = json.loads(TRAFFIC_FILE.read_text()) if TRAFFIC_FILE.exists() else {"captures": []}
     for k, v in per.items():
-        if not k.startswith("zb::") or "step_kernel" not in k:
-            continue
         data["captures"] = [c for c in data["captures"] if not (c["kernel"] == k and c["scene"] == scene)]
         data["captures"].append({"kernel": k, "scene": scene, "envs": envs, "launches": len(v),
                                  "dram_bytes_per_launch": sum(v) / len(v), "command": command})
