@@ -21,6 +21,7 @@ constexpr uint32_t kB = 32, kJ = 32, kJF = 64, kK = 96, kG = 32, kP = 254, kH = 
 constexpr uint32_t kNoHit = 127;  // hittable-index field of a candidate that never hits
 constexpr uint32_t kNoPair = 255; // gg_pair entry for geom pairs that are not candidates
 constexpr uint32_t kMaxSlots = 255;  // contact slots per env the per-slot byte fields can index
+constexpr uint32_t kNoGroup = 0xFFu; // empty member of a constraint group
 }  // namespace fm
 
 struct FModel {
@@ -75,6 +76,14 @@ struct FModel {
   uint32_t o_gforce;           // float4[B], filled by each block: gravity * mass (zero when massless)
   uint32_t o_runs;             // u32[num_runs]: first constraint | count << 12 | type << 24
   uint32_t num_runs;
+  // One iteration of the colour sweep for one lane per environment, as groups: a hinge's
+  // point, axis and (when it acts) angle-limit constraints on one body pair, solved
+  // together with the two bodies' poses kept in registers, or a single constraint.
+  // k0 | k1 << 8 | k2 << 16 | kind << 24; kind 0: constraint k0 alone, 1: point k0 then
+  // axis k1, 2: point k0, axis k1, limit k2.  The groups are a dependency-respecting order
+  // of the sweep (pack_fast_model).
+  uint32_t o_groups;
+  uint32_t num_groups;
 };
 
 // Fills *out and the hot image *hot (to be uploaded and linked through out->hot); false

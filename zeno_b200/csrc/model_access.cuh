@@ -46,6 +46,7 @@ struct ModelS {
   __device__ __forceinline__ uint32_t ggpair(uint32_t ga, uint32_t gb) const { return h[f.o_ggpair + ga * f.G + gb]; }
   __device__ __forceinline__ float4 gforce(uint32_t b) const { return at<float4>(f.o_gforce, b); }
   __device__ __forceinline__ uint32_t run(uint32_t r) const { return at<uint32_t>(f.o_runs, r); }
+  __device__ __forceinline__ uint32_t group(uint32_t g) const { return at<uint32_t>(f.o_groups, g); }
 };
 
 struct ModelG {

@@ -174,6 +174,23 @@ __device__ __forceinline__ void solve_typed(const M& m, const ConstraintV& c, S&
   s.quat(c.b) = qb;
 }
 
+// A hinge's constraints on one body pair -- point (c0), axis (c1) and, when `limit`, angle
+// limit (c2) -- in that order, with the two poses kept in registers between them.
+template <class M, class S>
+__device__ __forceinline__ void solve_hinge(const M& m, const ConstraintV& c0, const ConstraintV& c1,
+                                            const ConstraintV& c2, bool limit, S& s) {
+  const float4 mia = m.imi(c0.a), mib = m.imi(c0.b);
+  if (mia.x + mib.x < 1e-8f) return;
+  float4 pa = s.pos(c0.a), qa = s.quat(c0.a), pb = s.pos(c0.b), qb = s.quat(c0.b);
+  cons_math<2>(m, c0, mia, mib, pa, qa, pb, qb);
+  cons_math<3>(m, c1, mia, mib, pa, qa, pb, qb);
+  if (limit) cons_math<4>(m, c2, mia, mib, pa, qa, pb, qb);
+  s.pos(c0.a) = pa;
+  s.quat(c0.a) = qa;
+  s.pos(c0.b) = pb;
+  s.quat(c0.b) = qb;
+}
+
 // One constraint of any type, in place.
 template <class M, class S>
 __device__ __forceinline__ void solve_constraint(const M& m, const ConstraintV& c, S& s) {
