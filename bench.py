@@ -587,7 +587,9 @@ def run_stage_profile(args):
             acc[k] = acc.get(k, 0.0) + v / args.steps
     lanes, epb = w.get_launch()
     print(json.dumps({"stage_profile": args.scene, "envs": E, "steps": args.steps, "launch": [lanes, epb],
-                      "cycles_per_block_step": {k: round(v) for k, v in acc.items() if k != "ns_per_cycle"},
+                      "cycles_per_block_step": {k: round(v) for k, v in acc.items()
+                                                if k != "ns_per_cycle" and not k.startswith("max_")},
+                      "max_over_blocks": {k[4:]: round(v) for k, v in acc.items() if k.startswith("max_")},
                       "ns_per_cycle": acc.get("ns_per_cycle"), "profiling_data": w.get_profiling_data()}), flush=True)
     return 0
 

@@ -255,8 +255,10 @@ const void* zeno_world_model_table(ZenoWorldHandle world, const char* name, uint
  * kinematic bodies, 2 wrenches and integration, 3 broad phase, 4 sort, 5 narrow phase and
  * warm start, 6 contact schedule, 7 joint constraints, 8 contact solve, 9 velocity
  * update, 10 joint states and sensors, 11 contact write-back, 12 caches and task,
- * 13 block epilogue -- then the average block span in cycles, then nanoseconds per cycle.
- * Returns the number of values written (16 at most), 0 when no profile exists (profiling
+ * 13 block epilogue -- then the average block span in cycles, nanoseconds per cycle, the
+ * slowest block's span in cycles (the kernel's duration is the slowest block's), and the
+ * 14 stages' largest per-block cycles.  Returns the number of values written (31 at most),
+ * 0 when no profile exists (profiling
  * off, no synchronous step yet, or the world runs the general kernel), -1 for NULL. */
 int zeno_world_get_stage_cycles(ZenoWorldHandle world, double* out, uint32_t n);
 

@@ -32,6 +32,8 @@ def test_profiling_world_bit_identical_and_filled(name):
         assert prof[k] > 0, k
     assert prof["span_cycles"] >= 0.9 * sum(prof[k] for k in stages)
     assert 0.2 < prof["ns_per_cycle"] < 5.0
+    assert prof["max_span_cycles"] >= prof["span_cycles"]
+    assert all(prof["max_" + k] >= prof[k] for k in stages)
     d = w1.get_profiling_data()
     for k in ("integrate_ms", "collision_broad_ms", "collision_narrow_ms", "constraint_solve_ms", "total_step_ms"):
         assert d[k] > 0, k

@@ -511,15 +511,19 @@ class ZenoWorld:
 
     def get_stage_profile(self) -> Dict[str, float]:
         """Per-stage device cycles of the last synchronous step, averaged over the kernel's
-        blocks, plus the block span ("span_cycles") and "ns_per_cycle" (a world created with
-        enable_profiling=True on the compressed-state kernel; {} otherwise)."""
-        n = len(self.STAGES) + 2
+        blocks, plus the block span ("span_cycles"), "ns_per_cycle", the slowest block's
+        span ("max_span_cycles") and each stage's largest per-block cycles ("max_<stage>")
+        (a world created with enable_profiling=True on the compressed-state kernel; {}
+        otherwise)."""
+        k = len(self.STAGES)
+        n = 2 * k + 3
         out = ffi.new("double[]", n)
         got = _lib.zeno_world_get_stage_cycles(self._handle, out, n)
         if got < n:
             return {}
         d = {name: out[i] for i, name in enumerate(self.STAGES)}
-        d["span_cycles"], d["ns_per_cycle"] = out[n - 2], out[n - 1]
+        d["span_cycles"], d["ns_per_cycle"], d["max_span_cycles"] = out[k], out[k + 1], out[k + 2]
+        d.update({"max_" + name: out[k + 3 + i] for i, name in enumerate(self.STAGES)})
         return d
 
     def reset_profiling(self) -> None:

@@ -24,6 +24,22 @@ inline bool narrow_pair_supported(uint32_t mode, uint32_t ta, uint32_t tb) {
          (ta == 3 && tb == 1);
 }
 inline float4 f4(const float* v) { return make_float4(v[0], v[1], v[2], v[3]); }
+// +z rotated by q, evaluated exactly as the kernels' capsule_axis / rotate (physics.cuh,
+// devmath.cuh): the same products and fused multiply-adds in the same order.
+inline float4 capsule_axis_host(const float* q) {
+  const float v[3] = {0.0f, 0.0f, 1.0f};
+  auto cross = [](const float* a, const float* b, float* o) {
+    o[0] = std::fmaf(a[1], b[2], -(a[2] * b[1]));
+    o[1] = std::fmaf(a[2], b[0], -(a[0] * b[2]));
+    o[2] = std::fmaf(a[0], b[1], -(a[1] * b[0]));
+  };
+  float uv[3], uuv[3];
+  cross(q, v, uv);
+  cross(q, uv, uuv);
+  return make_float4(std::fmaf(2.0f, std::fmaf(q[3], uv[0], uuv[0]), v[0]),
+                     std::fmaf(2.0f, std::fmaf(q[3], uv[1], uuv[1]), v[1]),
+                     std::fmaf(2.0f, std::fmaf(q[3], uv[2], uuv[2]), v[2]), 0.0f);
+}
 }  // namespace
 
 bool pack_fast_model(const HostModel& h, uint32_t max_contacts, uint32_t narrow_mode, FModel* out,
@@ -94,21 +110,33 @@ bool pack_fast_model(const HostModel& h, uint32_t max_contacts, uint32_t narrow_
   std::sort(distinct.begin(), distinct.end());
   distinct.erase(std::unique(distinct.begin(), distinct.end()), distinct.end());
 
-  uint32_t H = 0;
+  // Hittable candidates are numbered with the capsule-plane pairs first (reference GPU
+  // narrow phase), which the kernel tests four at a time; the numbering is internal (slot
+  // words, pair tables, hit masks) and does not change results.
+  std::vector<uint32_t> hit_index(P, fm::kNoHit);
+  uint32_t H = 0, n_cp = 0;
+  for (int pass = 0; pass < 2; ++pass)
+    for (uint32_t p = 0; p < P; ++p) {
+      const DGeom &ga = h.geoms[h.pairs[p].ga], &gb = h.geoms[h.pairs[p].gb];
+      if (!narrow_pair_supported(narrow_mode, ga.type, gb.type)) continue;
+      const bool cp = narrow_mode == 0 && ((ga.type == 1 && gb.type == 3) || (ga.type == 3 && gb.type == 1));
+      if (cp != (pass == 0)) continue;
+      if (H >= fm::kH) return fail("more hittable candidates than the constant-bank model holds");
+      hit_index[p] = H++;
+      n_cp += cp ? 1u : 0u;
+    }
   for (uint32_t p = 0; p < P; ++p) {
     const DPair& pr = h.pairs[p];
     const DGeom &ga = h.geoms[pr.ga], &gb = h.geoms[pr.gb];
     const uint32_t rank = uint32_t(std::lower_bound(distinct.begin(), distinct.end(), keys[p]) - distinct.begin());
-    uint32_t hidx = fm::kNoHit;
-    if (narrow_pair_supported(narrow_mode, ga.type, gb.type)) {
-      if (H >= fm::kH) return fail("more hittable candidates than the constant-bank model holds");
-      hidx = H++;
+    const uint32_t hidx = hit_index[p];
+    if (hidx != fm::kNoHit) {
       m.h_pair[hidx] = p;
       m.h_info[hidx] = (ga.type & 0xFFu) | ((gb.type & 0xFFu) << 8) | (ga.body << 16) | (gb.body << 24);
       m.h_ga[hidx] = f4(ga.pos_size0);
       m.h_gb[hidx] = f4(gb.pos_size0);
       const DGeom& cap = ga.type == 1 ? ga : gb;
-      m.h_cq[hidx] = f4(cap.quat);
+      m.h_cax[hidx] = capsule_axis_host(cap.quat);
       m.h_hl[hidx] = cap.size12_fr_rest[0];
       m.h_sz[hidx] = make_float4(ga.size12_fr_rest[0], ga.size12_fr_rest[1], gb.size12_fr_rest[0], gb.size12_fr_rest[1]);
       const float fp = ga.size12_fr_rest[2] * gb.size12_fr_rest[2];  // one IEEE product, then sqrt
@@ -133,6 +161,7 @@ bool pack_fast_model(const HostModel& h, uint32_t max_contacts, uint32_t narrow_
     m.s_info[s] = (d.type & 0xFFu) | ((d.object & 0xFFu) << 8) | (d.offset << 16);
   }
   m.P = P, m.H = H, m.G = h.G;
+  m.n_capsule_plane = n_cp;
   m.narrow_mode = narrow_mode;
   {
     std::vector<uint8_t> seen(256, 0);
@@ -177,7 +206,7 @@ bool pack_fast_model(const HostModel& h, uint32_t max_contacts, uint32_t narrow_
   m.o_hinfo = section(4 * H), put(m.o_hinfo, m.h_info, 4 * H);
   m.o_hga = section(16 * H), put(m.o_hga, m.h_ga, 16 * H);
   m.o_hgb = section(16 * H), put(m.o_hgb, m.h_gb, 16 * H);
-  m.o_hcq = section(16 * H), put(m.o_hcq, m.h_cq, 16 * H);
+  m.o_hcax = section(16 * H), put(m.o_hcax, m.h_cax, 16 * H);
   m.o_hhl = section(4 * H), put(m.o_hhl, m.h_hl, 4 * H);
   m.o_hfr = section(4 * H), put(m.o_hfr, m.h_fr, 4 * H);
   m.o_hpair = section(4 * H), put(m.o_hpair, m.h_pair, 4 * H);

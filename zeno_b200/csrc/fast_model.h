@@ -46,7 +46,7 @@ struct FModel {
   uint32_t h_info[fm::kH];  // type a | type b << 8 | body a << 16 | body b << 24
   float4 h_ga[fm::kH];      // geom a offset xyz, size[0]
   float4 h_gb[fm::kH];      // geom b offset xyz, size[0]
-  float4 h_cq[fm::kH];      // local quaternion of the capsule (when one geom is a capsule)
+  float4 h_cax[fm::kH];     // capsule axis: +z rotated by the capsule's local quaternion (when one geom is a capsule)
   float h_hl[fm::kH];       // capsule half length (size[1])
   float4 h_sz[fm::kH];      // size[1], size[2] of geom a, size[1], size[2] of geom b
   float h_fr[fm::kH];       // combined friction sqrt(f_a * f_b)
@@ -60,6 +60,7 @@ struct FModel {
   // sensors
   uint32_t s_info[fm::kS];  // type | object << 8 | obs offset << 16
   uint32_t P, H, G;
+  uint32_t n_capsule_plane;  // hittables [0, n) are capsule-plane pairs (reference narrow phase)
   uint32_t narrow_mode;  // 0: reference GPU narrow phase; 1: its CPU detectCollision
   // 1 when no two hittable candidates share a sort key (body pair): the warm-start match
   // of a hittable then reads only its own previous point, so one narrow-phase pass can
@@ -71,7 +72,7 @@ struct FModel {
   const uint4* hot;  // device copy of the image
   uint32_t hot_bytes;
   uint32_t o_imi, o_com, o_body, o_jf, o_jaxis, o_jinfo, o_caa, o_cab, o_cat, o_clim, o_cinfo;
-  uint32_t o_pbody, o_pinfo, o_pmd2, o_gps, o_hinfo, o_hga, o_hgb, o_hcq, o_hhl, o_hfr, o_hpair, o_hsz;
+  uint32_t o_pbody, o_pinfo, o_pmd2, o_gps, o_hinfo, o_hga, o_hgb, o_hcax, o_hhl, o_hfr, o_hpair, o_hsz;
   uint32_t o_gbody, o_ggpair;  // geom -> body (u32[G]), (ga, gb) -> candidate (u8[G * G])
   uint32_t o_gforce;           // float4[B], filled by each block: gravity * mass (zero when massless)
   uint32_t o_runs;             // u32[num_runs]: first constraint | count << 12 | type << 24

@@ -175,7 +175,7 @@ __device__ __forceinline__ bool narrow_h(const ModelS& m, uint32_t h, EnvBodies&
   }
   const V3 pa = v3(S.pos(ba)) + v3(ga);
   const V3 pb = v3(S.pos(bb)) + v3(gb);
-  return narrow_core(hi & 0xFFu, (hi >> 8) & 0xFFu, pa, pb, ga.w, gb.w, m.hhl(h), m.hcq(h), point, normal, pen);
+  return narrow_core(hi & 0xFFu, (hi >> 8) & 0xFFu, pa, pb, ga.w, gb.w, m.hhl(h), v3(m.hcax(h)), point, normal, pen);
 }
 
 enum : uint32_t {
@@ -492,12 +492,11 @@ __device__ __forceinline__ void run_env(const StepArgs& a, const FModel& f, cons
     //      otherwise this pass only matches and a second one stores.
     const bool one_pass = m.f.hit_keys_unique != 0;
     uint64_t hit_now = 0;
-    for (uint32_t h = lane; h < H; h += L) {
-      V3 point, normal;
-      float pen;
-      if (!narrow_h(m, h, S, point, normal, pen)) {
+    // the warm-start match and the stores of hittable pair h, given its narrow-phase result
+    auto narrow_finish = [&](uint32_t h, bool hit, V3 point, V3 normal, float pen) {
+      if (!hit) {
         if (one_pass) reinterpret_cast<float*>(&pp[h * ne])[3] = -1.0f;
-        continue;
+        return;
       }
       const uint32_t rank = m.pinfo(m.hpair(h)) >> 24;
       float best = 0.04f;
@@ -552,6 +551,41 @@ __device__ __forceinline__ void run_env(const StepArgs& a, const FModel& f, cons
       } else {
         reinterpret_cast<float*>(&nt[h * ne])[3] = val;
       }
+    };
+    // Capsule-plane pairs (the first n_capsule_plane hittables; the reference GPU narrow
+    // phase only): four per lane and round, their tests first -- independent and
+    // branch-free, so the loads and arithmetic of the four overlap -- then each one's match
+    // and stores in turn (one copy of that code; the results move down the registers).
+    uint32_t hc = 0;
+    if (m.f.narrow_mode == 0) {
+      hc = m.f.n_capsule_plane;
+      for (uint32_t h0 = lane; h0 < hc; h0 += 4 * L) {
+        bool hit[4];
+        V3 pt[4], nm[4];
+        float pe[4];
+#pragma unroll
+        for (uint32_t u = 0; u < 4; ++u) {
+          const uint32_t h = h0 + u * L < hc ? h0 + u * L : h0;  // (clamped: a valid pair, result unused)
+          const uint32_t hi = m.hinfo(h);
+          const bool ca = (hi & 0xFFu) == 1u;  // the capsule is geom A
+          const float4 g = ca ? m.hga(h) : m.hgb(h);
+          const V3 cpos = v3(S.pos(ca ? (hi >> 16) & 0xFFu : hi >> 24)) + v3(g);
+          hit[u] = capsule_plane(cpos, g.w, m.hhl(h), v3(m.hcax(h)), ca, pt[u], nm[u], pe[u]);
+        }
+#pragma unroll 1
+        for (uint32_t u = 0; u < 4 && h0 + u * L < hc; ++u) {
+          narrow_finish(h0 + u * L, hit[0], pt[0], nm[0], pe[0]);
+          hit[0] = hit[1], pt[0] = pt[1], nm[0] = nm[1], pe[0] = pe[1];
+          hit[1] = hit[2], pt[1] = pt[2], nm[1] = nm[2], pe[1] = pe[2];
+          hit[2] = hit[3], pt[2] = pt[3], nm[2] = nm[3], pe[2] = pe[3];
+        }
+      }
+    }
+    for (uint32_t h = hc + lane; h < H; h += L) {
+      V3 point, normal;
+      float pen;
+      const bool hit = narrow_h(m, h, S, point, normal, pen);
+      narrow_finish(h, hit, point, normal, pen);
     }
     G.sync();
     for (uint32_t h = lane; h < H && !one_pass; h += L) {
@@ -1426,10 +1460,17 @@ __global__ void __launch_bounds__(32 * L, 1) fast_step_kernel(const __grid_const
       clk.mark(kStEpilogue);
       long long ns1;
       asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(ns1));
-      for (uint32_t k = 0; k < kStageCount; ++k) atomicAdd(a.stage_clk + k, clk.acc[k]);
-      atomicAdd(a.stage_clk + kStageCount, static_cast<unsigned long long>(clk.last - clk0));
-      atomicAdd(a.stage_clk + kStageCount + 1, static_cast<unsigned long long>(ns1 - ns0));
+      for (uint32_t k = 0; k < kStageCount; ++k) {
+        atomicAdd(a.stage_clk + k, clk.acc[k]);
+        atomicMax(a.stage_clk + kStageMax + k, clk.acc[k]);
+      }
+      const auto span = static_cast<unsigned long long>(clk.last - clk0);
+      const auto span_ns = static_cast<unsigned long long>(ns1 - ns0);
+      atomicAdd(a.stage_clk + kStageCount, span);
+      atomicAdd(a.stage_clk + kStageCount + 1, span_ns);
       atomicAdd(a.stage_clk + kStageCount + 2, 1ull);
+      atomicMax(a.stage_clk + kStageCount + 3, span);
+      atomicMax(a.stage_clk + kStageCount + 4, span_ns);
     }
   }
 }

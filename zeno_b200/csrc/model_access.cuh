@@ -37,7 +37,7 @@ struct ModelS {
   __device__ __forceinline__ uint32_t hinfo(uint32_t x) const { return at<uint32_t>(f.o_hinfo, x); }
   __device__ __forceinline__ float4 hga(uint32_t x) const { return at<float4>(f.o_hga, x); }
   __device__ __forceinline__ float4 hgb(uint32_t x) const { return at<float4>(f.o_hgb, x); }
-  __device__ __forceinline__ float4 hcq(uint32_t x) const { return at<float4>(f.o_hcq, x); }
+  __device__ __forceinline__ float4 hcax(uint32_t x) const { return at<float4>(f.o_hcax, x); }
   __device__ __forceinline__ float hhl(uint32_t x) const { return at<float>(f.o_hhl, x); }
   __device__ __forceinline__ float hfr(uint32_t x) const { return at<float>(f.o_hfr, x); }
   __device__ __forceinline__ uint32_t hpair(uint32_t x) const { return at<uint32_t>(f.o_hpair, x); }

@@ -275,8 +275,26 @@ __device__ __forceinline__ void solve_contact(const M& m, float4 cpp, float4 cnf
 // pa, pb: body position + unrotated geom offset; ra, rb: size[0]; hl, cq: half length
 // and local quaternion of the capsule when one of the two geoms is a capsule.
 // ------------------------------------------------------------------------------------
+// Axis of a capsule geom: +z rotated by the geom's local quaternion (all_shaders.metal:
+// 858-860 uses the geom quaternion, not the body's).
+__device__ __forceinline__ V3 capsule_axis(float4 cq) { return rotate(v3(0.0f, 0.0f, 1.0f), cq); }
+
+// Capsule-plane contact (the capsule's geom-frame axis, see capsule_axis): the deeper of
+// the two segment ends below the plane z = 0 (the plane position is not used).
+// capsule_a: the capsule is geom A (normal +z), else geom B (normal -z).
+__device__ __forceinline__ bool capsule_plane(V3 cpos, float cr, float hl, V3 axis, bool capsule_a, V3& point,
+                                              V3& normal, float& pen) {
+  const V3 p1 = msub(axis, hl, cpos), p2 = madd(axis, hl, cpos);
+  const float d1 = p1.z - cr, d2 = p2.z - cr;
+  point = d1 < d2 ? p1 : p2;
+  point.z = 0.0f;
+  pen = -fminf(d1, d2);
+  normal = capsule_a ? v3(0.0f, 0.0f, 1.0f) : v3(0.0f, 0.0f, -1.0f);
+  return d1 < 0.0f || d2 < 0.0f;
+}
+
 __device__ __forceinline__ bool narrow_core(uint32_t ta, uint32_t tb, V3 pa, V3 pb, float ra, float rb, float hl,
-                                            float4 cq, V3& point, V3& normal, float& pen) {
+                                            V3 caxis, V3& point, V3& normal, float& pen) {
   if (ta == 0 && tb == 0) {
     const V3 d = pb - pa;
     float dist;
@@ -300,18 +318,7 @@ __device__ __forceinline__ bool narrow_core(uint32_t ta, uint32_t tb, V3 pa, V3 
       return true;
     }
   } else if ((ta == 1 && tb == 3) || (ta == 3 && tb == 1)) {
-    const V3 cpos = ta == 1 ? pa : pb;
-    const float cr = ta == 1 ? ra : rb;
-    const V3 axis = rotate(v3(0.0f, 0.0f, 1.0f), cq);
-    const V3 p1 = msub(axis, hl, cpos), p2 = madd(axis, hl, cpos);
-    const float d1 = p1.z - cr, d2 = p2.z - cr;
-    if (d1 < 0.0f || d2 < 0.0f) {
-      point = d1 < d2 ? p1 : p2;
-      point.z = 0.0f;
-      pen = -fminf(d1, d2);
-      normal = ta == 1 ? v3(0.0f, 0.0f, 1.0f) : v3(0.0f, 0.0f, -1.0f);
-      return true;
-    }
+    return capsule_plane(ta == 1 ? pa : pb, ta == 1 ? ra : rb, hl, caxis, ta == 1, point, normal, pen);
   }
   return false;
 }

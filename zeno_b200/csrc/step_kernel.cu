@@ -186,8 +186,9 @@ __device__ __forceinline__ void narrow(Pk pk, const DGeom* geoms, const float4* 
   } else {
     const V3 pa = v3(pos[pk_a(pk)]) + v3(ga0), pb = v3(pos[pk_b(pk)]) + v3(gb0);
     const DGeom& cg = ta == 1 ? gA : gB;
-    hit = narrow_core(ta, tb, pa, pb, ga0.w, gb0.w, __ldg(&cg.size12_fr_rest[0]),
-                      __ldg(reinterpret_cast<const float4*>(cg.quat)), point, normal, pen);
+    const V3 caxis = (ta == 1 || tb == 1) ? capsule_axis(__ldg(reinterpret_cast<const float4*>(cg.quat)))
+                                          : v3(0.0f, 0.0f, 0.0f);
+    hit = narrow_core(ta, tb, pa, pb, ga0.w, gb0.w, __ldg(&cg.size12_fr_rest[0]), caxis, point, normal, pen);
   }
   if (hit) {
     const float fr = __fsqrt_rn(__ldg(&gA.size12_fr_rest[2]) * __ldg(&gB.size12_fr_rest[2]));

@@ -308,11 +308,13 @@ uint32_t World::stage_cycles(double* out, uint32_t n) const {
   if (!stage_valid_ || !h_stage_ || h_stage_[kStageCount + 2] == 0) return 0;
   const double blocks = double(h_stage_[kStageCount + 2]);
   const double span = double(h_stage_[kStageCount]);
-  const uint32_t total = kStageCount + 2;
+  const uint32_t total = 2 * kStageCount + 3;
   uint32_t k = 0;
   for (; k < n && k < kStageCount; ++k) out[k] = double(h_stage_[k]) / blocks;
   if (k < n) out[k++] = span / blocks;
   if (k < n) out[k++] = span > 0 ? double(h_stage_[kStageCount + 1]) / span : 0.0;
+  if (k < n) out[k++] = double(h_stage_[kStageCount + 3]);
+  for (uint32_t i = 0; k < n && i < kStageCount; ++i) out[k++] = double(h_stage_[kStageMax + i]);
   return k < total ? k : total;
 }
 

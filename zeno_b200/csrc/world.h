@@ -81,8 +81,9 @@ class World {
   }
   // Stage profile of the last synchronous step of a profiling world on the
   // environment-per-lane kernel: per-stage clock cycles averaged over the blocks
-  // (kStageCount values, Stage order), then the average block span in cycles and the
-  // nanoseconds per cycle.  Returns the values written, 0 when no profile exists.
+  // (kStageCount values, Stage order), then the average block span in cycles, the
+  // nanoseconds per cycle, the largest block span in cycles and the per-stage maxima over
+  // the blocks (kStageCount values).  Returns the values written, 0 when no profile exists.
   uint32_t stage_cycles(double* out, uint32_t n) const;
   // The contacts buffer pointer for the caller (zeno_world_get_contacts).  From then on
   // every step reads the contact records themselves, so that the caller's writes count.

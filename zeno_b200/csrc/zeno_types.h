@@ -161,7 +161,8 @@ struct StepArgs {
   float4* pose_scratch;      // environment-per-lane kernel: 2 * B * num_envs poses before integration
   // stage profile (environment-per-lane kernel, when profiling is enabled; null otherwise):
   // kStageCount per-stage clock64 sums over the blocks' first threads, then the sums of the
-  // blocks' clock64 and %globaltimer (ns) spans and the number of blocks
+  // blocks' clock64 and %globaltimer (ns) spans, the number of blocks, the largest block
+  // span in cycles and in ns, then kStageCount per-stage maxima over the blocks
   unsigned long long* stage_clk;
   // slot cache (environment-per-lane kernel; null when the contacts buffer has been handed
   // to the caller, whose writes the next step must then read): per environment the contact
@@ -191,6 +192,8 @@ enum Stage : uint32_t {
   kStEpilogue,         // deferred record writes, coalesced state stores
   kStageCount
 };
-constexpr uint32_t kStageSlots = kStageCount + 3;  // + clock span, ns span, blocks
+// sums, then clock span, ns span, blocks, largest clock span, largest ns span, then maxima
+constexpr uint32_t kStageMax = kStageCount + 5;
+constexpr uint32_t kStageSlots = kStageMax + kStageCount;
 
 }  // namespace zb
