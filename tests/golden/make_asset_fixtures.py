@@ -8,7 +8,7 @@ hopper, pusher, reacher, swimmer, walker) as model data under tests/golden/asset
 XML comments and rgba attributes removed (they do not reach the step), and records a
 10-step oracle rollout of each (4 envs, seeded actions) next to it as a golden fixture.
 
-    python tests/golden/make_asset_fixtures.py [reference checkout, default /root/reference]
+    python tests/golden/make_asset_fixtures.py <path of the reference checkout>
 """
 import re
 import sys
@@ -41,7 +41,9 @@ def rollout(xml: str):
 
 
 def main():
-    ref = Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit("usage: make_asset_fixtures.py <path of the reference checkout>")
+    ref = Path(sys.argv[1])
     out = HERE / "assets"
     out.mkdir(exist_ok=True)
     for name in ASSETS:

@@ -744,10 +744,14 @@ __device__ __forceinline__ bool gjk(const Shape& A, const Shape& B, Simplex& x) 
   }
   return false;
 }
-struct Face {
-  uint32_t idx;  // vertex indices i0 | i1 << 8 | i2 << 16
+// Two 16-byte words, so that the removal pass reads a face with two vector loads: the
+// outward normal and distance, then the face's first vertex (a copy of v[i0], which the
+// visibility test reads) and the vertex indices.
+struct alignas(16) Face {
   P3 n;
   float d;
+  P3 v0;
+  uint32_t idx;  // vertex indices i0 | i1 << 8 | i2 << 16
 };
 __device__ __forceinline__ uint32_t fidx(uint32_t i0, uint32_t i1, uint32_t i2) { return i0 | (i1 << 8) | (i2 << 16); }
 __device__ __forceinline__ P3 face_normal(P3 a, P3 b, P3 c) { return safe_normalize(cross(sub(b, a), sub(c, a))); }
@@ -793,23 +797,26 @@ static __device__ __noinline__ bool gjk_contact(const Shape& A, const Shape& B, 
   uint16_t edges[kEpaEdges];
   uint32_t nv = 4, nf = 0;
   for (int i = 0; i < 4; ++i) v[i] = x.s[i], va[i] = x.sa[i], vb[i] = x.sb[i];
+  // The closest face (the first position holding the smallest distance) is tracked as
+  // the polytope changes rather than searched for at the top of each iteration: a face
+  // the removal pass keeps stays at the position where the pass tested it, and positions
+  // are settled in increasing order (kept faces, then appended ones), so a strict-less
+  // scan in settling order picks the same face as a scan of the array.
+  uint32_t k = 0;
+  float cd = __int_as_float(0x7f800000);
   const uint8_t tf[4][3] = {{0, 1, 2}, {0, 3, 1}, {0, 2, 3}, {1, 3, 2}};
 #pragma unroll
   for (int t = 0; t < 4; ++t) {
     const uint32_t i0 = tf[t][0], i1 = tf[t][1], i2 = tf[t][2];
     const P3 n = face_normal(v[i0], v[i1], v[i2]);
     const float d = dot(n, v[i0]);
-    if (d < 0.0f) f[nf++] = Face{fidx(i0, i2, i1), neg(n), -d};
-    else f[nf++] = Face{fidx(i0, i1, i2), n, d};
+    if (d < 0.0f) f[nf] = Face{neg(n), -d, v[i0], fidx(i0, i2, i1)};
+    else f[nf] = Face{n, d, v[i0], fidx(i0, i1, i2)};
+    if (f[nf].d < cd) cd = f[nf].d, k = nf;
+    nf += 1;
   }
   bool done = false;
-  uint32_t k = 0;
-  float cd = 0.0f;
   for (int it = 0; it < kEpaIters; ++it) {
-    k = 0;
-    cd = __int_as_float(0x7f800000);
-    for (uint32_t i = 0; i < nf; ++i)
-      if (f[i].d < cd) cd = f[i].d, k = i;
     const P3 dir = f[k].n;
     const MinkPoint m = mink(A, B, dir);
     if (__fsub_rn(dot(m.p, dir), cd) < kEpaTol) {
@@ -820,15 +827,19 @@ static __device__ __noinline__ bool gjk_contact(const Shape& A, const Shape& B, 
     v[nv] = m.p, va[nv] = m.sa, vb[nv] = m.sb;
     nv += 1;
     uint32_t ne = 0;
+    k = 0;
+    cd = __int_as_float(0x7f800000);
     for (uint32_t i = 0; i < nf;) {
-      const uint32_t fi = f[i].idx;
-      if (dot(f[i].n, sub(m.p, v[fi & 0xFFu])) > 0.0f) {
+      const Face fc = f[i];
+      const uint32_t fi = fc.idx;
+      if (dot(fc.n, sub(m.p, fc.v0)) > 0.0f) {
         add_edge(edges, ne, fi & 0xFFu, (fi >> 8) & 0xFFu);
         add_edge(edges, ne, (fi >> 8) & 0xFFu, fi >> 16);
         add_edge(edges, ne, fi >> 16, fi & 0xFFu);
         f[i] = f[nf - 1];
         nf -= 1;
       } else {
+        if (fc.d < cd) cd = fc.d, k = i;  // kept: position i is final
         i += 1;
       }
     }
@@ -837,18 +848,15 @@ static __device__ __noinline__ bool gjk_contact(const Shape& A, const Shape& B, 
       const uint32_t e0 = edges[e] & 0xFFu, e1 = edges[e] >> 8;
       const P3 n = face_normal(v[e0], v[e1], v[ni]);
       const float d = dot(n, v[e0]);
-      if (d < 0.0f) f[nf++] = Face{fidx(e1, e0, ni), neg(n), -d};
-      else f[nf++] = Face{fidx(e0, e1, ni), n, d};
+      if (d < 0.0f) f[nf] = Face{neg(n), -d, v[e1], fidx(e1, e0, ni)};
+      else f[nf] = Face{n, d, v[e0], fidx(e0, e1, ni)};
+      if (f[nf].d < cd) cd = f[nf].d, k = nf;
+      nf += 1;
     }
     if (nf == 0) break;
   }
-  if (!done) {  // fallback: the closest face of the current polytope
-    if (nf == 0) return false;
-    k = 0;
-    cd = __int_as_float(0x7f800000);
-    for (uint32_t i = 0; i < nf; ++i)
-      if (f[i].d < cd) cd = f[i].d, k = i;
-  }
+  // not converged: the closest face of the current polytope, as tracked
+  if (!done && nf == 0) return false;
   const uint32_t fi = f[k].idx, i0 = fi & 0xFFu, i1 = (fi >> 8) & 0xFFu, i2 = fi >> 16;
   float w0, w1, w2;
   barycentric(v[i0], v[i1], v[i2], w0, w1, w2);
