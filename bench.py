@@ -582,7 +582,7 @@ def run_stage_profile(args):
             continue
         prof = w.get_stage_profile()
         if not prof:
-            raise RuntimeError("no stage profile: the world does not run the compressed-state kernel")
+            raise RuntimeError("no stage profile returned")
         for k, v in prof.items():
             acc[k] = acc.get(k, 0.0) + v / args.steps
     lanes, epb = w.get_launch()

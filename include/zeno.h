@@ -246,8 +246,9 @@ int zeno_world_get_launch(ZenoWorldHandle world, int* lanes, int* envs_per_block
 const void* zeno_world_model_table(ZenoWorldHandle world, const char* name, uint64_t* nbytes);
 
 /* Stage profile (extends zeno_world_get_profiling, main.zig:666-683).  A world created
- * with ZenoConfig.enable_profiling runs an instrumented instantiation of the
- * compressed-state kernel whose blocks time each stage of the step with the SM clock.
+ * with ZenoConfig.enable_profiling runs an instrumented instantiation of its step kernel
+ * (compressed-state or general) whose blocks time each stage of the step with the SM clock
+ * (the general kernel: the block's first environment).
  * After each synchronous zeno_world_step, zeno_world_get_profiling's integrate / broad /
  * narrow / constraint fields hold those stages' device times (summed over the substeps,
  * averaged over the blocks, which run side by side), and this call writes up to n values:
@@ -258,8 +259,7 @@ const void* zeno_world_model_table(ZenoWorldHandle world, const char* name, uint
  * 13 block epilogue -- then the average block span in cycles, nanoseconds per cycle, the
  * slowest block's span in cycles (the kernel's duration is the slowest block's), and the
  * 14 stages' largest per-block cycles.  Returns the number of values written (31 at most),
- * 0 when no profile exists (profiling
- * off, no synchronous step yet, or the world runs the general kernel), -1 for NULL. */
+ * 0 when no profile exists (profiling off or no synchronous step yet), -1 for NULL. */
 int zeno_world_get_stage_cycles(ZenoWorldHandle world, double* out, uint32_t n);
 
 /* Message of the last failed zeno_world_create* on this thread ("" if none). */

@@ -513,8 +513,7 @@ class ZenoWorld:
         """Per-stage device cycles of the last synchronous step, averaged over the kernel's
         blocks, plus the block span ("span_cycles"), "ns_per_cycle", the slowest block's
         span ("max_span_cycles") and each stage's largest per-block cycles ("max_<stage>")
-        (a world created with enable_profiling=True on the compressed-state kernel; {}
-        otherwise)."""
+        (a world created with enable_profiling=True, either kernel; {} otherwise)."""
         k = len(self.STAGES)
         n = 2 * k + 3
         out = ffi.new("double[]", n)

@@ -38,7 +38,7 @@ CXX_FLAGS = ["-O2", "-std=c++17", "-fPIC", "-ffp-contract=off", "-fno-fast-math"
              f"-I{CUDA_HOME / 'include'}", f"-I{INCLUDE}"]
 CU_SOURCES = ["step_kernel.cu", "fast_step.cu", "noalloc.cu", "math_eval.cu"]
 CXX_SOURCES = ["mjcf.cpp", "model.cpp", "fast_model.cpp", "world.cpp", "capi.cpp"]
-HEADERS = ["zeno_types.h", "devmath.cuh", "physics.cuh", "model_access.cuh", "fast_model.h", "step_kernel.h", "scene.h", "model.h", "world.h"]
+HEADERS = ["zeno_types.h", "devmath.cuh", "physics.cuh", "model_access.cuh", "stage_clock.cuh", "fast_model.h", "step_kernel.h", "scene.h", "model.h", "world.h"]
 
 
 def _newer(target: Path, deps) -> bool:

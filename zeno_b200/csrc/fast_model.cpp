@@ -232,53 +232,16 @@ bool pack_fast_model(const HostModel& h, uint32_t max_contacts, uint32_t narrow_
   }
   m.num_runs = uint32_t(runs.size());
   m.o_runs = section(4 * m.num_runs), put(m.o_runs, runs.data(), 4 * runs.size());
-  // Hinge groups for one lane per environment.  Solving the colour-sorted constraints one
-  // by one is the reference's colour-by-colour sweep; two constraints with no dynamic body
-  // in common commute exactly (each reads and writes only its own two bodies; static
-  // bodies are never written), so moving a constraint forward past constraints that share
-  // no dynamic body with it leaves every pose bit-identical.  Walking the sweep, each
-  // unplaced point constraint (type 2) pulls forward the axis constraint (3) and then the
-  // angle limit (4) of the same body pair, when every unplaced constraint in between shares
-  // no dynamic body with them.
+  // Hinge groups (model.cpp hinge_groups) for one lane per environment, in sweep order:
+  // k0 | k1 << 8 | k2 << 16 | kind << 24 (unused members kNoGroup).
   {
-    const uint32_t K = uint32_t(h.constraints.size());
-    auto dyn = [&](uint32_t b) { return h.bodies[b].inv_mass_inertia[0] > 0.0f; };
-    auto type = [&](uint32_t k) { return h.constraints[k].type & 0xFFu; };
-    auto shares = [&](uint32_t i, uint32_t j) {
-      const DConstraint &a = h.constraints[i], &b = h.constraints[j];
-      return (dyn(a.body_a) && (a.body_a == b.body_a || a.body_a == b.body_b)) ||
-             (dyn(a.body_b) && (a.body_b == b.body_a || a.body_b == b.body_b));
-    };
-    std::vector<uint8_t> placed(K, 0);
     std::vector<uint32_t> groups;
-    auto pull = [&](uint32_t i, uint32_t want) -> uint32_t {  // next movable constraint of type want on i's pair
-      const DConstraint& c = h.constraints[i];
-      for (uint32_t j = i + 1; j < K; ++j) {
-        if (placed[j]) continue;
-        const DConstraint& d = h.constraints[j];
-        if (type(j) == want && d.body_a == c.body_a && d.body_b == c.body_b) {
-          for (uint32_t x = i + 1; x < j; ++x)
-            if (!placed[x] && shares(x, j)) return fm::kNoGroup;
-          return j;
-        }
-        if (shares(j, i)) return fm::kNoGroup;  // an earlier constraint on a body of the pair comes first
-      }
-      return fm::kNoGroup;
-    };
-    for (uint32_t i = 0; i < K; ++i) {
-      if (placed[i]) continue;
-      placed[i] = 1;
-      uint32_t w = i | (fm::kNoGroup << 8) | (fm::kNoGroup << 16);
-      if (type(i) == 2u) {
-        const uint32_t j = pull(i, 3u);
-        if (j != fm::kNoGroup) {
-          placed[j] = 1;
-          const uint32_t l = pull(j, 4u);
-          if (l != fm::kNoGroup) placed[l] = 1;
-          w = i | (j << 8) | (l << 16) | ((l != fm::kNoGroup ? 2u : 1u) << 24);
-        }
-      }
-      groups.push_back(w);
+    for (size_t g = 0; g + 3 < h.hinge_groups.size(); g += 4) {
+      const uint32_t* q = &h.hinge_groups[g];
+      if (q[0] >= fm::kNoGroup || q[1] >= fm::kNoGroup || q[2] >= fm::kNoGroup)
+        return fail("constraint index out of the group word's range");
+      const uint32_t k1 = q[3] >= 1 ? q[1] : fm::kNoGroup, k2 = q[3] == 2 ? q[2] : fm::kNoGroup;
+      groups.push_back(q[0] | (k1 << 8) | (k2 << 16) | (q[3] << 24));
     }
     m.num_groups = uint32_t(groups.size());
     m.o_groups = section(4 * m.num_groups), put(m.o_groups, groups.data(), 4 * groups.size());

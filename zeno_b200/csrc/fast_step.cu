@@ -35,6 +35,7 @@
 #include "fast_model.h"
 #include "model_access.cuh"
 #include "physics.cuh"
+#include "stage_clock.cuh"
 #include "step_kernel.h"
 #include "zeno_types.h"
 
@@ -190,26 +191,6 @@ enum : uint32_t {
   kWbPublish = 1u << 17,  // into the contacts buffer (else into the step_subset cache)
 };
 constexpr uint32_t kWbParts = 12;  // 16-byte record parts staged per thread
-
-// Stage profile (profiling worlds only): the block's first thread accumulates clock64
-// deltas per stage in shared memory; with C = false every mark compiles to nothing.
-template <bool C>
-struct StageClock {
-  __device__ __forceinline__ void mark(uint32_t) {}
-};
-template <>
-struct StageClock<true> {
-  unsigned long long* acc;  // shared, kStageCount entries
-  long long last;
-  bool on;                  // the block's first thread
-  __device__ __forceinline__ void mark(uint32_t k) {
-    if (on) {
-      const long long t = clock64();
-      acc[k] += static_cast<unsigned long long>(t - last);
-      last = t;
-    }
-  }
-};
 
 // Everything a group does for its environment between the cooperative load and store.
 // The block has already handed over the environments this kernel cannot represent.
@@ -1188,14 +1169,9 @@ __global__ void __launch_bounds__(32 * L, 1) fast_step_kernel(const __grid_const
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const uint32_t nt = blockDim.x, tid = threadIdx.x;
   StageClock<C> clk;
-  [[maybe_unused]] long long clk0 = 0, ns0 = 0;
   if constexpr (C) {
     __shared__ unsigned long long s_clk[kStageCount];
-    if (tid < kStageCount) s_clk[tid] = 0;
-    clk.acc = s_clk;
-    clk.on = tid == 0;
-    clk.last = clk0 = clock64();
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(ns0));
+    clk.start(s_clk, tid == 0);
     __syncthreads();
   }
   const uint32_t ne = nt / L;  // environments per block
@@ -1455,23 +1431,9 @@ __global__ void __launch_bounds__(32 * L, 1) fast_step_kernel(const __grid_const
     }
     for (uint32_t el = tid; el < nb; el += nt) a.slot_cache_ok[e0 + el] = (s_flags[el] & kSkipState) ? 0 : 1;
   }
-  if constexpr (C) {
-    if (tid == 0) {  // (the first thread's own stores are issued; the block's others may still drain)
-      clk.mark(kStEpilogue);
-      long long ns1;
-      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(ns1));
-      for (uint32_t k = 0; k < kStageCount; ++k) {
-        atomicAdd(a.stage_clk + k, clk.acc[k]);
-        atomicMax(a.stage_clk + kStageMax + k, clk.acc[k]);
-      }
-      const auto span = static_cast<unsigned long long>(clk.last - clk0);
-      const auto span_ns = static_cast<unsigned long long>(ns1 - ns0);
-      atomicAdd(a.stage_clk + kStageCount, span);
-      atomicAdd(a.stage_clk + kStageCount + 1, span_ns);
-      atomicAdd(a.stage_clk + kStageCount + 2, 1ull);
-      atomicMax(a.stage_clk + kStageCount + 3, span);
-      atomicMax(a.stage_clk + kStageCount + 4, span_ns);
-    }
+  if constexpr (C) {  // (the first thread's own stores are issued; the block's others may still drain)
+    clk.mark(kStEpilogue);
+    clk.publish(a.stage_clk);
   }
 }
 

@@ -182,6 +182,88 @@ void blob(std::vector<uint8_t>& dst, const std::vector<T>& v) {
 
 }  // namespace
 
+// Hinge groups.  Solving the colour-sorted constraints one by one is the reference's
+// colour-by-colour sweep; two constraints with no dynamic body in common commute exactly
+// (each reads and writes only its own two bodies; static bodies are never written), so
+// moving a constraint forward past constraints that share no dynamic body with it leaves
+// every pose bit-identical.  Walking the sweep, each unplaced point constraint (type 2)
+// pulls forward the axis constraint (3) and then the angle limit (4) of the same body
+// pair, when every unplaced constraint in between shares no dynamic body with them; a
+// group is then solved with the pair's poses held in registers.  Levels (general kernel):
+// a group's level is one more than the highest level of the earlier groups it shares a
+// dynamic body with, so the groups of a level touch disjoint dynamic bodies and can be
+// solved side by side, and every body sees its groups in sweep order.
+static void hinge_groups(HostModel* hp) {
+  HostModel& h = *hp;
+  const uint32_t K = uint32_t(h.constraints.size());
+  auto dyn = [&](uint32_t b) { return h.bodies[b].inv_mass_inertia[0] > 0.0f; };
+  auto type = [&](uint32_t k) { return h.constraints[k].type & 0xFFu; };
+  auto shares = [&](uint32_t i, uint32_t j) {
+    const DConstraint &a = h.constraints[i], &b = h.constraints[j];
+    return (dyn(a.body_a) && (a.body_a == b.body_a || a.body_a == b.body_b)) ||
+           (dyn(a.body_b) && (a.body_b == b.body_a || a.body_b == b.body_b));
+  };
+  constexpr uint32_t kNone = 0xFFFFFFFFu;
+  std::vector<uint8_t> placed(K, 0);
+  auto pull = [&](uint32_t i, uint32_t want) -> uint32_t {  // next movable constraint of type want on i's pair
+    const DConstraint& c = h.constraints[i];
+    for (uint32_t j = i + 1; j < K; ++j) {
+      if (placed[j]) continue;
+      const DConstraint& d = h.constraints[j];
+      if (type(j) == want && d.body_a == c.body_a && d.body_b == c.body_b) {
+        for (uint32_t x = i + 1; x < j; ++x)
+          if (!placed[x] && shares(x, j)) return kNone;
+        return j;
+      }
+      if (shares(j, i)) return kNone;  // an earlier constraint on a body of the pair comes first
+    }
+    return kNone;
+  };
+  h.hinge_groups.clear();
+  for (uint32_t i = 0; i < K; ++i) {
+    if (placed[i]) continue;
+    placed[i] = 1;
+    uint32_t k1 = i, k2 = i, kind = 0;
+    if (type(i) == 2u) {
+      const uint32_t j = pull(i, 3u);
+      if (j != kNone) {
+        placed[j] = 1;
+        const uint32_t l = pull(j, 4u);
+        if (l != kNone) placed[l] = 1;
+        k1 = j, k2 = l != kNone ? l : i, kind = l != kNone ? 2u : 1u;
+      }
+    }
+    h.hinge_groups.insert(h.hinge_groups.end(), {i, k1, k2, kind});
+  }
+  // levels (constraint indices packed in 16 bits)
+  h.jgroup_words.clear();
+  h.jgroup_levels.clear();
+  if (K > 0xFFFFu) return;
+  const uint32_t NG = uint32_t(h.hinge_groups.size() / 4);
+  std::vector<uint32_t> level(NG, 0), body_level(h.B, 0);  // body_level: highest level + 1 so far
+  uint32_t num_levels = 0;
+  for (uint32_t g = 0; g < NG; ++g) {
+    const DConstraint& c = h.constraints[h.hinge_groups[4 * g]];
+    uint32_t lv = 0;
+    if (dyn(c.body_a)) lv = std::max(lv, body_level[c.body_a]);
+    if (dyn(c.body_b)) lv = std::max(lv, body_level[c.body_b]);
+    level[g] = lv;
+    if (dyn(c.body_a)) body_level[c.body_a] = lv + 1;
+    if (dyn(c.body_b)) body_level[c.body_b] = lv + 1;
+    num_levels = std::max(num_levels, lv + 1);
+  }
+  h.jgroup_levels.assign(1, 0u);
+  for (uint32_t lv = 0; lv < num_levels; ++lv) {
+    for (uint32_t g = 0; g < NG; ++g) {
+      if (level[g] != lv) continue;
+      const uint32_t* q = &h.hinge_groups[4 * g];
+      h.jgroup_words.push_back(q[0] | (q[1] << 16));
+      h.jgroup_words.push_back(q[2] | (q[3] << 16));
+    }
+    h.jgroup_levels.push_back(uint32_t(h.jgroup_words.size() / 2));
+  }
+}
+
 bool build_model(const Scene& sc, HostModel* m, std::string* err) {
   HostModel h;
   h.corrected = sc.corrected;
@@ -323,6 +405,7 @@ bool build_model(const Scene& sc, HostModel* m, std::string* err) {
   }
   h.K = uint32_t(h.constraints.size());
   blob(h.ref_constraints, tc);
+  hinge_groups(&h);
 
   // initial-state template (world.zig:663-691, env 0; state.zig:358-388)
   h.init_state.assign(16 * h.B + 2 * h.J, 0.0f);

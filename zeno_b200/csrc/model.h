@@ -31,6 +31,14 @@ struct HostModel {
   std::vector<DConstraint> constraints;
   std::vector<uint32_t> kcolor_ranges;
   std::vector<uint32_t> color_ranges;
+  // Hinge groups (see hinge_groups in model.cpp): per group k0, k1, k2, kind (0 a single
+  // constraint k0; 1 point k0 + axis k1; 2 point + axis + angle limit k2) in sweep order,
+  // and for the general kernel the same groups by dependency level: jgroup_words holds
+  // (k0 | k1 << 16, k2 | kind << 16) per group, level by level; jgroup_levels the start of
+  // each level and the end (num_levels + 1 entries).
+  std::vector<uint32_t> hinge_groups;
+  std::vector<uint32_t> jgroup_words;
+  std::vector<uint32_t> jgroup_levels;
   std::vector<uint32_t> subtree;
   std::vector<float> init_state;         // B*4 pos, B*4 quat, B*4 vel, B*4 angvel, J jpos, J jvel
   bool actuators_unique = true;

@@ -30,6 +30,7 @@
 #include "devmath.cuh"
 #include "model_access.cuh"
 #include "physics.cuh"
+#include "stage_clock.cuh"
 #include "step_kernel.h"
 #include "zeno_types.h"
 
@@ -157,7 +158,7 @@ struct ArrBodies {
 // Narrow phase for one slot (narrow_phase, all_shaders.metal:751-894; mode 1: the
 // reference's CPU detectCollision, src/collision/narrow_phase.zig:28-136; mode 2: as 1,
 // with GJK + EPA, src/collision/gjk.zig, for box-capsule pairs)
-__device__ __forceinline__ void narrow(Pk pk, const DGeom* geoms, const float4* pos, const float4* quat,
+__device__ __forceinline__ bool narrow(Pk pk, const DGeom* geoms, const float4* pos, const float4* quat,
                                        uint32_t mode, uint32_t corrected, float restitution, float4& cpp, float4& cnf,
                                        float4& cim) {
   const DGeom& gA = geoms[pk_ga(pk)];
@@ -198,6 +199,7 @@ __device__ __forceinline__ void narrow(Pk pk, const DGeom* geoms, const float4* 
   } else {
     cpp.w = -1.0f;
   }
+  return hit;
 }
 
 // ------------------------------------------------------------------------------------
@@ -398,9 +400,9 @@ __device__ __noinline__ uint32_t grid_broad_phase(GridIn in, uint32_t count, uin
 // ------------------------------------------------------------------------------------
 // One environment, stepped by the L lanes of group g (syncs are group-local).
 // ------------------------------------------------------------------------------------
-template <int L>
+template <int L, bool C>
 __device__ __forceinline__ void step_env(const StepArgs& a, uint32_t e, unsigned char* smem_raw, uint32_t g,
-                                         uint32_t l) {
+                                         uint32_t l, StageClock<C>& clk) {
   const unsigned gmask = L == 32 ? 0xFFFFFFFFu : (((1u << L) - 1u) << ((threadIdx.x & 31u) & ~(L - 1u)));
   const uint32_t gshift = (threadIdx.x & 31u) & ~(L - 1u);
   const ModelG mg{a.bodies, a.constraints};
@@ -482,6 +484,14 @@ __device__ __forceinline__ void step_env(const StepArgs& a, uint32_t e, unsigned
   __syncwarp(gmask);
 
   const float dt = a.dt, inv_dt = a.inv_dt;
+  // bit b: body b is dynamic (inverse mass above the reference's 1e-8), for the contact
+  // schedule's walk; models of more than 64 bodies read the body table there instead
+  uint64_t dyn = 0;
+  if (B <= 64u) {
+    for (uint32_t b = l; b < B; b += L)
+      if (__ldg(&a.bodies[b].inv_mass_inertia[0]) > 1e-8f) dyn |= 1ull << b;
+    for (uint32_t off = 1; off < uint32_t(L); off <<= 1) dyn |= __shfl_xor_sync(gmask, dyn, off);
+  }
   const V3 grav{a.gravity[0], a.gravity[1], a.gravity[2]};
   const float* act = a.actions + size_t(e) * A;
 
@@ -490,6 +500,7 @@ __device__ __forceinline__ void step_env(const StepArgs& a, uint32_t e, unsigned
   uint32_t n_hi = 0;
   // the last contact schedule: its level count, valid-slot count and list length
   uint32_t sched_nlev = 0, sched_nv = 0, sched_n = 0xFFFFFFFFu;
+  clk.mark(kStPrologue);
   for (uint32_t s = 0; s < a.substeps; ++s) {
     // ---- prev snapshot = final slot list of the previous substep ----
     const uint32_t n_prev = prev_count < M ? prev_count : M;
@@ -509,6 +520,7 @@ __device__ __forceinline__ void step_env(const StepArgs& a, uint32_t e, unsigned
       float tq = clampf(act[k], __ldg(&ad.ctrl_min), __ldg(&ad.ctrl_max)) * __ldg(&ad.gear);
       jt[__ldg(&ad.joint)] = clampf(tq, __ldg(&ad.force_min), __ldg(&ad.force_max));
     }
+    clk.mark(kStActions);
     // ---- gravity wrench, kinematic bodies ----
     for (uint32_t b = l; b < B; b += L) {
       const DBody& bd = a.bodies[b];
@@ -563,6 +575,7 @@ __device__ __forceinline__ void step_env(const StepArgs& a, uint32_t e, unsigned
       quat[b] = qnormalize(qmadd(qmul_v((w * dt) * 0.5f, q), 1.0f, q));
     }
     __syncwarp(gmask);
+    clk.mark(kStIntegrate);
     // ---- broad phase: candidate pairs in emission order, compacted by ballot ----
     // (corrected semantics rebuild the list every substep; the reference's counter only
     // grows, so its list freezes with duplicates once M candidates were emitted)
@@ -654,8 +667,20 @@ __device__ __forceinline__ void step_env(const StepArgs& a, uint32_t e, unsigned
     const uint32_t n_old = count0 < M ? count0 : M;
     n_hi = n > n_hi ? n : n_hi;
     __syncwarp(gmask);
+    clk.mark(kStBroad);
     // ---- stable sort by body-pair key (only when slots were appended) ----
+    // A list already in key order is left as it is by the stable sort; the check is
+    // cheap against the sort, and lists usually pass it (the stored slots are sorted,
+    // emission order follows the key order when geoms are numbered in body order, and a
+    // rebuilt list is emitted whole).
+    bool in_order = true;
     if (n > n_old) {
+      for (uint32_t i = 1u + l; i < n; i += L)
+        in_order = in_order && pk_key(cpk[ord[i - 1]]) <= pk_key(cpk[ord[i]]);
+      const uint32_t lm = L == 32 ? 0xFFFFFFFFu : ((1u << L) - 1u);
+      in_order = ((__ballot_sync(gmask, !in_order) >> gshift) & lm) == 0u;
+    }
+    if (n > n_old && !in_order) {
       for (uint32_t i = l; i < n; i += L) {
         const uint32_t ki = pk_key(cpk[ord[i]]);
         uint32_t rank = 0;
@@ -669,10 +694,56 @@ __device__ __forceinline__ void step_env(const StepArgs& a, uint32_t e, unsigned
       for (uint32_t i = l; i < n; i += L) ord[i] = sched[i];
       __syncwarp(gmask);
     }
+    clk.mark(kStSort);
     // ---- narrow phase ----
-    for (uint32_t i = l; i < n; i += L) {
-      const uint32_t st = ord[i];
-      narrow(cpk[st], a.geoms, pos, quat, a.narrow_mode, a.corrected, a.restitution, cpp[st], cnf[st], cim[st]);
+    // A slot's result depends only on its pair and the poses, and a list the reference's
+    // ever-growing counter filled holds the same pair several times (appended in several
+    // substeps), so each pair is computed once, by the first slot holding it (a "holder";
+    // slots in key order keep copies of a pair in one run), and its copies take the
+    // holder's result: the three parts on a hit, the miss marker otherwise.  Scratch
+    // (free between the sort and the contact schedule): slev[i] = position of slot i's
+    // holder, for a holder itself i on a hit and 0xFFFF on a miss; lcur = the holders'
+    // positions, spread over the lanes.
+    {
+      const uint32_t lm = L == 32 ? 0xFFFFFFFFu : ((1u << L) - 1u);
+      uint32_t nlead = 0;
+      for (uint32_t c0 = 0; c0 < n; c0 += L) {
+        const uint32_t i = c0 + l;
+        uint32_t first = i;
+        if (i < n) {
+          const Pk pk = cpk[ord[i]];
+          const uint32_t key = pk_key(pk);
+          for (uint32_t j = i; j > 0 && pk_key(cpk[ord[j - 1]]) == key;) {
+            --j;
+            const Pk q = cpk[ord[j]];
+            if (q.x == pk.x && q.y == pk.y) first = j;
+          }
+          slev[i] = uint16_t(first);
+        }
+        const bool lead = i < n && first == i;
+        const uint32_t bal = (__ballot_sync(gmask, lead) >> gshift) & lm;
+        if (lead) lcur[nlead + __popc(bal & ((1u << l) - 1u))] = uint16_t(i);
+        nlead += __popc(bal);
+      }
+      __syncwarp(gmask);
+      for (uint32_t k = l; k < nlead; k += L) {
+        const uint32_t i = lcur[k], st = ord[i];
+        if (!narrow(cpk[st], a.geoms, pos, quat, a.narrow_mode, a.corrected, a.restitution, cpp[st], cnf[st], cim[st]))
+          slev[i] = 0xFFFFu;
+      }
+      __syncwarp(gmask);
+      for (uint32_t i = l; i < n; i += L) {
+        const uint32_t f = slev[i];
+        if (f == i || f == 0xFFFFu) continue;  // a holder
+        const uint32_t st = ord[i], sf = ord[f];
+        if (slev[f] == f) {
+          cpp[st] = cpp[sf];
+          cnf[st] = cnf[sf];
+          cim[st] = cim[sf];
+        } else {
+          cpp[st].w = -1.0f;
+        }
+      }
     }
     __syncwarp(gmask);
     // ---- warm start: best previous contact of the same pair within 0.2 ----
@@ -707,14 +778,38 @@ __device__ __forceinline__ void step_env(const StepArgs& a, uint32_t e, unsigned
       }
     }
     __syncwarp(gmask);
-    // ---- XPBD joints: colours in order, constraints of a colour in parallel ----
-    for (uint32_t it = 0; it < a.iterations; ++it) {
-      for (uint32_t col = 0; col < a.num_colors; ++col) {
-        const uint32_t off = __ldg(&a.color_ranges[2 * col]), cnt = __ldg(&a.color_ranges[2 * col + 1]);
-        for (uint32_t k = l; k < cnt; k += L) solve_constraint(mg, mg.constraint(off + k), bodies);
-        __syncwarp(gmask);
+    clk.mark(kStNarrow);
+    // ---- XPBD joints: the colour sweep as hinge groups by dependency level (a level's
+    //      groups touch disjoint dynamic bodies and run side by side; each body sees its
+    //      constraints in sweep order), or colour by colour ----
+    if (a.num_jlevels > 0) {
+      for (uint32_t it = 0; it < a.iterations; ++it) {
+        for (uint32_t lv = 0; lv < a.num_jlevels; ++lv) {
+          const uint32_t g0 = __ldg(&a.jgroup_levels[lv]), g1 = __ldg(&a.jgroup_levels[lv + 1]);
+          for (uint32_t g = g0 + l; g < g1; g += L) {
+            const uint2 gw = __ldg(&a.jgroups[g]);
+            const uint32_t kind = gw.y >> 16;
+            const ConstraintV c0 = mg.constraint(gw.x & 0xFFFFu);
+            if (kind == 0u) {
+              solve_constraint(mg, c0, bodies);
+            } else {
+              const ConstraintV c1 = mg.constraint(gw.x >> 16);
+              solve_hinge(mg, c0, c1, kind == 2u ? mg.constraint(gw.y & 0xFFFFu) : c0, kind == 2u, bodies);
+            }
+          }
+          __syncwarp(gmask);
+        }
+      }
+    } else {
+      for (uint32_t it = 0; it < a.iterations; ++it) {
+        for (uint32_t col = 0; col < a.num_colors; ++col) {
+          const uint32_t off = __ldg(&a.color_ranges[2 * col]), cnt = __ldg(&a.color_ranges[2 * col + 1]);
+          for (uint32_t k = l; k < cnt; k += L) solve_constraint(mg, mg.constraint(off + k), bodies);
+          __syncwarp(gmask);
+        }
       }
     }
+    clk.mark(kStJoints);
     // ---- contacts: level schedule equivalent to solving slots in slot order ----
     // level(i) = 1 + max level of earlier valid slots sharing a dynamic body; slots of
     // one level touch disjoint dynamic bodies, and every conflicting pair keeps its slot
@@ -751,8 +846,8 @@ __device__ __forceinline__ void step_env(const StepArgs& a, uint32_t e, unsigned
         const uint32_t st = ord[i];
         if (cpp[st].w < 0.0f) continue;
         const uint32_t ba = pk_a(cpk[st]), bb = pk_b(cpk[st]);
-        const bool da = __ldg(&a.bodies[ba].inv_mass_inertia[0]) > 1e-8f;
-        const bool db = __ldg(&a.bodies[bb].inv_mass_inertia[0]) > 1e-8f;
+        const bool da = B <= 64u ? ((dyn >> ba) & 1ull) != 0 : __ldg(&a.bodies[ba].inv_mass_inertia[0]) > 1e-8f;
+        const bool db = B <= 64u ? ((dyn >> bb) & 1ull) != 0 : __ldg(&a.bodies[bb].inv_mass_inertia[0]) > 1e-8f;
         uint32_t lv = 0;
         if (da && blev[ba] > lv) lv = blev[ba];
         if (db && blev[bb] > lv) lv = blev[bb];
@@ -773,6 +868,7 @@ __device__ __forceinline__ void step_env(const StepArgs& a, uint32_t e, unsigned
     nv = __shfl_sync(gmask, nv, gshift);
     sched_nlev = nlev, sched_nv = nv, sched_n = n;
     __syncwarp(gmask);
+    clk.mark(kStSchedule);
     for (uint32_t it = 0; it < a.iterations; ++it) {
       for (uint32_t lv = 0; lv < nlev; ++lv) {
         const uint32_t k0 = lvl[lv], k1 = lvl[lv + 1];
@@ -786,6 +882,7 @@ __device__ __forceinline__ void step_env(const StepArgs& a, uint32_t e, unsigned
         __syncwarp(gmask);
       }
     }
+    clk.mark(kStContacts);
     // ---- velocities from the position change ----
     for (uint32_t b = l; b < B; b += L) {
       if (__ldg(&a.bodies[b].inv_mass_inertia[0]) < 1e-8f) continue;
@@ -796,6 +893,7 @@ __device__ __forceinline__ void step_env(const StepArgs& a, uint32_t e, unsigned
     }
     prev_count = count;
     __syncwarp(gmask);
+    clk.mark(kStVelocities);
   }
 
   // ---- joint states and sensors from the final substep ----
@@ -874,6 +972,7 @@ __device__ __forceinline__ void step_env(const StepArgs& a, uint32_t e, unsigned
     return;
   }
 
+  clk.mark(kStJointState);
   // ---- accelerations from the whole-step velocity change (world.zig:736-746) ----
   float4* gacc = reinterpret_cast<float4*>(a.acc) + eb;
   for (uint32_t b = l; b < B; b += L) {
@@ -891,6 +990,7 @@ __device__ __forceinline__ void step_env(const StepArgs& a, uint32_t e, unsigned
     reinterpret_cast<uint4*>(dst)[2] = make_uint4(pk_a(k), pk_b(k), pk_ga(k), pk_gb(k));
     dst[3] = cim[st];
   }
+  clk.mark(kStWriteBack);
   // ---- episode task extension ----
   uint32_t count_out = count;
   if (a.task.enabled) {
@@ -918,6 +1018,7 @@ __device__ __forceinline__ void step_env(const StepArgs& a, uint32_t e, unsigned
     __syncwarp(gmask);
     count_out = __shfl_sync(gmask, count_out, gshift);
   }
+  clk.mark(kStTask);
   // ---- body and joint state back to HBM ----
   float4* wpos = reinterpret_cast<float4*>(a.pos) + eb;
   float4* wquat = reinterpret_cast<float4*>(a.quat) + eb;
@@ -944,6 +1045,7 @@ __device__ __forceinline__ void step_env(const StepArgs& a, uint32_t e, unsigned
       a.prev_sep[e] = 0;
     }
   }
+  clk.mark(kStEpilogue);
 }
 
 // ------------------------------------------------------------------------------------
@@ -952,15 +1054,22 @@ __device__ __forceinline__ void step_env(const StepArgs& a, uint32_t e, unsigned
 // ones the environment-per-lane kernel handed over); the last block to finish clears
 // the count for the next step.
 // ------------------------------------------------------------------------------------
-template <int L>
+template <int L, bool C>
 __global__ void __launch_bounds__(256, 1) step_kernel(StepArgs a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const uint32_t NE = blockDim.x / L;
   const uint32_t g = threadIdx.x / L;
   const uint32_t l = threadIdx.x % L;
+  StageClock<C> clk;
   if (a.env_list == nullptr) {
+    if constexpr (C) {  // the block's first environment is timed (its lane 0)
+      __shared__ unsigned long long s_clk[kStageCount];
+      clk.start(s_clk, threadIdx.x == 0);
+      __syncthreads();
+    }
     const uint32_t e = blockIdx.x * NE + g;
-    if (e < a.num_envs) step_env<L>(a, e, smem_raw, g, l);  // whole groups retire together
+    if (e < a.num_envs) step_env<L, C>(a, e, smem_raw, g, l, clk);  // whole groups retire together
+    if constexpr (C) clk.publish(a.stage_clk);
     return;
   }
   const uint32_t cnt = *a.env_count;
@@ -968,7 +1077,7 @@ __global__ void __launch_bounds__(256, 1) step_kernel(StepArgs a) {
   // count is written only before this launch and cleared after every block has read it,
   // so all blocks see the same value.
   if (cnt == 0) return;
-  for (uint32_t i = blockIdx.x * NE + g; i < cnt; i += gridDim.x * NE) step_env<L>(a, a.env_list[i], smem_raw, g, l);
+  for (uint32_t i = blockIdx.x * NE + g; i < cnt; i += gridDim.x * NE) step_env<L, C>(a, a.env_list[i], smem_raw, g, l, clk);
   __syncthreads();
   if (threadIdx.x == 0) {
     __threadfence();
@@ -992,12 +1101,20 @@ cudaError_t launch_step(const StepArgs& args, int lanes, int envs_per_block, cud
   const uint32_t blocks = args.env_list ? std::min<uint32_t>(full, 148u * 4u) : full;
   const size_t smem = size_t(env_bytes) * envs_per_block;
   cudaError_t err = cudaSuccess;
+  // the stage-profiling instantiation runs when args.stage_clk is set (never in list mode)
+  const bool prof = args.stage_clk != nullptr && args.env_list == nullptr;
   switch (lanes) {
-#define ZB_LAUNCH(LN)                                                                               \
-  case LN:                                                                                          \
-    err = cudaFuncSetAttribute(step_kernel<LN>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)); \
-    if (err != cudaSuccess) return err;                                                             \
-    step_kernel<LN><<<blocks, threads, smem, stream>>>(args);                                       \
+#define ZB_LAUNCH(LN)                                                                                         \
+  case LN:                                                                                                    \
+    if (prof) {                                                                                               \
+      err = cudaFuncSetAttribute(step_kernel<LN, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)); \
+      if (err != cudaSuccess) return err;                                                                     \
+      step_kernel<LN, true><<<blocks, threads, smem, stream>>>(args);                                         \
+    } else {                                                                                                  \
+      err = cudaFuncSetAttribute(step_kernel<LN, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)); \
+      if (err != cudaSuccess) return err;                                                                     \
+      step_kernel<LN, false><<<blocks, threads, smem, stream>>>(args);                                        \
+    }                                                                                                         \
     break;
     ZB_LAUNCH(4)
     ZB_LAUNCH(8)

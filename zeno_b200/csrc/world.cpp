@@ -162,6 +162,8 @@ World* World::create(const Scene& sc, const WorldConfig& cfg, std::string* err) 
   upload(&w->d_sensors_, m.sensors);
   upload(&w->d_cons_, m.constraints);
   upload(&w->d_colors_, m.kcolor_ranges);
+  upload(&w->d_jgroups_, m.jgroup_words);
+  upload(&w->d_jgroup_levels_, m.jgroup_levels);
   upload(&w->d_subtree_, m.subtree);
   upload(&w->d_init_, m.init_state);
   upload(&w->d_bound_, m.geom_bound);
@@ -292,6 +294,9 @@ StepArgs World::args(uint32_t substeps, const float* actions, const uint8_t* mas
   a.bodies = d_bodies_, a.jf_list = d_jf_, a.joints = d_joints_, a.geoms = d_geoms_, a.pairs = d_pairs_;
   a.pair_bodies = d_pair_bodies_, a.pair_la = d_pair_la_, a.pair_lb = d_pair_lb_;
   a.actuators = d_act_, a.sensors = d_sensors_, a.constraints = d_cons_, a.color_ranges = d_colors_;
+  a.jgroups = reinterpret_cast<const uint2*>(d_jgroups_);
+  a.jgroup_levels = d_jgroup_levels_;
+  a.num_jlevels = m.jgroup_levels.empty() ? 0u : uint32_t(m.jgroup_levels.size() - 1);
   a.subtree = d_subtree_, a.init_state = d_init_;
   a.pos = pos, a.quat = quat, a.vel = vel, a.angvel = angvel, a.acc = acc;
   a.jpos = jpos, a.jvel = jvel, a.jtorque = jtorque, a.obs = obs, a.rewards = rewards, a.dones = dones;
@@ -327,7 +332,15 @@ cudaError_t World::launch(uint32_t substeps, const float* actions, const uint8_t
   out_stream_ = stream_;
   if (!use_fast_) {
     cache_dirty_ = true;  // the general kernel does not maintain the slot cache
-    return launch_step(a, lanes_, envs_per_block_, stream_);
+    if (!d_stage_) return launch_step(a, lanes_, envs_per_block_, stream_);
+    // profiling world: the general kernel's stage-profiling instantiation
+    a.stage_clk = d_stage_;
+    cudaError_t e = cudaMemsetAsync(d_stage_, 0, kStageSlots * sizeof(unsigned long long), stream_);
+    if (e == cudaSuccess) e = launch_step(a, lanes_, envs_per_block_, stream_);
+    if (e == cudaSuccess)
+      e = cudaMemcpyAsync(h_stage_, d_stage_, kStageSlots * sizeof(unsigned long long), cudaMemcpyDeviceToHost,
+                          stream_);
+    return e;
   }
   if (d_cache_w_ && !contacts_exposed_) {  // the slot cache (see World::expose_contacts)
     if (cache_dirty_) {
@@ -395,10 +408,10 @@ cudaError_t World::step(const float* actions, uint32_t substeps, bool async) {
     for (uint32_t v : c) total += v;
     prof_.num_contacts = uint32_t(total > 0xFFFFFFFFull ? 0xFFFFFFFFull : total);
     prof_.num_active_constraints = model_.K * cfg_.num_envs;
-    // stage times (environment-per-lane kernel): the blocks run side by side, so a stage's
-    // time is its average over the blocks, in cycles converted with the measured ns/cycle
+    // stage times (either kernel): the blocks run side by side, so a stage's time is its
+    // average over the blocks, in cycles converted with the measured ns/cycle
     double st[kStageCount + 2];
-    stage_valid_ = use_fast_ && d_stage_ != nullptr;
+    stage_valid_ = d_stage_ != nullptr;
     if (stage_valid_ && stage_cycles(st, kStageCount + 2) == kStageCount + 2) {
       const double ns = st[kStageCount + 1];
       prof_.integrate_ns = float((st[kStActions] + st[kStIntegrate] + st[kStVelocities]) * ns);

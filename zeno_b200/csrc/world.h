@@ -184,6 +184,8 @@ class World {
   DSensor* d_sensors_ = nullptr;
   DConstraint* d_cons_ = nullptr;
   uint32_t* d_colors_ = nullptr;
+  uint32_t* d_jgroups_ = nullptr;       // hinge groups by level (HostModel::jgroup_words)
+  uint32_t* d_jgroup_levels_ = nullptr;
   uint32_t* d_subtree_ = nullptr;
   float* d_init_ = nullptr;
   float* d_bound_ = nullptr;

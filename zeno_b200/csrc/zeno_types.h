@@ -129,6 +129,11 @@ struct StepArgs {
   const DSensor* sensors;
   const DConstraint* constraints;
   const uint32_t* color_ranges;  // 2*num_colors (start, count)
+  // hinge groups by dependency level (general kernel; num_jlevels 0: solve by colour):
+  // per group (k0 | k1 << 16, k2 | kind << 16), jgroup_levels[lv]..[lv + 1] per level
+  const uint2* jgroups;
+  const uint32_t* jgroup_levels;
+  uint32_t num_jlevels;
   const uint32_t* subtree;       // per-body subtree size (task reset noise)
   const float* init_state;       // template: B*4 pos, B*4 quat, B*4 vel, B*4 angvel, J jpos, J jvel
   // state (device-accessible)
