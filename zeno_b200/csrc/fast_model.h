@@ -82,7 +82,7 @@ struct FModel {
   // together with the two bodies' poses kept in registers, or a single constraint.
   // k0 | k1 << 8 | k2 << 16 | kind << 24; kind 0: constraint k0 alone, 1: point k0 then
   // axis k1, 2: point k0, axis k1, limit k2.  The groups are a dependency-respecting order
-  // of the sweep (pack_fast_model).
+  // of the sweep (hinge_groups in model.cpp).
   uint32_t o_groups;
   uint32_t num_groups;
 };
