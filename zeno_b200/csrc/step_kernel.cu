@@ -158,7 +158,7 @@ struct ArrBodies {
 // Narrow phase for one slot (narrow_phase, all_shaders.metal:751-894; mode 1: the
 // reference's CPU detectCollision, src/collision/narrow_phase.zig:28-136; mode 2: as 1,
 // with GJK + EPA, src/collision/gjk.zig, for box-capsule pairs)
-__device__ __forceinline__ bool narrow(Pk pk, const DGeom* geoms, const float4* pos, const float4* quat,
+__device__ __forceinline__ void narrow(Pk pk, const DGeom* geoms, const float4* pos, const float4* quat,
                                        uint32_t mode, uint32_t corrected, float restitution, float4& cpp, float4& cnf,
                                        float4& cim) {
   const DGeom& gA = geoms[pk_ga(pk)];
@@ -199,7 +199,6 @@ __device__ __forceinline__ bool narrow(Pk pk, const DGeom* geoms, const float4* 
   } else {
     cpp.w = -1.0f;
   }
-  return hit;
 }
 
 // ------------------------------------------------------------------------------------
@@ -696,54 +695,9 @@ __device__ __forceinline__ void step_env(const StepArgs& a, uint32_t e, unsigned
     }
     clk.mark(kStSort);
     // ---- narrow phase ----
-    // A slot's result depends only on its pair and the poses, and a list the reference's
-    // ever-growing counter filled holds the same pair several times (appended in several
-    // substeps), so each pair is computed once, by the first slot holding it (a "holder";
-    // slots in key order keep copies of a pair in one run), and its copies take the
-    // holder's result: the three parts on a hit, the miss marker otherwise.  Scratch
-    // (free between the sort and the contact schedule): slev[i] = position of slot i's
-    // holder, for a holder itself i on a hit and 0xFFFF on a miss; lcur = the holders'
-    // positions, spread over the lanes.
-    {
-      const uint32_t lm = L == 32 ? 0xFFFFFFFFu : ((1u << L) - 1u);
-      uint32_t nlead = 0;
-      for (uint32_t c0 = 0; c0 < n; c0 += L) {
-        const uint32_t i = c0 + l;
-        uint32_t first = i;
-        if (i < n) {
-          const Pk pk = cpk[ord[i]];
-          const uint32_t key = pk_key(pk);
-          for (uint32_t j = i; j > 0 && pk_key(cpk[ord[j - 1]]) == key;) {
-            --j;
-            const Pk q = cpk[ord[j]];
-            if (q.x == pk.x && q.y == pk.y) first = j;
-          }
-          slev[i] = uint16_t(first);
-        }
-        const bool lead = i < n && first == i;
-        const uint32_t bal = (__ballot_sync(gmask, lead) >> gshift) & lm;
-        if (lead) lcur[nlead + __popc(bal & ((1u << l) - 1u))] = uint16_t(i);
-        nlead += __popc(bal);
-      }
-      __syncwarp(gmask);
-      for (uint32_t k = l; k < nlead; k += L) {
-        const uint32_t i = lcur[k], st = ord[i];
-        if (!narrow(cpk[st], a.geoms, pos, quat, a.narrow_mode, a.corrected, a.restitution, cpp[st], cnf[st], cim[st]))
-          slev[i] = 0xFFFFu;
-      }
-      __syncwarp(gmask);
-      for (uint32_t i = l; i < n; i += L) {
-        const uint32_t f = slev[i];
-        if (f == i || f == 0xFFFFu) continue;  // a holder
-        const uint32_t st = ord[i], sf = ord[f];
-        if (slev[f] == f) {
-          cpp[st] = cpp[sf];
-          cnf[st] = cnf[sf];
-          cim[st] = cim[sf];
-        } else {
-          cpp[st].w = -1.0f;
-        }
-      }
+    for (uint32_t i = l; i < n; i += L) {
+      const uint32_t st = ord[i];
+      narrow(cpk[st], a.geoms, pos, quat, a.narrow_mode, a.corrected, a.restitution, cpp[st], cnf[st], cim[st]);
     }
     __syncwarp(gmask);
     // ---- warm start: best previous contact of the same pair within 0.2 ----
