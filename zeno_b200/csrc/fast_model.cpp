@@ -246,6 +246,22 @@ bool pack_fast_model(const HostModel& h, uint32_t max_contacts, uint32_t narrow_
     m.num_groups = uint32_t(groups.size());
     m.o_groups = section(4 * m.num_groups), put(m.o_groups, groups.data(), 4 * groups.size());
   }
+  {
+    std::vector<uint32_t> words;
+    bool fits = !h.jgroup_levels.empty();
+    for (size_t g = 0; fits && 2 * g + 1 < h.jgroup_words.size(); ++g) {
+      const uint32_t w0 = h.jgroup_words[2 * g], w1 = h.jgroup_words[2 * g + 1];
+      const uint32_t k0 = w0 & 0xFFFFu, k1 = w0 >> 16, k2 = w1 & 0xFFFFu, kind = w1 >> 16;
+      if (k0 >= fm::kNoGroup || k1 >= fm::kNoGroup || k2 >= fm::kNoGroup) fits = false;
+      words.push_back(k0 | ((kind >= 1 ? k1 : fm::kNoGroup) << 8) | ((kind == 2 ? k2 : fm::kNoGroup) << 16) |
+                      (kind << 24));
+    }
+    m.num_glv = fits ? uint32_t(h.jgroup_levels.size() - 1) : 0u;
+    if (m.num_glv) {
+      m.o_glv = section(4 * (m.num_glv + 1)), put(m.o_glv, h.jgroup_levels.data(), 4 * (m.num_glv + 1));
+      m.o_gwords = section(4 * words.size()), put(m.o_gwords, words.data(), 4 * words.size());
+    }
+  }
   section(0);
   m.hot_bytes = uint32_t(img.size());
   m.hot = nullptr;

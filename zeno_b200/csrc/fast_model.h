@@ -85,6 +85,12 @@ struct FModel {
   // of the sweep (hinge_groups in model.cpp).
   uint32_t o_groups;
   uint32_t num_groups;
+  // The same groups by dependency level, for two lanes per environment (HostModel::
+  // jgroup_levels): a level's groups touch disjoint dynamic bodies and are split across
+  // the lanes.  u32[num_glv + 1] level starts, then the group words (packed as above) level
+  // by level; num_glv 0 when a constraint index does not fit the packing (colour runs then).
+  uint32_t o_glv, o_gwords;
+  uint32_t num_glv;
 };
 
 // Fills *out and the hot image *hot (to be uploaded and linked through out->hot); false

@@ -689,10 +689,11 @@ __device__ __forceinline__ void run_env(const StepArgs& a, const FModel& f, cons
         if (v0 + u * L < nh) imp[i4[u] * ne] = w4[u];
     }
     clk.mark(kStSchedule);
-    // ---- XPBD joints (solve_joints 909-1399): with two lanes colour by colour, as runs of
-    //      one type, a run's constraints (one colour: disjoint bodies) split across the
-    //      lanes; with one lane as the model's hinge groups.
-    if constexpr (L == 1) {  // one lane: the sweep as hinge groups (pack_fast_model)
+    // ---- XPBD joints (solve_joints 909-1399): with one lane as the model's hinge groups;
+    //      with two as the groups by dependency level, or (models whose constraint indices
+    //      do not fit the group words) colour by colour, as runs of one type, a run's
+    //      constraints (one colour: disjoint bodies) split across the lanes.
+    if constexpr (L == 1) {  // one lane: the sweep as hinge groups (hinge_groups, model.cpp)
       for (uint32_t it = 0; it < a.iterations; ++it)
         for (uint32_t g = 0; g < f.num_groups; ++g) {
           const uint32_t gw = m.group(g);
@@ -712,6 +713,31 @@ __device__ __forceinline__ void run_env(const StepArgs& a, const FModel& f, cons
             case 10: solve_typed<10>(m, c, S); break;
             default: break;
           }
+        }
+    } else if (f.num_glv > 0) {  // several lanes: hinge groups level by level, split across the lanes
+      for (uint32_t it = 0; it < a.iterations; ++it)
+        for (uint32_t v = 0; v < f.num_glv; ++v) {
+          const uint32_t g1 = m.glv(v + 1);
+          for (uint32_t g = m.glv(v) + lane; g < g1; g += L) {
+            const uint32_t gw = m.gword(g);
+            const uint32_t k0 = gw & 0xFFu, kind = gw >> 24;
+            if (kind != 0u) {
+              const uint32_t k2 = kind == 2u ? (gw >> 16) & 0xFFu : k0;
+              solve_hinge(m, m.constraint(k0), m.constraint((gw >> 8) & 0xFFu), m.constraint(k2), kind == 2u, S);
+              continue;
+            }
+            const ConstraintV c = m.constraint(k0);
+            switch (c.type) {
+              case 2: solve_typed<2>(m, c, S); break;
+              case 3: solve_typed<3>(m, c, S); break;
+              case 4: solve_typed<4>(m, c, S); break;
+              case 5: solve_typed<5>(m, c, S); break;
+              case 7: solve_typed<7>(m, c, S); break;
+              case 10: solve_typed<10>(m, c, S); break;
+              default: break;
+            }
+          }
+          G.sync();
         }
     } else
     for (uint32_t it = 0; it < a.iterations; ++it)

@@ -47,6 +47,8 @@ struct ModelS {
   __device__ __forceinline__ float4 gforce(uint32_t b) const { return at<float4>(f.o_gforce, b); }
   __device__ __forceinline__ uint32_t run(uint32_t r) const { return at<uint32_t>(f.o_runs, r); }
   __device__ __forceinline__ uint32_t group(uint32_t g) const { return at<uint32_t>(f.o_groups, g); }
+  __device__ __forceinline__ uint32_t glv(uint32_t v) const { return at<uint32_t>(f.o_glv, v); }
+  __device__ __forceinline__ uint32_t gword(uint32_t g) const { return at<uint32_t>(f.o_gwords, g); }
 };
 
 struct ModelG {
