@@ -436,6 +436,27 @@ def test_gjk_box_capsule_scene(lanes):
     assert gjk_hits > 0
 
 
+def test_general_blocking_follows_the_narrow_phase():
+    """The general kernel takes 16 environments per block when GJK + EPA can run (narrow
+    phase 2 with box-capsule candidates) and 4 otherwise; a shape set by the caller is
+    kept; results are the oracle's either way."""
+    E = 40
+    w, o, c = make_pair("humanoid", E)
+    acts = actions(np.random.default_rng(21), 6, E, w.action_dim, c["act"])
+    for mode, shape in ((2, (8, 16)), (1, (8, 4)), (2, (8, 16))):
+        w.set_narrow_phase(mode)
+        assert o.set_narrow_phase(mode) == 0
+        assert w.get_launch() == shape
+        for s in range(2):
+            w.step(acts[s])
+            o.step(acts[s])
+        assert not diff_report(product_state(w), o.state())
+    w.set_launch(8, 2)
+    w.set_narrow_phase(1)
+    w.set_narrow_phase(2)
+    assert w.get_launch() == (8, 2)
+
+
 def test_extended_narrow_phase_drop_scene_gjk():
     """The 64-body drop scene with narrow phase 2 (box-capsule through GJK + EPA)."""
     xml = scenes.collision_stress(0)

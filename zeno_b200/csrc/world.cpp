@@ -106,6 +106,7 @@ World* World::create(const Scene& sc, const WorldConfig& cfg, std::string* err) 
   // environment-per-lane kernel when the model packs into its fixed-capacity tables
   std::string why;
   if (m.corrected) w->narrow_mode_ = 2;  // corrected semantics use the CPU routines + GJK
+  w->choose_general_blocking();
   w->fast_ok_ = pack_fast_model(m, M, w->narrow_mode_, &w->fmodel_, &w->hot_image_, &why);
 
   if (cudaStreamCreateWithFlags(&w->own_stream_, cudaStreamNonBlocking) != cudaSuccess) return fail("stream", w);
@@ -574,6 +575,24 @@ int World::set_launch(int lanes, int envs_per_block) {
   return 0;
 }
 
+// With GJK + EPA on box-capsule pairs, each lane running EPA keeps a polytope of about
+// 7 KB in local memory, and with 4 environments per block six blocks share an SM, so most
+// of those loads miss L1.  Blocks of 16 environments (larger blocks, fewer per SM) measured
+// faster there (Humanoid narrow phase 2: 7.60 -> 6.59 ms per step; corrected semantics
+// 12.3 -> 11.2) and slower without EPA (narrow phase 1: 1.65 -> 1.84; Ant corrected
+// semantics 1.44 -> 1.68), so the larger block is used only when EPA can run.
+void World::choose_general_blocking() {
+  if (prefer_general_ || lanes_ != 8) return;
+  bool epa = false;
+  if (narrow_mode_ == 2)
+    for (const DPair& p : model_.pairs) {
+      const uint32_t ta = model_.geoms[p.ga].type, tb = model_.geoms[p.gb].type;
+      epa = epa || (ta == 1 && tb == 2) || (ta == 2 && tb == 1);
+    }
+  const uint32_t fit = uint32_t(opt_in_smem(device_)) / std::max(general_env_bytes(8), 1u);
+  envs_per_block_ = int(std::max(1u, std::min(epa ? 16u : 4u, fit)));
+}
+
 uint32_t World::general_env_bytes(int lanes) const {
   const bool g = grid_on();
   return env_smem_bytes(model_.B, model_.J, cfg_.max_contacts_per_env, g ? model_.G : 0u,
@@ -605,6 +624,7 @@ int World::set_narrow_phase(uint32_t mode) {
   if (mode == narrow_mode_) return 0;
   if (cudaStreamSynchronize(stream_) != cudaSuccess) return -4;
   narrow_mode_ = mode;
+  choose_general_blocking();
   cache_dirty_ = true;  // hittable indices in the cached slot words depend on the narrow phase
   std::string why;
   std::vector<uint8_t> img;

@@ -125,6 +125,9 @@ class World {
   World() = default;
   StepArgs args(uint32_t substeps, const float* actions, const uint8_t* mask) const;
   void choose_fast_shape();
+  // General kernel with 8 lanes: environments per block for the current narrow phase
+  // (more when GJK + EPA runs, see world.cpp).  A caller's set_launch shape is kept.
+  void choose_general_blocking();
   cudaError_t launch(uint32_t substeps, const float* actions, const uint8_t* mask);
   template <class T>
   cudaError_t managed(T** p, size_t n);
